@@ -1,0 +1,444 @@
+#!/usr/bin/env python3
+"""Benchmark of the static-lm hot path on B200: batched greedy decode at the
+SmolLM2-135M shape: 64 independent sequences, KV cache
+pre-filled to 2048 positions from seeded N(0,1), sharded by sequence over N
+GPUs (one process per GPU, no data-path collective, total batch fixed =>
+strong scaling).  One step = one decode step of every sequence: 30 layers of
+RMSNorm+Q8, Wq/Wk/Wv+RoPE+KV append, GQA attention, Wo, SwiGLU FFN, then
+final norm, lm_head and argmax.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the CPU restatement of the reference's own path
+(oracle/, the reference itself is Rust and cannot be built here) on the
+host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "static-lm_b200"))
+
+import numpy as np  # noqa: E402
+
+GLOBAL_BATCH = 64
+CTX = 2048
+DECODE_ROOM = 128  # max_seq_len = 2048 + 128: the steps after the prefilled context
+METRIC = "decode tok/s (SmolLM2-135M shape, batch 64, 2048-token context)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seed", type=int, default=2024)
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="target CPU work of the cpu_baseline / reference sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return ws, rank, local
+
+
+def workload(n_gpus):
+    return {
+        "workload": "cfg3: SmolLM2-135M-shaped synthetic Q4_0 model (dim 576, hidden 1536, "
+                    "30 layers, 9/3 heads, vocab 49152), batched greedy decode of 64 independent "
+                    "sequences, KV cache pre-filled to 2048 positions from seeded N(0,1)",
+        "global_batch": GLOBAL_BATCH,
+        "seq_len": CTX,
+        "max_seq_len": CTX + DECODE_ROOM,
+        "parallelism": f"dp{n_gpus} (sequences sharded over GPUs, no collective)",
+        "weights": "seeded N(0,0.02) quantized to Q4_0, RMSNorm scales 1.0",
+        "l2": "inputs larger than L2: each step streams the 6.0 GB KV cache (L2 is 126 MB)",
+    }
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, power, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------- model setup
+
+def build_weights(seed):
+    from static_lm import synth
+    cfg, layers, vocab = synth.config("cfg3", max_seq_len=CTX + DECODE_ROOM)
+    w = synth.synth_model(cfg, layers, vocab, seed=seed)
+    return cfg, layers, vocab, w
+
+
+def kv_seed(seed, gseq, layer, which):
+    return (seed * 1000003 + gseq * 131 + layer * 2 + which) & 0x7FFFFFFFFFFFFFFF
+
+
+def prefill_kv(torch, model, seqs_global, layers, kvd, seed):
+    """KV rows 0..2047 of every layer from seeded N(0,1) (device generator)."""
+    g = torch.Generator(device="cuda")
+    buf = torch.empty(CTX * kvd, dtype=torch.float32, device="cuda")
+    for local, gs in enumerate(seqs_global):
+        for l in range(layers):
+            for which in (0, 1):
+                g.manual_seed(kv_seed(seed, gs, l, which))
+                torch.randn(CTX * kvd, generator=g, out=buf, device="cuda")
+                torch.cuda.synchronize()
+                model.kv_write_device(local, l, which, 0, CTX, buf.data_ptr())
+                torch.cuda.synchronize()
+                torch.cuda.ExternalStream(model.stream).synchronize()
+
+
+def first_tokens(seqs_global, vocab):
+    return [int((gs * 7919 + 17) % vocab) for gs in seqs_global]
+
+
+# ---------------------------------------------------------------- CPU leg
+
+def cpu_decode_sample(cfg, w, kv_of, toks, n_steps_max, budget_s, threads):
+    """The oracle (restated reference path, AVX2 dot + JIT-op numerics, the
+    reference's row-parallel pool) decoding sample sequences one after
+    another, each with its own KV cache, as separate TransformerModels would.
+    Returns (tokens produced, seconds, tokens per sequence)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    done, secs, outs = 0, 0.0, []
+    for i, (k_list, v_list) in enumerate(kv_of):
+        m = O.Model(cfg, w, O.MODE_X86, threads)
+        kvd = m.kv_dim
+        for l in range(len(k_list)):
+            m.k_cache(l)[:CTX * kvd] = k_list[l]
+            m.v_cache(l)[:CTX * kvd] = v_list[l]
+        tok, seq_out = toks[i], []
+        for s in range(n_steps_max):
+            t0 = time.perf_counter()
+            tok = m.forward_token(tok, CTX + s)
+            secs += time.perf_counter() - t0
+            done += 1
+            seq_out.append(tok)
+            if secs > budget_s:
+                break
+        outs.append(seq_out)
+        m.close()
+        if secs > budget_s:
+            break
+    return done, secs, outs
+
+
+def gather_kv(model, local, layers, kvd):
+    k = [model.kv_read(local, l, 0, 0, CTX) for l in range(layers)]
+    v = [model.kv_read(local, l, 1, 0, CTX) for l in range(layers)]
+    return k, v
+
+
+# ---------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from static_lm import synth
+    cfg, layers, vocab, w = build_weights(args.seed)
+    kvd = cfg.dim // cfg.num_heads * cfg.num_kv_heads
+    threads = O.lib.orc_default_pool_threads()
+    per_step_budget = max(1.0, args.cpu_seconds / max(1, args.steps))
+    # one reference "step": a bounded sample of the 64-sequence decode step
+    # (one sequence's token per sample unit), scaled to tok/s
+    m = O.Model(cfg, w, O.MODE_X86, threads)
+    for l in range(layers):
+        m.k_cache(l)[:CTX * kvd] = synth.normal_f32(CTX * kvd, kv_seed(args.seed, 0, l, 0))
+        m.v_cache(l)[:CTX * kvd] = synth.normal_f32(CTX * kvd, kv_seed(args.seed, 0, l, 1))
+    tok = first_tokens([0], vocab)[0]
+    pos = CTX
+    for _ in range(max(1, min(args.warmup, 1))):
+        tok = m.forward_token(tok, pos)
+        pos += 1
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            tok = m.forward_token(tok, pos)
+            pos += 1
+            n += 1
+            if time.perf_counter() - t0 >= per_step_budget or pos >= CTX + DECODE_ROOM:
+                break
+        times.append((time.perf_counter() - t0) / n)
+        if pos >= CTX + DECODE_ROOM:
+            break
+    sec_per_tok = statistics.mean(times)
+    value = 1.0 / sec_per_tok
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": sec_per_tok * 1000.0 * GLOBAL_BATCH, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"one sequence decoding at context {CTX}+, "
+                                   f"{sum(1 for _ in times)} samples of ~{per_step_budget:.1f}s; "
+                                   "ms_per_step scales one token to the 64-sequence step"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Rust (cargo absent); its CPU path is timed through the "
+                "C restatement in oracle/ with the reference's thread policy "
+                "(logical_cpus/2 GEMV workers, single-threaded attention)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import torch
+    ws, rank, local = dist_env()
+    n = args.gpus
+    if ws != n:
+        n = ws
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    import static_lm as S
+
+    if GLOBAL_BATCH % ws:
+        raise SystemExit("global batch must divide by the number of GPUs")
+    B = GLOBAL_BATCH // ws
+    seqs_global = list(range(rank * B, (rank + 1) * B))
+    t_build = time.time()
+    cfg, layers, vocab, w = build_weights(args.seed)
+    model = S.Model(cfg, w, max_sequences=B, max_rows=B, device=local)
+    kvd = model.kv_dim
+    prefill_kv(torch, model, seqs_global, layers, kvd, args.seed)
+    stream = torch.cuda.ExternalStream(model.stream)
+    setup_s = time.time() - t_build
+
+    def device_state():
+        seqs = torch.arange(B, dtype=torch.int32, device="cuda")
+        toks = torch.tensor(first_tokens(seqs_global, vocab), dtype=torch.int32, device="cuda")
+        pos = torch.full((B,), CTX, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        return seqs, toks, pos
+
+    W, K = args.warmup, args.steps
+    if W + K > DECODE_ROOM:
+        raise SystemExit(f"--warmup + --steps must be <= {DECODE_ROOM}")
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timed region (graph replay, inputs in HBM)
+    seqs, toks, pos = device_state()
+    out = torch.zeros((W + K) * B, dtype=torch.int32, device="cuda")
+    model.decode_steps_device(B, seqs.data_ptr(), toks.data_ptr(), pos.data_ptr(), W,
+                              out.data_ptr(), CTX)
+    stream.synchronize()
+    props = torch.cuda.get_device_properties(local)
+    uuid = str(getattr(props, "uuid", "") or "")
+    clocks = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else
+                          (uuid or str(local)))
+    barrier()
+    clocks.start()
+    time.sleep(0.4)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    model.decode_steps_device(B, seqs.data_ptr(), toks.data_ptr(), pos.data_ptr(), K,
+                              out.data_ptr() + W * B * 4, CTX + W)
+    ev1.record(stream)
+    stream.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_per_step = ms / K
+    value = GLOBAL_BATCH * K / (ms / 1000.0)
+    tokens_dev = out.view(W + K, B).cpu().numpy()
+
+    # ---- phase profile (same steps, eager launches with events on the model stream)
+    seqs, toks, pos = device_state()
+    prof_steps = min(8, K)
+    phases = model.profile_decode(B, seqs.data_ptr(), toks.data_ptr(), pos.data_ptr(),
+                                  prof_steps, CTX)
+    per_step = {k: v / prof_steps for k, v in phases.items()}
+
+    # ---- end-to-end through the public API with host buffers
+    seqs_h = np.arange(B, dtype=np.uint32)
+    toks_h = np.array(first_tokens(seqs_global, vocab), dtype=np.int32)
+    pos_h = np.full(B, CTX, dtype=np.uint32)
+    for _ in range(2):  # warm the graphs for the host path
+        toks_h = model.decode_batch(seqs_h, toks_h, pos_h)
+        pos_h = pos_h + 1
+    barrier()
+    t0 = time.perf_counter()
+    e2e_steps = min(K, DECODE_ROOM - 2)
+    for _ in range(e2e_steps):
+        toks_h = model.decode_batch(seqs_h, toks_h, pos_h)
+        pos_h = pos_h + 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_value = GLOBAL_BATCH * e2e_steps / e2e_s
+
+    # ---- roofline of the dominant kernel(s) (algorithmic bytes / event time)
+    Lp = CTX + (prof_steps + 1) / 2.0
+    kv_bytes_layer = B * 2 * Lp * kvd * 4          # K and V rows read once
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm_peak = peaks.get("hbm_gbs")
+    peak_note = "of measured" if hbm_peak else "of fallback"
+    hbm_peak = hbm_peak or 6650.0
+    attn_ms = per_step["attn_scores"] + per_step["attn_softmax"] + per_step["attn_pv"]
+    attn_launch_ms = attn_ms / layers
+    achieved = kv_bytes_layer / (attn_launch_ms / 1000.0) / 1e9
+    dominant = max(per_step, key=per_step.get)
+    traffic = None
+    try:
+        tj = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        traffic = tj.get("attention_bytes_per_layer_launch")
+    except Exception:
+        pass
+    # attention + GEMV kernels together: all HBM bytes of a step over their time
+    w_bytes = w.q4_bytes()
+    gemv_keys = ["qkv_gemv_rope", "wo_gemv_residual", "gate_up_gemv_swiglu", "down_gemv_residual",
+                 "lm_head_gemv"]
+    gemv_ms = sum(per_step[k] for k in gemv_keys)
+    step_bytes = layers * kv_bytes_layer + w_bytes
+    combined = step_bytes / ((attn_ms + gemv_ms) / 1000.0) / 1e9
+
+    # ---- CPU baseline on a bounded sample (rank 0 at N=1 only)
+    cpu = None
+    parity = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        threads = O.lib.orc_default_pool_threads()
+        sample_seqs = [0, 1]
+        kv_of = [gather_kv(model, s, layers, kvd) for s in sample_seqs]
+        toks0 = first_tokens([seqs_global[s] for s in sample_seqs], vocab)
+        done, secs, outs = cpu_decode_sample(cfg, w, kv_of, toks0, min(W + K, 6),
+                                             args.cpu_seconds, threads)
+        cpu = {"value": done / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{done} decode tokens of {len(outs)} sequence(s) at context {CTX}+ "
+                         f"({secs:.1f} s), sequences one after another with the reference's "
+                         "thread policy"}
+        # free parity check: the GPU's first tokens of the sampled sequences
+        parity = all(list(tokens_dev[:len(o), s]) == o for s, o in zip(sample_seqs, outs))
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
+        "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload(ws),
+        "roofline": {"bound": "hbm", "kernel": "attention (scores+softmax+pv, one layer)",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_source": peak_note,
+                     "traffic": traffic,
+                     "algorithmic_bytes_per_launch": kv_bytes_layer},
+        "attention_gemv_hbm": {"achieved_gbs": combined, "frac": combined / hbm_peak,
+                               "bytes_per_step": step_bytes,
+                               "kernel_ms_per_step": attn_ms + gemv_ms},
+        "phases_ms_per_step": {k: round(v, 4) for k, v in per_step.items()},
+        "dominant_phase": dominant,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * GLOBAL_BATCH,
+                "d2h_bytes_per_step": 4 * GLOBAL_BATCH,
+                "api": "slm_model_decode_batch (host token/position arrays in, next tokens out)"},
+        "gpu_launches": model.launches_per_decode_step * K,
+        "clocks": clk,
+        "setup_s": round(setup_s, 1),
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+        line["cpu_parity_tokens_equal"] = parity
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

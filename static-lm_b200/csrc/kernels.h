@@ -1,0 +1,114 @@
+// kernels.h -- launchers of the sm_100a kernels (internal to libslm_b200).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace slm {
+
+// ---- vector ops / quantization (kernels_vec.cu)
+// RMSNorm of `rows` rows (graph.rs:141-155) fused with Q8_0 quantization of the
+// result into Q8X (n must be a multiple of 32 when q8 is requested).
+// y (optional) receives the f32 normalized rows.
+void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float eps,
+                       float *y, size_t ldy, Q8X q8, int rows, cudaStream_t s);
+// Q8_0 quantization of f32 rows into Q8X (blocks.rs:102-123).
+void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s);
+// Q8_0 quantization into the reference's 34-byte BlockQ8_0 layout.
+void launch_quantize_q8_ref(const float *x, void *blocks, size_t n, cudaStream_t s);
+// Reference BlockQ8_0 blocks -> Q8X (for callers that hand in pre-quantized input).
+void launch_q8_ref_to_q8x(const void *blocks, Q8X q8, size_t nblocks, cudaStream_t s);
+// x[r] = dequantize(token_embd row tokens[r]) (transformer.rs:768-770).
+void launch_embed(const uint8_t *tiles, int nb, const int32_t *tokens, int vocab, float *x,
+                  size_t ldx, int rows, int32_t *err, cudaStream_t s);
+// out[r] = argmax(logits[r]) with the first maximum winning (transformer.rs:656-667).
+void launch_argmax(const float *logits, size_t ld, int n, int32_t *out, int rows,
+                   cudaStream_t s);
+// Standalone JIT-op equivalents on one vector of `len` elements.
+void launch_softmax_vec(const float *x, float *out, size_t len, cudaStream_t s);
+void launch_rmsnorm_vec(const float *x, const float *w, float *out, size_t len, float eps,
+                        cudaStream_t s);
+void launch_swiglu_vec(const float *g, const float *u, float *out, size_t len, cudaStream_t s);
+void launch_residual_add_vec(const float *a, const float *b, float *out, size_t len,
+                             cudaStream_t s);
+void launch_l2norm_vec(const float *x, float *out, size_t len, float eps, cudaStream_t s);
+// accum[i] = sum over rows b (in order) of y[b][i] * inv_batch, starting from
+// 0 (the embedding mean pool, transformer.rs:928-940).
+void launch_mean_pool(const float *y, size_t ldy, int rows, int n, float inv_batch,
+                      float *accum, cudaStream_t s);
+// Greedy feedback between decode steps: tokens = next, pos += 1.
+void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows,
+                    cudaStream_t s);
+void launch_rope_vec(float *vec, size_t len, const float *cos_row, const float *sin_row,
+                     int head_dim, cudaStream_t s);
+
+// ---- Q4_0 x Q8_0 GEMV / GEMM (kernels_gemv.cu)
+enum Epilogue : int {
+    EPI_STORE = 0,      // out[b*ld_out + r] = y
+    EPI_RESIDUAL = 1,   // out[b*ld_out + r] = res[b*ld_res + r] + y
+    EPI_QKV = 2,        // RoPE(q), RoPE(k) -> K cache, v -> V cache
+    EPI_SWIGLU_Q8 = 3,  // rows [0,h) gate, [h,2h) up -> silu(g)*u -> Q8X (+ f32 copy)
+};
+
+// K and V of activation row b live at
+//   k_base + slot[b]*slot_stride + layer_off + pos[b]*kv_dim   (same for v_base)
+// i.e. the reference's position-major LayerKvCache (transformer.rs:323-338)
+// repeated per sequence slot and layer.
+struct QkvArgs {
+    float *q;                // [rows_b][dim]
+    size_t ldq;
+    float *k_base, *v_base;
+    const int32_t *slot;     // [rows_b] sequence slot of each activation row
+    const int32_t *pos;      // [rows_b] position of each activation row
+    size_t slot_stride;      // floats between consecutive slots
+    size_t layer_off;        // floats from a slot's start to this layer's block
+    int dim, kv_dim, head_dim, max_seq;
+    const float *rope_cos, *rope_sin;  // [max_seq][head_dim/2]
+    int32_t *err;            // set to 2 when a position is out of range
+};
+
+struct GemvArgs {
+    const uint8_t *w;        // repacked tiles
+    int rows;                // logical rows (for SWIGLU: 2*h, gate then up)
+    int nb;                  // blocks per row (cols/32)
+    Q8X x;                   // activations, batch rows of nb blocks
+    int batch;
+    int epi;
+    float *out;              // EPI_STORE / EPI_RESIDUAL / SWIGLU f32 copy (may be null)
+    size_t ld_out;
+    const float *res;        // EPI_RESIDUAL
+    size_t ld_res;
+    Q8X q8_out;              // EPI_SWIGLU_Q8 destination (nb_out = h/32 blocks per row)
+    QkvArgs qkv;
+};
+void launch_gemv(const GemvArgs &a, cudaStream_t s);
+
+// ---- attention (kernels_attn.cu)
+struct AttnArgs {
+    const float *q;          // [rows][dim] (RoPE applied)
+    size_t ldq;
+    const float *k_base, *v_base;
+    const int32_t *slot, *pos;  // per-row slot/position; null = slot 0 / pos_const
+    int pos_const;
+    size_t slot_stride, layer_off;
+    int max_seq;             // positions >= max_seq are never read
+    float *att;              // [rows][num_heads][att_ld]
+    size_t att_ld;
+    float *out;              // [rows][dim]
+    size_t ldo;
+    int rows, dim, num_heads, num_kv_heads, head_dim, kv_dim;
+    int max_len;             // upper bound of pos+1 over rows (grid sizing)
+    float scale;             // 1/sqrt(head_dim) computed on the host
+};
+void launch_attention(const AttnArgs &a, cudaStream_t s);
+// the three phases of launch_attention, for callers that time them apart
+void launch_attn_scores(const AttnArgs &a, cudaStream_t s);
+void launch_attn_softmax(const AttnArgs &a, cudaStream_t s);
+void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
+// Opt the attention kernels into `bytes` of dynamic shared memory (current device).
+void set_attention_smem_limit(int bytes);
+
+}  // namespace slm

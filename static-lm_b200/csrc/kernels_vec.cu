@@ -1,0 +1,406 @@
+// kernels_vec.cu -- RMSNorm+Q8 quantize, Q8 quantizers, embedding lookup,
+// argmax and the standalone equivalents of the JIT vector ops.
+//
+// Reductions follow the order of the Cranelift lowering the reference runs
+// (src/jit/lower.rs:252-389): four lane accumulators over [0, len & ~3)
+// where lane l sees elements l, l+4, l+8, ..., then (l0+l1)+(l2+l3), then a
+// sequential tail.  These are serial chains by construction; the kernels
+// keep them on four threads and parallelise everything around them.
+#include <float.h>
+#include <limits.h>
+
+#include "kernels.h"
+
+namespace slm {
+
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// Lane-ordered sum of squares of x[0..n) computed by lanes 0..3 of a warp;
+// the result is returned on every lane.
+__device__ float warp_lane4_sumsq(const float *__restrict__ x, int n, int lane) {
+    int vl = n & ~3;
+    float acc = 0.0f;
+    if (lane < 4) {
+        int i = lane;
+        for (; i + 12 < vl; i += 16) {
+            float v0 = x[i], v1 = x[i + 4], v2 = x[i + 8], v3 = x[i + 12];
+            acc = __fadd_rn(acc, __fmul_rn(v0, v0));
+            acc = __fadd_rn(acc, __fmul_rn(v1, v1));
+            acc = __fadd_rn(acc, __fmul_rn(v2, v2));
+            acc = __fadd_rn(acc, __fmul_rn(v3, v3));
+        }
+        for (; i < vl; i += 4) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
+    }
+    float a1 = __shfl_sync(FULL, acc, 1);
+    float a2 = __shfl_sync(FULL, acc, 2);
+    float a3 = __shfl_sync(FULL, acc, 3);
+    float s = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+    if (lane == 0)
+        for (int i = vl; i < n; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+    return __shfl_sync(FULL, s, 0);
+}
+
+// One warp per row: rms = 1/sqrt(sum(x^2) * (1/n) + eps); y = (x*rms)*w;
+// each full 32-element block of y is quantized to Q8X.
+__global__ void rmsnorm_q8_kernel(const float *__restrict__ x, size_t ldx,
+                                  const float *__restrict__ w, int n, float eps, float inv_n,
+                                  float *__restrict__ y, size_t ldy, Q8X q8, int rows,
+                                  int do_q8) {
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= rows) return;
+    const float *xr = x + (size_t)r * ldx;
+    float s = warp_lane4_sumsq(xr, n, lane);
+    float mean = __fmul_rn(s, inv_n);
+    float var = __fadd_rn(mean, eps);
+    float sd = __fsqrt_rn(var);
+    float rms = __fdiv_rn(1.0f, sd);
+    int nb = n >> 5;
+    for (int j = 0; j < nb; j++) {
+        int i = j * 32 + lane;
+        float o = __fmul_rn(__fmul_rn(xr[i], rms), w[i]);
+        if (y) y[(size_t)r * ldy + i] = o;
+        if (do_q8) q8x_store_block(o, q8, (size_t)r * nb + j, lane);
+    }
+    int i = nb * 32 + lane;
+    if (y && i < n) y[(size_t)r * ldy + i] = __fmul_rn(__fmul_rn(xr[i], rms), w[i]);
+}
+
+// One warp per (row, block).
+__global__ void quantize_q8x_kernel(const float *__restrict__ x, size_t ldx, int nb, Q8X q8,
+                                    int rows) {
+    size_t gw = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (gw >= (size_t)rows * nb) return;
+    size_t r = gw / nb, j = gw % nb;
+    q8x_store_block(x[r * ldx + j * 32 + lane], q8, gw, lane);
+}
+
+// One warp per block, reference 34-byte BlockQ8_0 output (blocks.rs:102-123).
+__global__ void quantize_q8_ref_kernel(const float *__restrict__ x, uint8_t *__restrict__ dst,
+                                       size_t nblocks) {
+    size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (b >= nblocks) return;
+    float v = x[b * 32 + lane];
+    float amax = warp_max_abs(fabsf(v));
+    float d = __fdiv_rn(amax, 127.0f);
+    float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    int q = q8_round(__fmul_rn(v, id));
+    uint8_t *blk = dst + b * 34;
+    blk[2 + lane] = (uint8_t)(int8_t)q;
+    if (lane == 0) *(unsigned short *)blk = __half_as_ushort(__float2half_rn(d));
+}
+
+__global__ void q8_ref_to_q8x_kernel(const uint8_t *__restrict__ src, Q8X q8, size_t nblocks) {
+    size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (b >= nblocks) return;
+    const uint8_t *blk = src + b * 34;
+    int a = (int)(int8_t)blk[2 + lane];
+    a = a < -127 ? -127 : a;
+    q8.qs[b * 32 + lane] = (int8_t)a;
+    int s = a;
+    s += __shfl_xor_sync(FULL, s, 1);
+    s += __shfl_xor_sync(FULL, s, 2);
+    if ((lane & 3) == 0) q8.c[b * 8 + (lane >> 2)] = MAGIC_I - 8 * s;
+    if (lane == 0) q8.d[b] = __half2float(__ushort_as_half(*(const unsigned short *)blk));
+}
+
+// x[r][e] = (nibble - 8) * d of token_embd row tokens[r] (blocks.rs:85-99).
+__global__ void embed_kernel(const uint8_t *__restrict__ tiles, int nb,
+                             const int32_t *__restrict__ tokens, int vocab,
+                             float *__restrict__ x, size_t ldx, int rows, int32_t *err) {
+    int r = blockIdx.y;
+    int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows || e >= nb * 32) return;
+    int tok = tokens[r];
+    if (tok < 0 || tok >= vocab) {
+        if (e == 0 && err) atomicExch(err, 1);
+        x[(size_t)r * ldx + e] = 0.0f;
+        return;
+    }
+    int j = e >> 5, m = e & 31;
+    const uint8_t *t = tiles + tile_offset((size_t)tok / TILE_ROWS, nb, j);
+    int lane = tok % TILE_ROWS;
+    uint8_t byte = t[lane * 16 + (m & 15)];
+    int q = (m < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
+    float d = __half2float(__ushort_as_half(*(const unsigned short *)(t + 512 + lane * 2)));
+    x[(size_t)r * ldx + e] = __fmul_rn((float)q, d);
+}
+
+__global__ void argmax_kernel(const float *__restrict__ logits, size_t ld, int n,
+                              int32_t *__restrict__ out) {
+    const float *l = logits + (size_t)blockIdx.x * ld;
+    float best = -FLT_MAX;
+    int idx = INT_MAX;
+    bool init = false;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = l[i];
+        if (v != v) continue;
+        if (!init || v > best) {
+            best = v;
+            idx = i;
+            init = true;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(FULL, best, o);
+        int oi = __shfl_xor_sync(FULL, idx, o);
+        if (oi != INT_MAX && (idx == INT_MAX || ov > best || (ov == best && oi < idx))) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = idx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int nw = blockDim.x >> 5;
+        best = lane < nw ? sv[lane] : -FLT_MAX;
+        idx = lane < nw ? si[lane] : INT_MAX;
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(FULL, best, o);
+            int oi = __shfl_xor_sync(FULL, idx, o);
+            if (oi != INT_MAX && (idx == INT_MAX || ov > best || (ov == best && oi < idx))) {
+                best = ov;
+                idx = oi;
+            }
+        }
+        if (lane == 0) {
+            float l0 = l[0];
+            // logits[0] NaN: the reference's strict `>` never moves off index 0
+            out[blockIdx.x] = (l0 != l0 || idx == INT_MAX) ? 0 : idx;
+        }
+    }
+}
+
+// ---- standalone JIT-op equivalents (one CTA, any length)
+
+__device__ float block_max_cl(float v, float *sh) {
+    for (int o = 16; o > 0; o >>= 1) v = cl_fmax(v, __shfl_xor_sync(FULL, v, o));
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int nw = blockDim.x >> 5;
+        v = lane < nw ? sh[lane] : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) v = cl_fmax(v, __shfl_xor_sync(FULL, v, o));
+        if (lane == 0) sh[0] = v;
+    }
+    __syncthreads();
+    float r = sh[0];
+    __syncthreads();
+    return r;
+}
+
+// Lane-ordered sum of v[0..len) by threads 0..3; result broadcast through sh.
+__device__ float block_lane4_sum(const float *v, size_t len, float *sh) {
+    size_t vl = len & ~(size_t)3;
+    if (threadIdx.x < 4) {
+        float acc = 0.0f;
+        for (size_t i = threadIdx.x; i < vl; i += 4) acc = __fadd_rn(acc, v[i]);
+        sh[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = __fadd_rn(__fadd_rn(sh[0], sh[1]), __fadd_rn(sh[2], sh[3]));
+        for (size_t i = vl; i < len; i++) s = __fadd_rn(s, v[i]);
+        sh[4] = s;
+    }
+    __syncthreads();
+    float r = sh[4];
+    __syncthreads();
+    return r;
+}
+
+__device__ float block_lane4_sumsq(const float *x, size_t len, float *sh) {
+    size_t vl = len & ~(size_t)3;
+    if (threadIdx.x < 4) {
+        float acc = 0.0f;
+        for (size_t i = threadIdx.x; i < vl; i += 4) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
+        sh[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = __fadd_rn(__fadd_rn(sh[0], sh[1]), __fadd_rn(sh[2], sh[3]));
+        for (size_t i = vl; i < len; i++) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+        sh[4] = s;
+    }
+    __syncthreads();
+    float r = sh[4];
+    __syncthreads();
+    return r;
+}
+
+// graph.rs:168-179; out may alias x
+__global__ void softmax_vec_kernel(const float *x, float *out, size_t len) {
+    __shared__ float sh[32];
+    float m = -INFINITY;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) m = cl_fmax(m, x[i]);
+    float mx = block_max_cl(m, sh);
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) out[i] = exp_poly(__fsub_rn(x[i], mx));
+    __syncthreads();
+    float s = block_lane4_sum(out, len, sh);
+    float inv = __fdiv_rn(1.0f, s);
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) out[i] = __fmul_rn(out[i], inv);
+}
+
+// graph.rs:141-155 compiled with n = len
+__global__ void rmsnorm_vec_kernel(const float *x, const float *w, float *out, size_t len,
+                                   float eps) {
+    __shared__ float sh[32];
+    float s = block_lane4_sumsq(x, len, sh);
+    float inv_n = __fdiv_rn(1.0f, (float)len);
+    float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_n), eps)));
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x)
+        out[i] = __fmul_rn(__fmul_rn(x[i], rms), w[i]);
+}
+
+// graph.rs:182-193
+__global__ void l2norm_vec_kernel(const float *x, float *out, size_t len, float eps) {
+    __shared__ float sh[32];
+    float s = block_lane4_sumsq(x, len, sh);
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s, eps)));
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) out[i] = __fmul_rn(x[i], inv);
+}
+
+__global__ void swiglu_vec_kernel(const float *g, const float *u, float *out, size_t len) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < len) out[i] = swiglu1(g[i], u[i]);
+}
+
+__global__ void residual_vec_kernel(const float *a, const float *b, float *out, size_t len) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < len) out[i] = __fadd_rn(a[i], b[i]);
+}
+
+// transformer.rs:178-194; one thread per (head, pair)
+__global__ void rope_vec_kernel(float *vec, size_t len, const float *cos_row,
+                                const float *sin_row, int head_dim) {
+    size_t p = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int half = head_dim / 2;
+    size_t heads = len / (size_t)head_dim;
+    if (p >= heads * half) return;
+    size_t h = p / half;
+    int j = (int)(p % half);
+    float *hs = vec + h * head_dim;
+    float c = cos_row[j], s = sin_row[j];
+    float v0 = hs[2 * j], v1 = hs[2 * j + 1];
+    hs[2 * j] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    hs[2 * j + 1] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+}
+
+__global__ void mean_pool_kernel(const float *y, size_t ldy, int rows, int n, float inv_batch,
+                                 float *accum) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float acc = 0.0f;
+    for (int b = 0; b < rows; b++) acc = __fadd_rn(acc, __fmul_rn(y[(size_t)b * ldy + i], inv_batch));
+    accum[i] = acc;
+}
+
+__global__ void advance_kernel(int32_t *tokens, int32_t *pos, const int32_t *next, int rows) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    tokens[i] = next[i];
+    pos[i] = pos[i] + 1;
+}
+
+inline unsigned cdiv(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
+
+}  // namespace
+
+void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float eps, float *y,
+                       size_t ldy, Q8X q8, int rows, cudaStream_t s) {
+    if (rows <= 0) return;
+    float inv_n = 1.0f / (float)n;
+    rmsnorm_q8_kernel<<<cdiv(rows, 4), 128, 0, s>>>(x, ldx, w, n, eps, inv_n, y, ldy, q8, rows,
+                                                    q8.qs != nullptr);
+}
+
+void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s) {
+    size_t warps = (size_t)rows * (n / 32);
+    if (!warps) return;
+    quantize_q8x_kernel<<<cdiv(warps, 8), 256, 0, s>>>(x, ldx, n / 32, q8, rows);
+}
+
+void launch_quantize_q8_ref(const float *x, void *blocks, size_t n, cudaStream_t s) {
+    size_t nb = n / 32;
+    if (!nb) return;
+    quantize_q8_ref_kernel<<<cdiv(nb, 8), 256, 0, s>>>(x, (uint8_t *)blocks, nb);
+}
+
+void launch_q8_ref_to_q8x(const void *blocks, Q8X q8, size_t nblocks, cudaStream_t s) {
+    if (!nblocks) return;
+    q8_ref_to_q8x_kernel<<<cdiv(nblocks, 8), 256, 0, s>>>((const uint8_t *)blocks, q8, nblocks);
+}
+
+void launch_embed(const uint8_t *tiles, int nb, const int32_t *tokens, int vocab, float *x,
+                  size_t ldx, int rows, int32_t *err, cudaStream_t s) {
+    if (rows <= 0) return;
+    dim3 grid(cdiv((size_t)nb * 32, 256), rows);
+    embed_kernel<<<grid, 256, 0, s>>>(tiles, nb, tokens, vocab, x, ldx, rows, err);
+}
+
+void launch_argmax(const float *logits, size_t ld, int n, int32_t *out, int rows,
+                   cudaStream_t s) {
+    if (rows <= 0) return;
+    argmax_kernel<<<rows, 1024, 0, s>>>(logits, ld, n, out);
+}
+
+void launch_softmax_vec(const float *x, float *out, size_t len, cudaStream_t s) {
+    if (!len) return;
+    softmax_vec_kernel<<<1, 1024, 0, s>>>(x, out, len);
+}
+
+void launch_rmsnorm_vec(const float *x, const float *w, float *out, size_t len, float eps,
+                        cudaStream_t s) {
+    if (!len) return;
+    rmsnorm_vec_kernel<<<1, 1024, 0, s>>>(x, w, out, len, eps);
+}
+
+void launch_swiglu_vec(const float *g, const float *u, float *out, size_t len, cudaStream_t s) {
+    if (!len) return;
+    swiglu_vec_kernel<<<cdiv(len, 256), 256, 0, s>>>(g, u, out, len);
+}
+
+void launch_residual_add_vec(const float *a, const float *b, float *out, size_t len,
+                             cudaStream_t s) {
+    if (!len) return;
+    residual_vec_kernel<<<cdiv(len, 256), 256, 0, s>>>(a, b, out, len);
+}
+
+void launch_l2norm_vec(const float *x, float *out, size_t len, float eps, cudaStream_t s) {
+    if (!len) return;
+    l2norm_vec_kernel<<<1, 1024, 0, s>>>(x, out, len, eps);
+}
+
+void launch_mean_pool(const float *y, size_t ldy, int rows, int n, float inv_batch,
+                      float *accum, cudaStream_t s) {
+    if (n <= 0) return;
+    mean_pool_kernel<<<cdiv(n, 128), 128, 0, s>>>(y, ldy, rows, n, inv_batch, accum);
+}
+
+void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows,
+                    cudaStream_t s) {
+    if (rows <= 0) return;
+    advance_kernel<<<cdiv(rows, 128), 128, 0, s>>>(tokens, pos, next, rows);
+}
+
+void launch_rope_vec(float *vec, size_t len, const float *cos_row, const float *sin_row,
+                     int head_dim, cudaStream_t s) {
+    size_t pairs = len / (size_t)head_dim * (size_t)(head_dim / 2);
+    if (!pairs) return;
+    rope_vec_kernel<<<cdiv(pairs, 256), 256, 0, s>>>(vec, len, cos_row, sin_row, head_dim);
+}
+
+}  // namespace slm

@@ -1,0 +1,1188 @@
+// runtime.cu -- the C ABI of include/slm_b200.h: device arena, uploaded Q4_0
+// weights, the operator entry points and the model driver (prefill, batched
+// decode, greedy generation, embeddings) with CUDA-graph replay of decode.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/slm_b200.h"
+#include "kernels.h"
+
+using namespace slm;
+
+// The library is built with -fvisibility=hidden; only the C ABI is exported.
+#define SLM_EXPORT extern "C" __attribute__((visibility("default")))
+
+// ============================================================== errors
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+
+#define CUDA_TRY(call)                                                                  \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(SLM_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+#define TRY(expr)                   \
+    do {                            \
+        int rc_ = (expr);           \
+        if (rc_ != SLM_OK) return rc_; \
+    } while (0)
+
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+constexpr uint64_t ARENA_ALIGN_F32 = 16;  // 64 bytes (arena.rs:6-7)
+
+inline uint64_t round_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+int launch_check(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SLM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return SLM_OK;
+}
+
+// kernels with more than 48 KB of dynamic shared memory need an opt-in once
+// per device
+void ensure_kernel_attributes();
+
+}  // namespace
+
+// ============================================================== arena
+
+struct slm_arena {
+    int device;
+    float *base;
+    uint64_t capacity;
+    uint64_t cursor;
+};
+
+namespace {
+
+bool slice_ok(const slm_arena *a, slm_slice s) {
+    return s.offset <= a->capacity && s.len <= a->capacity - s.offset;
+}
+
+bool overlaps(slm_slice a, slm_slice b) {
+    return a.offset < b.offset + b.len && b.offset < a.offset + a.len;
+}
+
+}  // namespace
+
+SLM_EXPORT const char *slm_last_error(void) { return g_err.c_str(); }
+SLM_EXPORT const char *slm_version(void) { return "static-lm-b200 0.1 (sm_100a)"; }
+
+SLM_EXPORT int slm_arena_create(int device, uint64_t capacity, slm_arena **out) {
+    if (!out) return fail(SLM_ERR_INVALID_ARG, "slm_arena_create: out is null");
+    *out = nullptr;
+    DeviceScope ds(device);
+    uint64_t cap = round_up(std::max<uint64_t>(capacity, ARENA_ALIGN_F32), ARENA_ALIGN_F32);
+    float *p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, cap * sizeof(float)));
+    cudaError_t e = cudaMemset(p, 0, cap * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(SLM_ERR_CUDA, std::string("cudaMemset: ") + cudaGetErrorString(e));
+    }
+    *out = new slm_arena{device, p, cap, 0};
+    return SLM_OK;
+}
+
+SLM_EXPORT void slm_arena_destroy(slm_arena *a) {
+    if (!a) return;
+    DeviceScope ds(a->device);
+    cudaFree(a->base);
+    delete a;
+}
+
+SLM_EXPORT int slm_arena_alloc_slice(slm_arena *a, uint64_t len, slm_slice *out) {
+    if (!a || !out) return fail(SLM_ERR_INVALID_ARG, "slm_arena_alloc_slice: null argument");
+    uint64_t off = round_up(a->cursor, ARENA_ALIGN_F32);
+    if (off > a->capacity || len > a->capacity - off)
+        return fail(SLM_ERR_CAPACITY, "AlignedArena out of capacity: requested " +
+                                          std::to_string(len) + " elements at offset " +
+                                          std::to_string(off) + ", capacity " +
+                                          std::to_string(a->capacity));
+    a->cursor = off + len;
+    *out = slm_slice{off, len};
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_arena_alloc_q8_scratch(slm_arena *a, uint64_t num_blocks, slm_slice *out) {
+    return slm_arena_alloc_slice(a, (q8x_bytes(num_blocks) + 3) / 4, out);
+}
+
+SLM_EXPORT void slm_arena_reset(slm_arena *a) {
+    if (a) a->cursor = 0;
+}
+SLM_EXPORT uint64_t slm_arena_capacity(const slm_arena *a) { return a ? a->capacity : 0; }
+SLM_EXPORT uint64_t slm_arena_used(const slm_arena *a) { return a ? a->cursor : 0; }
+
+SLM_EXPORT float *slm_arena_device_ptr(slm_arena *a, slm_slice s) {
+    if (!a || !slice_ok(a, s)) {
+        fail(SLM_ERR_OUT_OF_BOUNDS, "ArenaSlice out of bounds");
+        return nullptr;
+    }
+    return a->base + s.offset;
+}
+
+SLM_EXPORT int slm_arena_write(slm_arena *a, slm_slice s, const float *host, uint64_t n) {
+    if (!a || (!host && n)) return fail(SLM_ERR_INVALID_ARG, "slm_arena_write: null argument");
+    if (!slice_ok(a, s)) return fail(SLM_ERR_OUT_OF_BOUNDS, "ArenaSlice out of bounds");
+    if (n != s.len) return fail(SLM_ERR_SHAPE, "slm_arena_write: length mismatch");
+    DeviceScope ds(a->device);
+    CUDA_TRY(cudaMemcpy(a->base + s.offset, host, n * sizeof(float), cudaMemcpyHostToDevice));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_arena_read(slm_arena *a, slm_slice s, float *host, uint64_t n) {
+    if (!a || (!host && n)) return fail(SLM_ERR_INVALID_ARG, "slm_arena_read: null argument");
+    if (!slice_ok(a, s)) return fail(SLM_ERR_OUT_OF_BOUNDS, "ArenaSlice out of bounds");
+    if (n != s.len) return fail(SLM_ERR_SHAPE, "slm_arena_read: length mismatch");
+    DeviceScope ds(a->device);
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(host, a->base + s.offset, n * sizeof(float), cudaMemcpyDeviceToHost));
+    return SLM_OK;
+}
+
+// ============================================================== Q4_0 weights
+
+namespace {
+
+// BlockQ4_0 rows [rows x cols/32] (18 B each) -> 576-byte row tiles.
+void repack_rows(const uint8_t *src, uint64_t rows, uint64_t nb, uint8_t *dst) {
+    uint64_t tiles = (rows + TILE_ROWS - 1) / TILE_ROWS;
+    std::memset(dst, 0, tiles * nb * TILE_BYTES);
+    for (uint64_t r = 0; r < rows; r++) {
+        uint64_t t = r / TILE_ROWS, lane = r % TILE_ROWS;
+        for (uint64_t j = 0; j < nb; j++) {
+            const uint8_t *blk = src + (r * nb + j) * 18;
+            uint8_t *tp = dst + tile_offset(t, nb, j);
+            std::memcpy(tp + 512 + lane * 2, blk, 2);
+            std::memcpy(tp + lane * 16, blk + 2, 16);
+        }
+    }
+}
+
+void unpack_rows(const uint8_t *tiles, uint64_t rows, uint64_t nb, uint8_t *dst) {
+    for (uint64_t r = 0; r < rows; r++) {
+        uint64_t t = r / TILE_ROWS, lane = r % TILE_ROWS;
+        for (uint64_t j = 0; j < nb; j++) {
+            uint8_t *blk = dst + (r * nb + j) * 18;
+            const uint8_t *tp = tiles + tile_offset(t, nb, j);
+            std::memcpy(blk, tp + 512 + lane * 2, 2);
+            std::memcpy(blk + 2, tp + lane * 16, 16);
+        }
+    }
+}
+
+uint64_t tiled_bytes(uint64_t rows, uint64_t cols) {
+    return (rows + TILE_ROWS - 1) / TILE_ROWS * (cols / QK) * TILE_BYTES;
+}
+
+}  // namespace
+
+struct slm_qmatrix {
+    int device;
+    uint8_t *tiles;
+    uint64_t rows, cols, bytes;
+};
+
+SLM_EXPORT int slm_qmatrix_upload(int device, const void *blocks, uint64_t rows, uint64_t cols,
+                                  slm_qmatrix **out) {
+    if (!blocks || !out) return fail(SLM_ERR_INVALID_ARG, "slm_qmatrix_upload: null argument");
+    *out = nullptr;
+    if (cols == 0 || cols % QK) return fail(SLM_ERR_SHAPE, "cols must be a multiple of 32");
+    if (rows == 0) return fail(SLM_ERR_SHAPE, "rows must be positive");
+    DeviceScope ds(device);
+    uint64_t bytes = tiled_bytes(rows, cols);
+    std::vector<uint8_t> host(bytes);
+    repack_rows((const uint8_t *)blocks, rows, cols / QK, host.data());
+    uint8_t *d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, bytes));
+    cudaError_t e = cudaMemcpy(d, host.data(), bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return fail(SLM_ERR_CUDA, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+    }
+    *out = new slm_qmatrix{device, d, rows, cols, bytes};
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_qmatrix_download(const slm_qmatrix *w, void *blocks_out) {
+    if (!w || !blocks_out) return fail(SLM_ERR_INVALID_ARG, "slm_qmatrix_download: null argument");
+    DeviceScope ds(w->device);
+    std::vector<uint8_t> host(w->bytes);
+    CUDA_TRY(cudaMemcpy(host.data(), w->tiles, w->bytes, cudaMemcpyDeviceToHost));
+    unpack_rows(host.data(), w->rows, w->cols / QK, (uint8_t *)blocks_out);
+    return SLM_OK;
+}
+
+SLM_EXPORT void slm_qmatrix_destroy(slm_qmatrix *w) {
+    if (!w) return;
+    DeviceScope ds(w->device);
+    cudaFree(w->tiles);
+    delete w;
+}
+
+// ============================================================== operators
+
+namespace {
+
+int gemm_into(const slm_qmatrix *w, Q8X x, float *out, uint64_t batch, uint64_t rows,
+              uint64_t cols, cudaStream_t st) {
+    GemvArgs g{};
+    g.w = w->tiles;
+    g.rows = (int)rows;
+    g.nb = (int)(cols / QK);
+    g.x = x;
+    g.batch = (int)batch;
+    g.epi = EPI_STORE;
+    g.out = out;
+    g.ld_out = rows;
+    launch_gemv(g, st);
+    return launch_check("gemv kernel");
+}
+
+int check_gemm_shape(const slm_qmatrix *w, uint64_t batch, uint64_t rows, uint64_t cols) {
+    if (!w) return fail(SLM_ERR_INVALID_ARG, "weights are null");
+    if (cols % QK) return fail(SLM_ERR_SHAPE, "cols must be a multiple of 32");
+    if (w->rows != rows || w->cols != cols)
+        return fail(SLM_ERR_SHAPE, "weights block count mismatch");
+    if (batch > (uint64_t)INT32_MAX || rows > (uint64_t)INT32_MAX)
+        return fail(SLM_ERR_SHAPE, "batch/rows too large");
+    return SLM_OK;
+}
+
+}  // namespace
+
+SLM_EXPORT int slm_gemm_q4_0_arena(slm_arena *a, const slm_qmatrix *w, slm_slice in,
+                                   slm_slice q8, slm_slice outs, uint64_t batch, uint64_t rows,
+                                   uint64_t cols, void *stream) {
+    if (!a) return fail(SLM_ERR_INVALID_ARG, "arena is null");
+    TRY(check_gemm_shape(w, batch, rows, cols));
+    if (in.len != batch * cols) return fail(SLM_ERR_SHAPE, "inputs batch size mismatch");
+    if (outs.len != batch * rows) return fail(SLM_ERR_SHAPE, "output batch size mismatch");
+    if (!slice_ok(a, in) || !slice_ok(a, q8) || !slice_ok(a, outs))
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "ArenaSlice out of bounds");
+    if (overlaps(in, q8) || overlaps(in, outs) || overlaps(q8, outs))
+        return fail(SLM_ERR_OVERLAP, "gemv_slices: slices must be pairwise disjoint");
+    uint64_t blocks = batch * (cols / QK);
+    if (q8x_bytes(blocks) > q8.len * 4) return fail(SLM_ERR_CAPACITY, "q8_scratch slice too small");
+    if (w->device != a->device) return fail(SLM_ERR_INVALID_ARG, "weights on another device");
+    if (batch == 0 || rows == 0) return SLM_OK;
+    DeviceScope ds(a->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    Q8X x = q8x_view(a->base + q8.offset, blocks);
+    launch_quantize_q8x(a->base + in.offset, cols, (int)cols, x, (int)batch, st);
+    TRY(launch_check("quantize kernel"));
+    return gemm_into(w, x, a->base + outs.offset, batch, rows, cols, st);
+}
+
+SLM_EXPORT int slm_gemv_q4_0_arena(slm_arena *a, const slm_qmatrix *w, slm_slice in, slm_slice q8,
+                                   slm_slice out, uint64_t rows, uint64_t cols, void *stream) {
+    if (out.len != rows) return fail(SLM_ERR_SHAPE, "output length mismatch");
+    if (in.len != cols) return fail(SLM_ERR_SHAPE, "input length mismatch");
+    return slm_gemm_q4_0_arena(a, w, in, q8, out, 1, rows, cols, stream);
+}
+
+SLM_EXPORT uint64_t slm_gemm_q4_0_scratch_bytes(uint64_t batch, uint64_t cols) {
+    return q8x_bytes(batch * (cols / QK));
+}
+
+SLM_EXPORT int slm_gemm_q4_0(const slm_qmatrix *w, const void *xq, float *out, uint64_t batch,
+                             uint64_t rows, uint64_t cols, void *scratch, uint64_t scratch_bytes,
+                             void *stream) {
+    TRY(check_gemm_shape(w, batch, rows, cols));
+    if (batch == 0 || rows == 0) return SLM_OK;
+    if (!xq || !out || !scratch) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    uint64_t blocks = batch * (cols / QK);
+    if (scratch_bytes < q8x_bytes(blocks)) return fail(SLM_ERR_CAPACITY, "scratch too small");
+    if ((uintptr_t)scratch % 16) return fail(SLM_ERR_INVALID_ARG, "scratch must be 16-byte aligned");
+    DeviceScope ds(w->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    Q8X x = q8x_view(scratch, blocks);
+    launch_q8_ref_to_q8x(xq, x, blocks, st);
+    TRY(launch_check("q8 conversion kernel"));
+    return gemm_into(w, x, out, batch, rows, cols, st);
+}
+
+SLM_EXPORT int slm_quantize_row_q8_0(const float *src, void *dst, uint64_t n, void *stream) {
+    if (n % QK) return fail(SLM_ERR_SHAPE, "src length must be a multiple of 32");
+    if (n == 0) return SLM_OK;
+    if (!src || !dst) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    launch_quantize_q8_ref(src, dst, n, (cudaStream_t)stream);
+    return launch_check("quantize kernel");
+}
+
+SLM_EXPORT int slm_exec_rmsnorm(const float *const *in, float *out, uint64_t len, float eps,
+                                void *stream) {
+    if (!in || !in[0] || !in[1] || !out) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    launch_rmsnorm_vec(in[0], in[1], out, len, eps, (cudaStream_t)stream);
+    return launch_check("rmsnorm kernel");
+}
+
+SLM_EXPORT int slm_exec_softmax(const float *const *in, float *out, uint64_t len, void *stream) {
+    if (!in || !in[0] || !out) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    launch_softmax_vec(in[0], out, len, (cudaStream_t)stream);
+    return launch_check("softmax kernel");
+}
+
+SLM_EXPORT int slm_exec_swiglu(const float *const *in, float *out, uint64_t len, void *stream) {
+    if (!in || !in[0] || !in[1] || !out) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    launch_swiglu_vec(in[0], in[1], out, len, (cudaStream_t)stream);
+    return launch_check("swiglu kernel");
+}
+
+SLM_EXPORT int slm_exec_residual_add(const float *const *in, float *out, uint64_t len,
+                                     void *stream) {
+    if (!in || !in[0] || !in[1] || !out) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    launch_residual_add_vec(in[0], in[1], out, len, (cudaStream_t)stream);
+    return launch_check("residual kernel");
+}
+
+SLM_EXPORT int slm_exec_l2_norm(const float *const *in, float *out, uint64_t len, float eps,
+                                void *stream) {
+    if (!in || !in[0] || !out) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    launch_l2norm_vec(in[0], out, len, eps, (cudaStream_t)stream);
+    return launch_check("l2norm kernel");
+}
+
+SLM_EXPORT int slm_rope_tables(uint32_t max_seq, uint32_t head_dim, float *cos_out,
+                               float *sin_out) {
+    if ((!cos_out || !sin_out) && max_seq) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    if (head_dim == 0 || head_dim % 2) return fail(SLM_ERR_SHAPE, "head_dim must be even");
+    uint32_t half = head_dim / 2;
+    float hd_f = (float)head_dim;
+    for (uint32_t pos = 0; pos < max_seq; pos++) {
+        float pos_f = (float)pos;
+        for (uint32_t j = 0; j < half; j++) {
+            float freq = 1.0f / powf(10000.0f, (float)(2 * j) / hd_f);
+            float ang = pos_f * freq;
+            sin_out[(size_t)pos * half + j] = sinf(ang);
+            cos_out[(size_t)pos * half + j] = cosf(ang);
+        }
+    }
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_apply_rope_cached(float *vec, uint64_t len, const float *c, const float *s,
+                                     uint32_t head_dim, void *stream) {
+    if (!vec || !c || !s) return fail(SLM_ERR_INVALID_ARG, "null pointer");
+    if (head_dim == 0 || head_dim % 2) return fail(SLM_ERR_SHAPE, "head_dim must be even");
+    launch_rope_vec(vec, len, c, s, (int)head_dim, (cudaStream_t)stream);
+    return launch_check("rope kernel");
+}
+
+namespace {
+
+int check_config(const slm_config *c) {
+    if (!c) return fail(SLM_ERR_INVALID_ARG, "config is null");
+    if (c->dim == 0 || c->dim % QK) return fail(SLM_ERR_SHAPE, "dim must be a multiple of 32");
+    if (c->hidden_dim == 0 || c->hidden_dim % QK)
+        return fail(SLM_ERR_SHAPE, "hidden_dim must be a multiple of 32");
+    if (c->num_heads == 0 || c->num_kv_heads == 0)
+        return fail(SLM_ERR_SHAPE, "head counts must be positive");
+    if (c->dim % c->num_heads) return fail(SLM_ERR_SHAPE, "dim must be divisible by num_heads");
+    if (c->num_heads % c->num_kv_heads)
+        return fail(SLM_ERR_SHAPE, "num_heads must be divisible by num_kv_heads");
+    uint32_t hd = c->dim / c->num_heads;
+    if (hd % 2) return fail(SLM_ERR_SHAPE, "head_dim must be even for RoPE rotation");
+    if ((hd * c->num_kv_heads) % QK) return fail(SLM_ERR_SHAPE, "kv_dim must be a multiple of 32");
+    if (c->num_heads / c->num_kv_heads > 32)
+        return fail(SLM_ERR_SHAPE, "num_heads / num_kv_heads above 32 is not supported");
+    if (c->max_seq_len == 0) return fail(SLM_ERR_SHAPE, "max_seq_len must be positive");
+    if ((uint64_t)c->max_seq_len * 4 > 200 * 1024)
+        return fail(SLM_ERR_SHAPE, "max_seq_len above 51200 is not supported");
+    return SLM_OK;
+}
+
+AttnArgs attn_args_for(const slm_config *c) {
+    AttnArgs a{};
+    a.dim = (int)c->dim;
+    a.num_heads = (int)c->num_heads;
+    a.num_kv_heads = (int)c->num_kv_heads;
+    a.head_dim = (int)(c->dim / c->num_heads);
+    a.kv_dim = a.head_dim * a.num_kv_heads;
+    a.max_seq = (int)c->max_seq_len;
+    a.scale = 1.0f / sqrtf((float)a.head_dim);
+    return a;
+}
+
+}  // namespace
+
+SLM_EXPORT int slm_causal_attention(const float *q, const float *k, const float *v, float *att,
+                                    float *out, const slm_config *cfg, uint32_t pos,
+                                    void *stream) {
+    TRY(check_config(cfg));
+    if (!q || !k || !v || !att || !out) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    if (pos >= cfg->max_seq_len) return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence position out of bounds");
+    ensure_kernel_attributes();
+    AttnArgs a = attn_args_for(cfg);
+    a.q = q;
+    a.ldq = cfg->dim;
+    a.k_base = k;
+    a.v_base = v;
+    a.slot = nullptr;
+    a.pos = nullptr;
+    a.pos_const = (int)pos;
+    a.att = att;
+    a.att_ld = cfg->max_seq_len;
+    a.out = out;
+    a.ldo = cfg->dim;
+    a.rows = 1;
+    a.max_len = (int)pos + 1;
+    launch_attention(a, (cudaStream_t)stream);
+    return launch_check("attention kernels");
+}
+
+SLM_EXPORT int slm_sample_argmax(const float *logits, uint64_t n, int32_t *out, void *stream) {
+    if (n == 0) return fail(SLM_ERR_INVALID_ARG, "logits cannot be empty");
+    if (!logits || !out) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    if (n > (uint64_t)INT32_MAX) return fail(SLM_ERR_SHAPE, "too many logits");
+    launch_argmax(logits, n, (int)n, out, 1, (cudaStream_t)stream);
+    return launch_check("argmax kernel");
+}
+
+// ============================================================== model
+
+namespace {
+
+struct QMat {
+    uint8_t *tiles = nullptr;
+    int rows = 0, cols = 0;
+};
+
+struct LayerDev {
+    QMat wqkv, wo, wgu, wdown;
+    float *rms_att = nullptr, *rms_ffn = nullptr;
+};
+
+enum StepKind { STEP_DECODE = 0, STEP_PREFILL = 1, STEP_EMBED = 2 };
+
+}  // namespace
+
+struct slm_model {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    slm_config cfg{};
+    int L = 0, vocab = 0, S = 0, R = 0, hd = 0, kvd = 0;
+    uint8_t *wbuf = nullptr;
+    uint64_t wbytes = 0;
+    std::vector<LayerDev> layers;
+    QMat embd, lm_head;
+    float *out_norm = nullptr;
+    slm_arena *arena = nullptr;
+    // arena views
+    float *rope_cos, *rope_sin, *x, *x_mid, *xb, *q, *logits, *att, *kv, *ybuf, *emb;
+    void *q8a, *q8b;
+    uint64_t q8_blocks = 0;
+    int32_t *d_tok, *d_pos, *d_slot, *d_next, *d_err;
+    uint64_t slot_stride = 0, layer_stride = 0, v_off = 0;
+    int32_t *h_io = nullptr;  // pinned staging: tok | pos | slot | next, R each
+    std::map<std::tuple<int, int>, cudaGraphExec_t> graphs;
+    bool use_graphs = true;
+};
+
+namespace {
+
+std::vector<uint8_t> concat_rows(const std::vector<std::pair<const void *, uint64_t>> &parts,
+                                 uint64_t cols) {
+    uint64_t nb = cols / QK, total = 0;
+    for (auto &p : parts) total += p.second;
+    std::vector<uint8_t> v(total * nb * 18);
+    uint64_t off = 0;
+    for (auto &p : parts) {
+        std::memcpy(v.data() + off, p.first, p.second * nb * 18);
+        off += p.second * nb * 18;
+    }
+    return v;
+}
+
+// Upload a row-concatenation of Q4_0 matrices into wbuf at `*cursor`.
+int upload_qmat(slm_model *m, const std::vector<std::pair<const void *, uint64_t>> &parts,
+                uint64_t cols, uint64_t *cursor, QMat *out) {
+    std::vector<uint8_t> src = concat_rows(parts, cols);
+    uint64_t rows = src.size() / ((cols / QK) * 18);
+    uint64_t bytes = tiled_bytes(rows, cols);
+    std::vector<uint8_t> tiles(bytes);
+    repack_rows(src.data(), rows, cols / QK, tiles.data());
+    CUDA_TRY(cudaMemcpy(m->wbuf + *cursor, tiles.data(), bytes, cudaMemcpyHostToDevice));
+    out->tiles = m->wbuf + *cursor;
+    out->rows = (int)rows;
+    out->cols = (int)cols;
+    *cursor += round_up(bytes, 256);
+    return SLM_OK;
+}
+
+int upload_f32(slm_model *m, const float *src, uint64_t n, uint64_t *cursor, float **out) {
+    CUDA_TRY(cudaMemcpy(m->wbuf + *cursor, src, n * 4, cudaMemcpyHostToDevice));
+    *out = (float *)(m->wbuf + *cursor);
+    *cursor += round_up(n * 4, 256);
+    return SLM_OK;
+}
+
+Q8X q8view(void *p, uint64_t blocks) { return q8x_view(p, blocks); }
+
+// Records an event on the model stream at every phase boundary; the interval
+// since the previous mark is attributed to the phase passed to mark().
+struct Profiler {
+    cudaStream_t st = nullptr;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> phase;
+    size_t n = 0;
+    void mark(int ph) {
+        if (n < ev.size()) {
+            cudaEventRecord(ev[n], st);
+            phase[n] = ph;
+            n++;
+        }
+    }
+};
+
+inline void mark(Profiler *p, int ph) {
+    if (p) p->mark(ph);
+}
+
+// Enqueue one forward pass over `n` activation rows already holding token
+// ids / slots / positions in d_tok / d_slot / d_pos.
+void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *prof = nullptr) {
+    cudaStream_t st = m->stream;
+    const slm_config &c = m->cfg;
+    const int d = (int)c.dim, h = (int)c.hidden_dim;
+    mark(prof, -1);
+    launch_embed(m->embd.tiles, d / QK, m->d_tok, m->vocab, m->x, d, n, m->d_err, st);
+    mark(prof, SLM_PHASE_EMBED);
+
+    QkvArgs qa{};
+    qa.q = m->q;
+    qa.ldq = d;
+    qa.k_base = m->kv;
+    qa.v_base = m->kv + m->v_off;
+    qa.slot = m->d_slot;
+    qa.pos = m->d_pos;
+    qa.slot_stride = m->slot_stride;
+    qa.dim = d;
+    qa.kv_dim = m->kvd;
+    qa.head_dim = m->hd;
+    qa.max_seq = (int)c.max_seq_len;
+    qa.rope_cos = m->rope_cos;
+    qa.rope_sin = m->rope_sin;
+    qa.err = m->d_err;
+
+    AttnArgs aa = attn_args_for(&c);
+    aa.q = m->q;
+    aa.ldq = d;
+    aa.k_base = m->kv;
+    aa.v_base = m->kv + m->v_off;
+    aa.slot = m->d_slot;
+    aa.pos = m->d_pos;
+    aa.slot_stride = m->slot_stride;
+    aa.att = m->att;
+    aa.att_ld = c.max_seq_len;
+    aa.out = m->xb;
+    aa.ldo = d;
+    aa.rows = n;
+    aa.max_len = max_len;
+
+    Q8X qa8 = q8view(m->q8a, m->q8_blocks), qb8 = q8view(m->q8b, m->q8_blocks);
+    for (int l = 0; l < m->L; l++) {
+        const LayerDev &ld = m->layers[l];
+        // rmsnorm(x) -> Q8 (transformer.rs:411, kernels.rs:301)
+        launch_rmsnorm_q8(m->x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
+        mark(prof, SLM_PHASE_RMSNORM);
+        // Wq/Wk/Wv + RoPE + KV append (transformer.rs:413-428)
+        GemvArgs g{};
+        g.w = ld.wqkv.tiles;
+        g.rows = ld.wqkv.rows;
+        g.nb = d / QK;
+        g.x = qa8;
+        g.batch = n;
+        g.epi = EPI_QKV;
+        qa.layer_off = (size_t)l * m->layer_stride;
+        g.qkv = qa;
+        launch_gemv(g, st);
+        mark(prof, SLM_PHASE_QKV);
+        // attention (transformer.rs:430-443)
+        aa.layer_off = (size_t)l * m->layer_stride;
+        launch_attn_scores(aa, st);
+        mark(prof, SLM_PHASE_ATTN_SCORES);
+        launch_attn_softmax(aa, st);
+        mark(prof, SLM_PHASE_ATTN_SOFTMAX);
+        launch_attn_pv(aa, st);
+        mark(prof, SLM_PHASE_ATTN_PV);
+        // Wo + residual (transformer.rs:445-446)
+        launch_quantize_q8x(m->xb, d, d, qb8, n, st);
+        mark(prof, SLM_PHASE_QUANTIZE);
+        g = GemvArgs{};
+        g.w = ld.wo.tiles;
+        g.rows = d;
+        g.nb = d / QK;
+        g.x = qb8;
+        g.batch = n;
+        g.epi = EPI_RESIDUAL;
+        g.out = m->x_mid;
+        g.ld_out = d;
+        g.res = m->x;
+        g.ld_res = d;
+        launch_gemv(g, st);
+        mark(prof, SLM_PHASE_WO);
+        // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
+        launch_rmsnorm_q8(m->x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
+        mark(prof, SLM_PHASE_RMSNORM);
+        g = GemvArgs{};
+        g.w = ld.wgu.tiles;
+        g.rows = 2 * h;
+        g.nb = d / QK;
+        g.x = qa8;
+        g.batch = n;
+        g.epi = EPI_SWIGLU_Q8;
+        g.q8_out = qb8;
+        launch_gemv(g, st);
+        mark(prof, SLM_PHASE_GATE_UP);
+        // down + residual (transformer.rs:477-486)
+        g = GemvArgs{};
+        g.w = ld.wdown.tiles;
+        g.rows = d;
+        g.nb = h / QK;
+        g.x = qb8;
+        g.batch = n;
+        g.epi = EPI_RESIDUAL;
+        g.out = m->x;
+        g.ld_out = d;
+        g.res = m->x_mid;
+        g.ld_res = d;
+        launch_gemv(g, st);
+        mark(prof, SLM_PHASE_DOWN);
+    }
+    if (kind == STEP_EMBED) return;
+    // final RMSNorm + lm_head + argmax (transformer.rs:776-794 / 835-853)
+    const float *xs = kind == STEP_PREFILL ? m->x + (size_t)(n - 1) * d : m->x;
+    int rows = kind == STEP_PREFILL ? 1 : n;
+    launch_rmsnorm_q8(xs, d, m->out_norm, d, c.rms_eps, nullptr, 0, qa8, rows, st);
+    mark(prof, SLM_PHASE_RMSNORM);
+    GemvArgs g{};
+    g.w = m->lm_head.tiles;
+    g.rows = m->vocab;
+    g.nb = d / QK;
+    g.x = qa8;
+    g.batch = rows;
+    g.epi = EPI_STORE;
+    g.out = m->logits;
+    g.ld_out = m->vocab;
+    launch_gemv(g, st);
+    mark(prof, SLM_PHASE_LM_HEAD);
+    launch_argmax(m->logits, m->vocab, m->vocab, m->d_next, rows, st);
+    mark(prof, SLM_PHASE_ARGMAX);
+}
+
+// kernel launches of one decode step (enqueue_forward + the greedy advance)
+uint32_t decode_launches(const slm_model *m) { return 1u + 10u * (uint32_t)m->L + 4u + 1u; }
+
+int len_bucket(const slm_model *m, int max_len) {
+    int b = (max_len + 255) / 256 * 256;
+    return std::min<int>(b, (int)m->cfg.max_seq_len);
+}
+
+// Run a decode step (optionally followed by the greedy advance) through a
+// cached CUDA graph keyed by (rows, length bucket, advance).
+int run_decode(slm_model *m, int n, int max_len, bool advance) {
+    int bucket = len_bucket(m, max_len);
+    if (!m->use_graphs) {
+        enqueue_forward(m, n, bucket, STEP_DECODE);
+        if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
+        return launch_check("decode step");
+    }
+    auto key = std::make_tuple(n * 2 + (advance ? 1 : 0), bucket);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t graph = nullptr;
+        CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        enqueue_forward(m, n, bucket, STEP_DECODE);
+        if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
+        cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(SLM_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+        }
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail(SLM_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        it = m->graphs.emplace(key, exec).first;
+    }
+    CUDA_TRY(cudaGraphLaunch(it->second, m->stream));
+    return SLM_OK;
+}
+
+int read_device_error(slm_model *m) {
+    int32_t err = 0;
+    CUDA_TRY(cudaMemcpyAsync(&err, m->d_err, 4, cudaMemcpyDeviceToHost, m->stream));
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    if (err) {
+        CUDA_TRY(cudaMemsetAsync(m->d_err, 0, 4, m->stream));
+        CUDA_TRY(cudaStreamSynchronize(m->stream));
+        return fail(SLM_ERR_DEVICE_INPUT, err == 1 ? "token_id out of vocabulary bounds"
+                                                   : "sequence position out of bounds");
+    }
+    return SLM_OK;
+}
+
+int alloc_view(slm_model *m, uint64_t floats, float **out) {
+    slm_slice s;
+    TRY(slm_arena_alloc_slice(m->arena, floats, &s));
+    *out = m->arena->base + s.offset;
+    return SLM_OK;
+}
+
+}  // namespace
+
+namespace {
+void ensure_kernel_attributes() {
+    // cudaFuncSetAttribute is per device and cheap; the attention softmax
+    // stages up to max_seq_len floats in dynamic shared memory.
+    static thread_local int done_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 31 && (done_mask & (1 << dev))) return;
+    slm::set_attention_smem_limit(200 * 1024);
+    if (dev < 31) done_mask |= 1 << dev;
+}
+}  // namespace
+
+SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_model_weights *w,
+                                uint32_t max_sequences, uint32_t max_rows, slm_model **out) {
+    if (!out) return fail(SLM_ERR_INVALID_ARG, "out is null");
+    *out = nullptr;
+    TRY(check_config(cfg));
+    if (!w || !w->token_embd || !w->output_norm || (!w->layers && w->num_layers))
+        return fail(SLM_ERR_INVALID_ARG, "weights are null");
+    if (w->vocab_size == 0) return fail(SLM_ERR_INVALID_ARG, "vocab_size must be positive");
+    if (max_sequences == 0 || max_rows == 0)
+        return fail(SLM_ERR_INVALID_ARG, "max_sequences and max_rows must be positive");
+    for (uint32_t l = 0; l < w->num_layers; l++) {
+        const slm_layer_weights &lw = w->layers[l];
+        if (!lw.rms_att_weight || !lw.wq || !lw.wk || !lw.wv || !lw.wo || !lw.rms_ffn_weight ||
+            !lw.w_gate || !lw.w_up || !lw.w_down)
+            return fail(SLM_ERR_INVALID_ARG, "layer " + std::to_string(l) + " has a null tensor");
+    }
+    DeviceScope ds(device);
+    ensure_kernel_attributes();
+    slm_model *m = new slm_model();
+    m->device = device;
+    m->cfg = *cfg;
+    m->L = (int)w->num_layers;
+    m->vocab = (int)w->vocab_size;
+    m->S = (int)max_sequences;
+    m->R = (int)std::max(max_rows, max_sequences);
+    m->hd = (int)(cfg->dim / cfg->num_heads);
+    m->kvd = m->hd * (int)cfg->num_kv_heads;
+    const uint64_t d = cfg->dim, h = cfg->hidden_dim, kvd = m->kvd, V = m->vocab;
+    auto cleanup = [&](int rc) {
+        slm_model_destroy(m);
+        return rc;
+    };
+    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, cudaGetErrorString(e)));
+
+    // ---- weights: one device buffer
+    uint64_t need = 0;
+    auto add = [&](uint64_t rows, uint64_t cols) { need += round_up(tiled_bytes(rows, cols), 256); };
+    for (int l = 0; l < m->L; l++) {
+        add(d + 2 * kvd, d);
+        add(d, d);
+        add(2 * h, d);
+        add(d, h);
+        need += 2 * round_up(d * 4, 256);
+    }
+    add(V, d);
+    add(V, d);
+    need += round_up(d * 4, 256);
+    e = cudaMalloc(&m->wbuf, need);
+    if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, std::string("weights: ") + cudaGetErrorString(e)));
+    m->wbytes = need;
+    uint64_t cur = 0;
+    m->layers.resize(m->L);
+    for (int l = 0; l < m->L; l++) {
+        const slm_layer_weights &lw = w->layers[l];
+        LayerDev &ld = m->layers[l];
+        int rc;
+        if ((rc = upload_qmat(m, {{lw.wq, d}, {lw.wk, kvd}, {lw.wv, kvd}}, d, &cur, &ld.wqkv)) ||
+            (rc = upload_qmat(m, {{lw.wo, d}}, d, &cur, &ld.wo)) ||
+            (rc = upload_qmat(m, {{lw.w_gate, h}, {lw.w_up, h}}, d, &cur, &ld.wgu)) ||
+            (rc = upload_qmat(m, {{lw.w_down, d}}, h, &cur, &ld.wdown)) ||
+            (rc = upload_f32(m, lw.rms_att_weight, d, &cur, &ld.rms_att)) ||
+            (rc = upload_f32(m, lw.rms_ffn_weight, d, &cur, &ld.rms_ffn)))
+            return cleanup(rc);
+    }
+    int rc;
+    if ((rc = upload_qmat(m, {{w->token_embd, V}}, d, &cur, &m->embd)) ||
+        (rc = upload_qmat(m, {{w->lm_head ? w->lm_head : w->token_embd, V}}, d, &cur,
+                          &m->lm_head)) ||
+        (rc = upload_f32(m, w->output_norm, d, &cur, &m->out_norm)))
+        return cleanup(rc);
+
+    // ---- arena (LayerWorkspace + BatchWorkspace + LayerKvCache per sequence)
+    const uint64_t R = m->R, S = m->S, T = cfg->max_seq_len;
+    const uint64_t maxk = std::max(d, h);
+    m->q8_blocks = R * (maxk / QK);
+    uint64_t q8f = (q8x_bytes(m->q8_blocks) + 3) / 4;
+    m->v_off = T * kvd;
+    m->layer_stride = 2 * T * kvd;
+    m->slot_stride = (uint64_t)m->L * m->layer_stride;
+    uint64_t a16 = ARENA_ALIGN_F32;
+    uint64_t cap = 0;
+    auto add_f = [&](uint64_t n) { cap = round_up(cap, a16) + n; };
+    add_f(T * (m->hd / 2));  // rope cos
+    add_f(T * (m->hd / 2));  // rope sin
+    for (int i = 0; i < 4; i++) add_f(R * d);  // x, x_mid, xb, q
+    add_f(R * d);                              // ybuf (embedding rows)
+    add_f(d);                                  // embedding accumulator
+    add_f(S * V);                              // logits
+    add_f(R * cfg->num_heads * T);             // att
+    add_f(q8f);
+    add_f(q8f);
+    for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
+    add_f(S * m->slot_stride);                 // KV
+    rc = slm_arena_create(device, cap + a16, &m->arena);
+    if (rc) return cleanup(rc);
+    float *p;
+    std::vector<float> cs(T * (m->hd / 2)), sn(T * (m->hd / 2));
+    slm_rope_tables((uint32_t)T, (uint32_t)m->hd, cs.data(), sn.data());
+    if ((rc = alloc_view(m, T * (m->hd / 2), &m->rope_cos)) ||
+        (rc = alloc_view(m, T * (m->hd / 2), &m->rope_sin)) || (rc = alloc_view(m, R * d, &m->x)) ||
+        (rc = alloc_view(m, R * d, &m->x_mid)) || (rc = alloc_view(m, R * d, &m->xb)) ||
+        (rc = alloc_view(m, R * d, &m->q)) || (rc = alloc_view(m, R * d, &m->ybuf)) ||
+        (rc = alloc_view(m, d, &m->emb)) || (rc = alloc_view(m, S * V, &m->logits)) ||
+        (rc = alloc_view(m, R * cfg->num_heads * T, &m->att)))
+        return cleanup(rc);
+    if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
+    m->q8a = p;
+    if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
+    m->q8b = p;
+    int32_t **ints[] = {&m->d_tok, &m->d_pos, &m->d_slot, &m->d_next, &m->d_err};
+    for (auto ip : ints) {
+        if ((rc = alloc_view(m, R, &p))) return cleanup(rc);
+        *ip = (int32_t *)p;
+    }
+    if ((rc = alloc_view(m, S * m->slot_stride, &m->kv))) return cleanup(rc);
+    e = cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMallocHost(&m->h_io, 4 * R * sizeof(int32_t));
+    if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, cudaGetErrorString(e)));
+    const char *env = getenv("SLM_DISABLE_GRAPHS");
+    m->use_graphs = !(env && env[0] == '1');
+    *out = m;
+    return SLM_OK;
+}
+
+SLM_EXPORT void slm_model_destroy(slm_model *m) {
+    if (!m) return;
+    DeviceScope ds(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto &kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    if (m->h_io) cudaFreeHost(m->h_io);
+    if (m->arena) slm_arena_destroy(m->arena);
+    if (m->wbuf) cudaFree(m->wbuf);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+SLM_EXPORT void *slm_model_stream(slm_model *m) { return m ? (void *)m->stream : nullptr; }
+
+SLM_EXPORT uint64_t slm_model_device_bytes(const slm_model *m) {
+    return m ? m->wbytes + m->arena->capacity * 4 : 0;
+}
+
+namespace {
+
+// Stage host rows (token, slot, position) into the device row arrays.
+int stage_rows(slm_model *m, int n, const int32_t *tok, const uint32_t *slot, uint32_t slot_const,
+               const uint32_t *pos, uint32_t pos0) {
+    int32_t *ht = m->h_io, *hp = m->h_io + m->R, *hs = m->h_io + 2 * m->R;
+    for (int i = 0; i < n; i++) {
+        ht[i] = tok[i];
+        hs[i] = (int32_t)(slot ? slot[i] : slot_const);
+        hp[i] = (int32_t)(pos ? pos[i] : pos0 + (uint32_t)i);
+    }
+    CUDA_TRY(cudaMemcpyAsync(m->d_tok, ht, n * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaMemcpyAsync(m->d_pos, hp, n * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaMemcpyAsync(m->d_slot, hs, n * 4, cudaMemcpyHostToDevice, m->stream));
+    return SLM_OK;
+}
+
+int fetch_next(slm_model *m, int n, int32_t *next) {
+    int32_t *hn = m->h_io + 3 * m->R;
+    CUDA_TRY(cudaMemcpyAsync(hn, m->d_next, n * 4, cudaMemcpyDeviceToHost, m->stream));
+    TRY(read_device_error(m));  // synchronizes
+    std::memcpy(next, hn, n * 4);
+    return SLM_OK;
+}
+
+int check_tokens(const slm_model *m, int n, const int32_t *tok) {
+    for (int i = 0; i < n; i++)
+        if (tok[i] < 0 || tok[i] >= m->vocab)
+            return fail(SLM_ERR_OUT_OF_BOUNDS, "token_id out of vocabulary bounds");
+    return SLM_OK;
+}
+
+}  // namespace
+
+SLM_EXPORT int slm_model_decode_batch(slm_model *m, uint32_t n, const uint32_t *seqs,
+                                      const int32_t *tokens, const uint32_t *pos,
+                                      int32_t *next) {
+    if (!m || !seqs || !tokens || !pos || !next) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return SLM_OK;
+    if (n > (uint32_t)m->R || n > (uint32_t)m->S)
+        return fail(SLM_ERR_CAPACITY, "batch larger than the model's max_rows/max_sequences");
+    TRY(check_tokens(m, (int)n, tokens));
+    uint32_t max_pos = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        if (seqs[i] >= (uint32_t)m->S) return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence out of range");
+        if (pos[i] >= m->cfg.max_seq_len)
+            return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence position out of bounds");
+        for (uint32_t k = 0; k < i; k++)
+            if (seqs[k] == seqs[i]) return fail(SLM_ERR_INVALID_ARG, "duplicate sequence in batch");
+        max_pos = std::max(max_pos, pos[i]);
+    }
+    DeviceScope ds(m->device);
+    TRY(stage_rows(m, (int)n, tokens, seqs, 0, pos, 0));
+    TRY(run_decode(m, (int)n, (int)max_pos + 1, false));
+    return fetch_next(m, (int)n, next);
+}
+
+SLM_EXPORT int slm_model_forward_token(slm_model *m, uint32_t seq, int32_t token, uint32_t pos,
+                                       int32_t *next) {
+    return slm_model_decode_batch(m, 1, &seq, &token, &pos, next);
+}
+
+SLM_EXPORT int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_t *tokens,
+                                        uint32_t n, uint32_t start_pos, int32_t *next) {
+    if (!m || !tokens || !next) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return fail(SLM_ERR_INVALID_ARG, "prompt_tokens cannot be empty");
+    if (n > (uint32_t)m->R) return fail(SLM_ERR_CAPACITY, "prompt longer than max_rows");
+    if (seq >= (uint32_t)m->S) return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence out of range");
+    if ((uint64_t)start_pos + n > m->cfg.max_seq_len)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "start_pos + batch_size exceeds max_seq_len");
+    TRY(check_tokens(m, (int)n, tokens));
+    DeviceScope ds(m->device);
+    TRY(stage_rows(m, (int)n, tokens, nullptr, seq, nullptr, start_pos));
+    enqueue_forward(m, (int)n, (int)(start_pos + n), STEP_PREFILL);
+    TRY(launch_check("prefill"));
+    return fetch_next(m, 1, next);
+}
+
+SLM_EXPORT int slm_model_generate(slm_model *m, uint32_t seq, const int32_t *prompt,
+                                  uint32_t n_prompt, int32_t *out, uint32_t n_out, int32_t eos,
+                                  uint32_t *generated) {
+    if (!m || !generated) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    *generated = 0;
+    if (n_out == 0 || n_prompt == 0) return SLM_OK;
+    if (!prompt || !out) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n_prompt > m->cfg.max_seq_len) return fail(SLM_ERR_OUT_OF_BOUNDS, "prompt longer than max_seq_len");
+    int32_t next = 0;
+    TRY(slm_model_prefill_tokens(m, seq, prompt, n_prompt, 0, &next));
+    out[0] = next;
+    uint32_t gen = 1;
+    if (eos >= 0 && next == eos) {
+        *generated = gen;
+        return SLM_OK;
+    }
+    uint32_t pos = n_prompt;
+    while (gen < n_out && pos < m->cfg.max_seq_len) {
+        TRY(slm_model_forward_token(m, seq, next, pos, &next));
+        out[gen++] = next;
+        pos++;
+        if (eos >= 0 && next == eos) break;
+    }
+    *generated = gen;
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_embed_tokens(slm_model *m, uint32_t seq, const int32_t *tokens,
+                                      uint32_t n, float *out_embedding) {
+    if (!m || !tokens || !out_embedding) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return fail(SLM_ERR_INVALID_ARG, "tokens cannot be empty");
+    if (n > (uint32_t)m->R || n > m->cfg.max_seq_len)
+        return fail(SLM_ERR_CAPACITY, "too many tokens for max_rows/max_seq_len");
+    if (seq >= (uint32_t)m->S) return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence out of range");
+    TRY(check_tokens(m, (int)n, tokens));
+    DeviceScope ds(m->device);
+    const int d = (int)m->cfg.dim;
+    TRY(stage_rows(m, (int)n, tokens, nullptr, seq, nullptr, 0));
+    enqueue_forward(m, (int)n, (int)n, STEP_EMBED);
+    Q8X none{};
+    launch_rmsnorm_q8(m->x, d, m->out_norm, d, m->cfg.rms_eps, m->ybuf, d, none, (int)n, m->stream);
+    launch_mean_pool(m->ybuf, d, (int)n, d, 1.0f / (float)n, m->emb, m->stream);
+    launch_l2norm_vec(m->emb, m->emb, d, m->cfg.rms_eps, m->stream);
+    TRY(launch_check("embed"));
+    std::vector<float> host(d);
+    CUDA_TRY(cudaMemcpyAsync(host.data(), m->emb, d * 4, cudaMemcpyDeviceToHost, m->stream));
+    TRY(read_device_error(m));
+    std::memcpy(out_embedding, host.data(), d * 4);
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_decode_steps_device(slm_model *m, uint32_t n, const uint32_t *seqs_dev,
+                                             int32_t *tokens_dev, uint32_t *pos_dev,
+                                             uint32_t steps, int32_t *out_dev,
+                                             uint32_t max_pos_hint) {
+    if (!m || !seqs_dev || !tokens_dev || !pos_dev) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n == 0 || steps == 0) return SLM_OK;
+    if (n > (uint32_t)m->R || n > (uint32_t)m->S)
+        return fail(SLM_ERR_CAPACITY, "batch larger than the model's max_rows/max_sequences");
+    if ((uint64_t)max_pos_hint + steps > m->cfg.max_seq_len)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "decode would run past max_seq_len");
+    DeviceScope ds(m->device);
+    cudaStream_t st = m->stream;
+    CUDA_TRY(cudaMemcpyAsync(m->d_slot, seqs_dev, n * 4, cudaMemcpyDeviceToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->d_tok, tokens_dev, n * 4, cudaMemcpyDeviceToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m->d_pos, pos_dev, n * 4, cudaMemcpyDeviceToDevice, st));
+    for (uint32_t s = 0; s < steps; s++) {
+        TRY(run_decode(m, (int)n, (int)(max_pos_hint + s + 1), true));
+        if (out_dev)
+            CUDA_TRY(cudaMemcpyAsync(out_dev + (size_t)s * n, m->d_tok, n * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+    }
+    CUDA_TRY(cudaMemcpyAsync(tokens_dev, m->d_tok, n * 4, cudaMemcpyDeviceToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(pos_dev, m->d_pos, n * 4, cudaMemcpyDeviceToDevice, st));
+    return SLM_OK;
+}
+
+namespace {
+int kv_ptr(slm_model *m, uint32_t seq, uint32_t layer, uint32_t which, uint32_t row0,
+           uint32_t nrows, float **p) {
+    if (seq >= (uint32_t)m->S || layer >= (uint32_t)m->L || which > 1)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence/layer/which out of range");
+    if ((uint64_t)row0 + nrows > m->cfg.max_seq_len)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "rows beyond max_seq_len");
+    *p = m->kv + seq * m->slot_stride + layer * m->layer_stride + which * m->v_off +
+         (uint64_t)row0 * m->kvd;
+    return SLM_OK;
+}
+}  // namespace
+
+SLM_EXPORT int slm_model_kv_write(slm_model *m, uint32_t seq, uint32_t layer, uint32_t which,
+                                  uint32_t row0, uint32_t nrows, const float *host) {
+    if (!m || (!host && nrows)) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    float *p;
+    TRY(kv_ptr(m, seq, layer, which, row0, nrows, &p));
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    CUDA_TRY(cudaMemcpy(p, host, (size_t)nrows * m->kvd * 4, cudaMemcpyHostToDevice));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_kv_read(slm_model *m, uint32_t seq, uint32_t layer, uint32_t which,
+                                 uint32_t row0, uint32_t nrows, float *host) {
+    if (!m || (!host && nrows)) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    float *p;
+    TRY(kv_ptr(m, seq, layer, which, row0, nrows, &p));
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    CUDA_TRY(cudaMemcpy(host, p, (size_t)nrows * m->kvd * 4, cudaMemcpyDeviceToHost));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_read_logits(slm_model *m, uint32_t row, float *host) {
+    if (!m || !host) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (row >= (uint32_t)m->S) return fail(SLM_ERR_OUT_OF_BOUNDS, "row out of range");
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    CUDA_TRY(cudaMemcpy(host, m->logits + (size_t)row * m->vocab, (size_t)m->vocab * 4,
+                        cudaMemcpyDeviceToHost));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_read_hidden(slm_model *m, uint32_t row, float *host) {
+    if (!m || !host) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (row >= (uint32_t)m->R) return fail(SLM_ERR_OUT_OF_BOUNDS, "row out of range");
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    CUDA_TRY(cudaMemcpy(host, m->x + (size_t)row * m->cfg.dim, (size_t)m->cfg.dim * 4,
+                        cudaMemcpyDeviceToHost));
+    return SLM_OK;
+}
+
+SLM_EXPORT uint32_t slm_model_launches_per_decode_step(const slm_model *m) {
+    return m ? decode_launches(m) : 0;
+}
+
+SLM_EXPORT int slm_model_kv_write_device(slm_model *m, uint32_t seq, uint32_t layer,
+                                         uint32_t which, uint32_t row0, uint32_t nrows,
+                                         const float *src_dev) {
+    if (!m || (!src_dev && nrows)) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    float *p;
+    TRY(kv_ptr(m, seq, layer, which, row0, nrows, &p));
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaMemcpyAsync(p, src_dev, (size_t)nrows * m->kvd * 4, cudaMemcpyDeviceToDevice,
+                             m->stream));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_profile_decode(slm_model *m, uint32_t n, const uint32_t *seqs_dev,
+                                        int32_t *tokens_dev, uint32_t *pos_dev, uint32_t steps,
+                                        uint32_t max_pos_hint, float *phase_ms) {
+    if (!m || !seqs_dev || !tokens_dev || !pos_dev || !phase_ms)
+        return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (n == 0 || n > (uint32_t)m->R || n > (uint32_t)m->S)
+        return fail(SLM_ERR_CAPACITY, "batch larger than the model's max_rows/max_sequences");
+    if ((uint64_t)max_pos_hint + steps > m->cfg.max_seq_len)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "decode would run past max_seq_len");
+    DeviceScope ds(m->device);
+    cudaStream_t st = m->stream;
+    for (int i = 0; i < SLM_NUM_PHASES; i++) phase_ms[i] = 0.0f;
+    Profiler prof;
+    prof.st = st;
+    size_t nev = 8 + (size_t)m->L * 12;
+    prof.ev.resize(nev);
+    prof.phase.resize(nev);
+    for (auto &e : prof.ev) CUDA_TRY(cudaEventCreate(&e));
+    int rc = SLM_OK;
+    cudaError_t e = cudaMemcpyAsync(m->d_slot, seqs_dev, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_tok, tokens_dev, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_pos, pos_dev, n * 4, cudaMemcpyDeviceToDevice, st);
+    for (uint32_t s = 0; s < steps && e == cudaSuccess && rc == SLM_OK; s++) {
+        prof.n = 0;
+        enqueue_forward(m, (int)n, len_bucket(m, (int)(max_pos_hint + s + 1)), STEP_DECODE, &prof);
+        launch_advance(m->d_tok, m->d_pos, m->d_next, (int)n, st);
+        prof.mark(SLM_PHASE_ADVANCE);
+        e = cudaStreamSynchronize(st);
+        for (size_t i = 1; i < prof.n && e == cudaSuccess; i++) {
+            float ms = 0.0f;
+            e = cudaEventElapsedTime(&ms, prof.ev[i - 1], prof.ev[i]);
+            if (prof.phase[i] >= 0 && prof.phase[i] < SLM_NUM_PHASES) phase_ms[prof.phase[i]] += ms;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tokens_dev, m->d_tok, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(pos_dev, m->d_pos, n * 4, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    for (auto &ev : prof.ev) cudaEventDestroy(ev);
+    if (e != cudaSuccess) return fail(SLM_ERR_CUDA, std::string("profile: ") + cudaGetErrorString(e));
+    return rc;
+}
