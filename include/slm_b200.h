@@ -249,7 +249,8 @@ enum {
     SLM_PHASE_LM_HEAD = 10,
     SLM_PHASE_ARGMAX = 11,
     SLM_PHASE_ADVANCE = 12,
-    SLM_NUM_PHASES = 13
+    SLM_PHASE_ATTN_FUSED = 13,   /* scores + softmax + PV (+ Q8_0) in one kernel */
+    SLM_NUM_PHASES = 14
 };
 /* Same work as slm_model_decode_steps_device, launched without graphs and
  * with a CUDA event on the model stream at every phase boundary; adds each

@@ -15,6 +15,7 @@ namespace slm {
 // y (optional) receives the f32 normalized rows.
 void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float eps,
                        float *y, size_t ldy, Q8X q8, int rows, cudaStream_t s);
+void set_rmsnorm_smem_limit(int bytes);
 // Q8_0 quantization of f32 rows into Q8X (blocks.rs:102-123).
 void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s);
 // Q8_0 quantization into the reference's 34-byte BlockQ8_0 layout.
@@ -102,12 +103,20 @@ struct AttnArgs {
     int rows, dim, num_heads, num_kv_heads, head_dim, kv_dim;
     int max_len;             // upper bound of pos+1 over rows (grid sizing)
     float scale;             // 1/sqrt(head_dim) computed on the host
+    Q8X q8_out;              // fused path: also quantize `out` (qs == null: no)
+    bool write_probs;        // fused path: also store the probabilities in att
 };
 void launch_attention(const AttnArgs &a, cudaStream_t s);
 // the three phases of launch_attention, for callers that time them apart
 void launch_attn_scores(const AttnArgs &a, cudaStream_t s);
 void launch_attn_softmax(const AttnArgs &a, cudaStream_t s);
 void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
+// Two-kernel path with cp.async-staged K and V tiles (tiled scores, then
+// softmax + PV per (row, KV head)); same results as the three-phase path.
+// attention_fused_ok() says whether shapes and alignments allow it
+// (head_dim % 4, kv_mul <= 8, 16-byte bases, scores fit in shared memory).
+bool attention_fused_ok(const AttnArgs &a);
+void launch_attn_fused(const AttnArgs &a, cudaStream_t s);
 // Opt the attention kernels into `bytes` of dynamic shared memory (current device).
 void set_attention_smem_limit(int bytes);
 

@@ -8,12 +8,15 @@
 // The batched form (gemm_q4_0, kernels.rs:308-394) is the same dot per
 // (r, b), so a GEMM equals repeated GEMVs bit for bit.
 //
-// Mapping: a warp owns RPT row tiles (32 rows each, one row per lane per
-// tile) and BT activation rows, so every lane keeps RPT*BT*8 accumulators in
-// registers while it walks the blocks of its rows in order.  Weights come
-// from the repacked 576-byte tiles with one coalesced 128-bit load per lane
-// and block; the activation rows of the CTA's batch tile are staged in shared
-// memory in chunks of JC blocks and read as warp-wide broadcasts.
+// Mapping: one warp per (32-row weight tile, tile of BT activation rows);
+// lane = row.  Every lane keeps RPT*BT*8 accumulators in registers while it
+// walks the blocks of its row in order (the order is what the numerics fix;
+// the parallelism comes from rows x activation rows).  Weights come from the
+// repacked 576-byte tiles -- one coalesced 128-bit load per lane and block,
+// PF blocks in flight; the four warps of a CTA work on four row tiles of the
+// same activation tile, which cp.async stages in shared memory in chunks of
+// JC blocks and the warps read as broadcasts.  BT is chosen per launch so that
+// (tiles x activation tiles) gives the SMs enough warps to hide latency.
 //
 // The int dot of a lane is one dp4a of the unsigned weight nibbles against
 // the activation bytes, seeded with c_k = 0x4B400000 - 8*sum(a): the result
@@ -25,37 +28,44 @@ namespace slm {
 
 namespace {
 
-constexpr int RPT = 2;   // row tiles per warp
-constexpr int JC = 64;   // blocks per shared-memory chunk
+struct WBlock {
+    uint4 q;
+    unsigned short d;
+};
+
+__device__ __forceinline__ WBlock load_wblock(const uint8_t *w, int tile, int nb, int j, int lane) {
+    const uint8_t *tp = w + tile_offset((size_t)tile, nb, j);
+    WBlock b;
+    b.q = __ldg(reinterpret_cast<const uint4 *>(tp) + lane);
+    b.d = __ldg(reinterpret_cast<const unsigned short *>(tp + 512) + lane);
+    return b;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc));
+}
+
+constexpr int JC = 64;   // activation blocks per shared-memory chunk (multiple of PF)
+constexpr int PF = 4;    // weight blocks in flight per lane
 
 template <int BT, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, int units) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     extern __shared__ __align__(16) unsigned char smem[];
-    int8_t *s_qs = (int8_t *)smem;                            // [BT][JC][32]
-    int32_t *s_c = (int32_t *)(smem + BT * JC * 32);          // [BT][JC][8]
-    float *s_d = (float *)(smem + BT * JC * 64);              // [BT][JC]
+    int8_t *s_qs = (int8_t *)smem;                    // [BT][JC][32]
+    int32_t *s_c = (int32_t *)(smem + BT * JC * 32);  // [BT][JC][8]
+    float *s_d = (float *)(smem + BT * JC * 64);      // [BT][JC]
 
     const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int nwarps = blockDim.x >> 5;
-    const int nb = a.nb;
-    const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
+    const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const bool live = unit < units;  // warp-uniform; idle warps still help staging
     const int b0 = blockIdx.y * BT;
+    const int nb = a.nb;
 
-    // which row tiles this warp owns
-    const int unit = blockIdx.x * nwarps + warp;
     int tile[RPT];
-    if (EPI == EPI_SWIGLU_Q8) {
-        const int half_tiles = total_tiles / 2;
-        tile[0] = unit < half_tiles ? unit : -1;
-        tile[1] = unit < half_tiles ? unit + half_tiles : -1;
-    } else {
-#pragma unroll
-        for (int t = 0; t < RPT; t++) {
-            int ti = unit * RPT + t;
-            tile[t] = ti < total_tiles ? ti : -1;
-        }
-    }
+    tile[0] = live ? unit : 0;
+    if (RPT == 2) tile[RPT - 1] = tile[0] + total_tiles / 2;
 
     float acc[RPT][BT][8];
 #pragma unroll
@@ -65,83 +75,92 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
 #pragma unroll
             for (int k = 0; k < 8; k++) acc[t][b][k] = 0.0f;
 
+    // weight blocks j..j+PF-1 are in flight while block j is consumed
+    WBlock ring[RPT][PF];
+    if (live) {
+#pragma unroll
+        for (int t = 0; t < RPT; t++)
+#pragma unroll
+            for (int u = 0; u < PF; u++)
+                if (u < nb) ring[t][u] = load_wblock(a.w, tile[t], nb, u, lane);
+    }
+
     for (int jc = 0; jc < nb; jc += JC) {
         const int jn = nb - jc < JC ? nb - jc : JC;
-        __syncthreads();
-        // stage activations [b0, b0+BT) x blocks [jc, jc+jn)
+        __syncthreads();  // the previous chunk has been consumed
+        // stage the Q8X blocks [jc, jc+jn) of activation rows [b0, b0+BT):
+        // 16-byte pieces 0,1 = int8 values, 2,3 = lane constants
         for (int i = threadIdx.x; i < BT * jn * 4; i += blockDim.x) {
-            int b = i / (jn * 4), rem = i % (jn * 4);
-            int jl = rem >> 2, part = rem & 3;  // part 0,1: qs halves; 2,3: c halves
-            int bb = b0 + b;
-            int4 v = make_int4(0, 0, 0, 0);
+            const int b = i / (jn * 4), rem = i - b * (jn * 4);
+            const int jl = rem >> 2, part = rem & 3;
+            const int bb = b0 + b;
+            void *dst = part < 2 ? (void *)(s_qs + (b * JC + jl) * 32 + part * 16)
+                                 : (void *)(s_c + (b * JC + jl) * 8 + (part - 2) * 4);
             if (bb < a.batch) {
-                size_t blk = (size_t)bb * nb + jc + jl;
-                if (part < 2)
-                    v = reinterpret_cast<const int4 *>(a.x.qs + blk * 32)[part];
-                else
-                    v = reinterpret_cast<const int4 *>(a.x.c + blk * 8)[part - 2];
-            } else if (part >= 2) {
-                v = make_int4(MAGIC_I, MAGIC_I, MAGIC_I, MAGIC_I);
+                const size_t blk = (size_t)bb * nb + jc + jl;
+                const void *src = part < 2 ? (const void *)(a.x.qs + blk * 32 + part * 16)
+                                           : (const void *)(a.x.c + blk * 8 + (part - 2) * 4);
+                cp_async16(dst, src);
+            } else {
+                const int fill = part < 2 ? 0 : MAGIC_I;
+                *reinterpret_cast<int4 *>(dst) = make_int4(fill, fill, fill, fill);
             }
-            if (part < 2)
-                reinterpret_cast<int4 *>(s_qs + (b * JC + jl) * 32)[part] = v;
-            else
-                reinterpret_cast<int4 *>(s_c + (b * JC + jl) * 8)[part - 2] = v;
         }
+        asm volatile("cp.async.commit_group;\n" ::);
         for (int i = threadIdx.x; i < BT * jn; i += blockDim.x) {
-            int b = i / jn, jl = i % jn;
-            int bb = b0 + b;
+            const int b = i / jn, jl = i - b * jn;
+            const int bb = b0 + b;
             s_d[b * JC + jl] = bb < a.batch ? a.x.d[(size_t)bb * nb + jc + jl] : 0.0f;
         }
+        asm volatile("cp.async.wait_group 0;\n" ::);
         __syncthreads();
+        if (!live) continue;
 
-#pragma unroll 2
-        for (int jl = 0; jl < jn; jl++) {
-            const int j = jc + jl;
-            unsigned lo[RPT][4], hi[RPT][4];
-            float dw[RPT];
+        for (int jl0 = 0; jl0 < jn; jl0 += PF) {
 #pragma unroll
-            for (int t = 0; t < RPT; t++) {
-                if (tile[t] >= 0) {
-                    const uint8_t *tp = a.w + tile_offset((size_t)tile[t], nb, j);
-                    uint4 q = __ldg(reinterpret_cast<const uint4 *>(tp) + lane);
-                    unsigned short hb = __ldg(reinterpret_cast<const unsigned short *>(tp + 512) + lane);
-                    dw[t] = __half2float(__ushort_as_half(hb));
-                    unsigned qw[4] = {q.x, q.y, q.z, q.w};
+            for (int u = 0; u < PF; u++) {
+                const int jl = jl0 + u;
+                const int j = jc + jl;
+                if (jl >= jn) break;  // warp-uniform (last chunk only)
+                unsigned lo[RPT][4], hi[RPT][4];
+                float dw[RPT];
+#pragma unroll
+                for (int t = 0; t < RPT; t++) {
+                    const WBlock cur = ring[t][u];
+                    if (j + PF < nb) ring[t][u] = load_wblock(a.w, tile[t], nb, j + PF, lane);
+                    dw[t] = __half2float(__ushort_as_half(cur.d));
+                    const unsigned qw[4] = {cur.q.x, cur.q.y, cur.q.z, cur.q.w};
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         lo[t][k] = qw[k] & 0x0F0F0F0Fu;
                         hi[t][k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
                     }
-                } else {
-                    dw[t] = 0.0f;
-#pragma unroll
-                    for (int k = 0; k < 4; k++) lo[t][k] = hi[t][k] = 0u;
                 }
-            }
 #pragma unroll
-            for (int b = 0; b < BT; b++) {
-                const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[0];
-                const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[1];
-                const int4 c0 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[0];
-                const int4 c1 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[1];
-                const float da = s_d[b * JC + jl];
-                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                for (int b = 0; b < BT; b++) {
+                    const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[0];
+                    const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[1];
+                    const int4 c0 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[0];
+                    const int4 c1 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[1];
+                    const float da = s_d[b * JC + jl];
+                    const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-                for (int t = 0; t < RPT; t++) {
-                    const float d = __fmul_rn(dw[t], da);
+                    for (int t = 0; t < RPT; t++) {
+                        const float d = __fmul_rn(dw[t], da);
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
-                        acc[t][b][k] = __fmaf_rn(d, f0, acc[t][b][k]);
-                        float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
-                        acc[t][b][4 + k] = __fmaf_rn(d, f1, acc[t][b][4 + k]);
+                        for (int k = 0; k < 4; k++) {
+                            float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
+                            acc[t][b][k] = __fmaf_rn(d, f0, acc[t][b][k]);
+                            float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
+                            acc[t][b][4 + k] = __fmaf_rn(d, f1, acc[t][b][4 + k]);
+                        }
                     }
                 }
             }
         }
     }
+    if (!live) return;
 
     // ---- epilogue
     float y[RPT][BT];
@@ -157,35 +176,31 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
         }
 
     if constexpr (EPI == EPI_SWIGLU_Q8) {
-        if (tile[0] < 0) return;  // warp-uniform
         const int hdim = (total_tiles / 2) * TILE_ROWS;
         const int nb_out = hdim / 32;
+        const int hrow = tile[0] * TILE_ROWS + lane;
 #pragma unroll
         for (int b = 0; b < BT; b++) {
             const int bb = b0 + b;
             if (bb >= a.batch) break;  // warp-uniform
-            const int hrow = tile[0] * TILE_ROWS + lane;
-            float o = swiglu1(y[0][b], y[1][b]);
+            float o = swiglu1(y[0][b], y[RPT - 1][b]);
             if (a.out) a.out[(size_t)bb * a.ld_out + hrow] = o;
             q8x_store_block(o, a.q8_out, (size_t)bb * nb_out + tile[0], lane);
         }
     } else {
-#pragma unroll
-    for (int t = 0; t < RPT; t++) {
-        if (tile[t] < 0) continue;  // warp-uniform
-        const int row = tile[t] * TILE_ROWS + lane;
+        const int row = tile[0] * TILE_ROWS + lane;
 #pragma unroll
         for (int b = 0; b < BT; b++) {
             const int bb = b0 + b;
             if (bb >= a.batch) break;  // warp-uniform
-            const float v = y[t][b];
-            if (EPI == EPI_STORE) {
+            const float v = y[0][b];
+            if constexpr (EPI == EPI_STORE) {
                 if (row < a.rows) a.out[(size_t)bb * a.ld_out + row] = v;
-            } else if (EPI == EPI_RESIDUAL) {
+            } else if constexpr (EPI == EPI_RESIDUAL) {
                 if (row < a.rows)
                     a.out[(size_t)bb * a.ld_out + row] =
                         __fadd_rn(a.res[(size_t)bb * a.ld_res + row], v);
-            } else if (EPI == EPI_QKV) {
+            } else if constexpr (EPI == EPI_QKV) {
                 const QkvArgs &q = a.qkv;
                 // RoPE pairs (2j, 2j+1) sit in lanes (2j, 2j+1) of the same tile
                 const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
@@ -220,30 +235,29 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
             }
         }
     }
-    }
 }
 
+constexpr int TARGET_WARPS = 148 * 8;
+
 template <int BT, int EPI>
-void launch_bt(const GemvArgs &a, cudaStream_t s) {
-    int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
-    int units = EPI == EPI_SWIGLU_Q8 ? total_tiles / 2 : (total_tiles + RPT - 1) / RPT;
-    int btiles = (a.batch + BT - 1) / BT;
-    // enough CTAs to cover the SMs: shrink the CTA when there are few units
-    int nw = 4;
-    while (nw > 1 && (long)((units + nw - 1) / nw) * btiles < 2 * 148) nw >>= 1;
-    dim3 grid((units + nw - 1) / nw, btiles);
-    size_t smem = (size_t)BT * JC * 68;
-    gemv_kernel<BT, EPI><<<grid, 32 * nw, smem, s>>>(a);
+void launch_bt(const GemvArgs &a, int total_tiles, int units, cudaStream_t s) {
+    const int nbt = (a.batch + BT - 1) / BT;
+    dim3 grid((unsigned)((units + 3) / 4), (unsigned)nbt);
+    gemv_kernel<BT, EPI><<<grid, 128, (size_t)BT * JC * 68, s>>>(a, total_tiles, units);
 }
 
 template <int EPI>
 void launch_epi(const GemvArgs &a, cudaStream_t s) {
-    if (a.batch <= 1)
-        launch_bt<1, EPI>(a, s);
-    else if (a.batch == 2)
-        launch_bt<2, EPI>(a, s);
+    const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
+    const int units = EPI == EPI_SWIGLU_Q8 ? total_tiles / 2 : total_tiles;
+    // the widest activation tile (<= 4) that still leaves enough warps
+    auto warps = [&](int bt) { return (long)units * ((a.batch + bt - 1) / bt); };
+    if (a.batch >= 4 && warps(4) >= TARGET_WARPS)
+        launch_bt<4, EPI>(a, total_tiles, units, s);
+    else if (a.batch >= 2 && warps(2) >= TARGET_WARPS)
+        launch_bt<2, EPI>(a, total_tiles, units, s);
     else
-        launch_bt<4, EPI>(a, s);
+        launch_bt<1, EPI>(a, total_tiles, units, s);
 }
 
 }  // namespace

@@ -453,6 +453,7 @@ SLM_EXPORT int slm_causal_attention(const float *q, const float *k, const float 
     a.pos_const = (int)pos;
     a.att = att;
     a.att_ld = cfg->max_seq_len;
+    a.write_probs = true;
     a.out = out;
     a.ldo = cfg->dim;
     a.rows = 1;
@@ -507,6 +508,7 @@ struct slm_model {
     int32_t *h_io = nullptr;  // pinned staging: tok | pos | slot | next, R each
     std::map<std::tuple<int, int>, cudaGraphExec_t> graphs;
     bool use_graphs = true;
+    bool use_fused_attention = true;
 };
 
 namespace {
@@ -611,6 +613,12 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
     aa.max_len = max_len;
 
     Q8X qa8 = q8view(m->q8a, m->q8_blocks), qb8 = q8view(m->q8b, m->q8_blocks);
+    const bool fused = m->use_fused_attention && attention_fused_ok(aa);
+    if (fused) {
+        aa.write_probs = false;  // probabilities stay in shared memory
+        const int kv_mul = (int)(c.num_heads / c.num_kv_heads);
+        if ((kv_mul * m->hd) % 32 == 0) aa.q8_out = qb8;
+    }
     for (int l = 0; l < m->L; l++) {
         const LayerDev &ld = m->layers[l];
         // rmsnorm(x) -> Q8 (transformer.rs:411, kernels.rs:301)
@@ -630,15 +638,25 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
         mark(prof, SLM_PHASE_QKV);
         // attention (transformer.rs:430-443)
         aa.layer_off = (size_t)l * m->layer_stride;
-        launch_attn_scores(aa, st);
-        mark(prof, SLM_PHASE_ATTN_SCORES);
-        launch_attn_softmax(aa, st);
-        mark(prof, SLM_PHASE_ATTN_SOFTMAX);
-        launch_attn_pv(aa, st);
-        mark(prof, SLM_PHASE_ATTN_PV);
+        if (fused) {
+            // scores, softmax, PV and the Q8_0 of the output in one kernel
+            launch_attn_fused(aa, st);
+            mark(prof, SLM_PHASE_ATTN_FUSED);
+            if (!aa.q8_out.qs) {
+                launch_quantize_q8x(m->xb, d, d, qb8, n, st);
+                mark(prof, SLM_PHASE_QUANTIZE);
+            }
+        } else {
+            launch_attn_scores(aa, st);
+            mark(prof, SLM_PHASE_ATTN_SCORES);
+            launch_attn_softmax(aa, st);
+            mark(prof, SLM_PHASE_ATTN_SOFTMAX);
+            launch_attn_pv(aa, st);
+            mark(prof, SLM_PHASE_ATTN_PV);
+            launch_quantize_q8x(m->xb, d, d, qb8, n, st);
+            mark(prof, SLM_PHASE_QUANTIZE);
+        }
         // Wo + residual (transformer.rs:445-446)
-        launch_quantize_q8x(m->xb, d, d, qb8, n, st);
-        mark(prof, SLM_PHASE_QUANTIZE);
         g = GemvArgs{};
         g.w = ld.wo.tiles;
         g.rows = d;
@@ -702,7 +720,17 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
 }
 
 // kernel launches of one decode step (enqueue_forward + the greedy advance)
-uint32_t decode_launches(const slm_model *m) { return 1u + 10u * (uint32_t)m->L + 4u + 1u; }
+uint32_t decode_launches(const slm_model *m) {
+    // embed; per layer: rmsnorm, qkv, attention (1 fused, +1 quantize unless
+    // fused into it; or 3 + quantize), wo, rmsnorm, gate/up, down; final
+    // rmsnorm, lm_head, argmax; advance
+    uint32_t attn = 4;
+    if (m->use_fused_attention) {
+        const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
+        attn = ((kv_mul * m->hd) % 32 == 0) ? 1 : 2;
+    }
+    return 1u + (6u + attn) * (uint32_t)m->L + 3u + 1u;
+}
 
 int len_bucket(const slm_model *m, int max_len) {
     int b = (max_len + 255) / 256 * 256;
@@ -771,6 +799,7 @@ void ensure_kernel_attributes() {
     cudaGetDevice(&dev);
     if (dev < 31 && (done_mask & (1 << dev))) return;
     slm::set_attention_smem_limit(200 * 1024);
+    slm::set_rmsnorm_smem_limit(200 * 1024);
     if (dev < 31) done_mask |= 1 << dev;
 }
 }  // namespace
@@ -897,6 +926,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, cudaGetErrorString(e)));
     const char *env = getenv("SLM_DISABLE_GRAPHS");
     m->use_graphs = !(env && env[0] == '1');
+    env = getenv("SLM_ATTENTION_3PASS");
+    m->use_fused_attention = !(env && env[0] == '1');
     *out = m;
     return SLM_OK;
 }

@@ -114,7 +114,7 @@ SIGNATURES = {
 
 PHASES = ["embed", "rmsnorm_q8", "qkv_gemv_rope", "attn_scores", "attn_softmax", "attn_pv",
           "quantize_q8", "wo_gemv_residual", "gate_up_gemv_swiglu", "down_gemv_residual",
-          "lm_head_gemv", "argmax", "advance"]
+          "lm_head_gemv", "argmax", "advance", "attn_fused"]
 
 
 class _Lib:

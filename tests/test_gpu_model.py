@@ -144,6 +144,26 @@ def test_graphs_and_eager_agree(cuda):
     assert np.array_equal(e.logits(1), g.logits(1))
 
 
+def test_fused_and_three_pass_attention_agree(cuda):
+    cfg, layers, vocab = synth.config("cfg2")
+    w = synth.synth_model(cfg, layers, vocab, seed=5)
+    os.environ["SLM_ATTENTION_3PASS"] = "1"
+    try:
+        three = S.Model(cfg, w, max_sequences=2, max_rows=32)
+    finally:
+        del os.environ["SLM_ATTENTION_3PASS"]
+    fused = S.Model(cfg, w, max_sequences=2, max_rows=32)
+    for m in (three, fused):
+        m.prefill_tokens(list(range(3, 30)), seq=0)
+        m.prefill_tokens([5, 6, 7], seq=1)
+    a = three.decode_batch([0, 1], [9, 10], [27, 3])
+    b = fused.decode_batch([0, 1], [9, 10], [27, 3])
+    assert list(a) == list(b)
+    for r in range(2):
+        assert np.array_equal(three.logits(r), fused.logits(r))
+    assert fused.launches_per_decode_step < three.launches_per_decode_step
+
+
 def test_cfg3_shape_prefilled_kv_decode(cuda):
     """SmolLM2-135M shape, KV rows 0..2047 from seeded N(0,1), two sequences,
     two decode steps at positions 2048 and 2049: logits bit-exact."""

@@ -61,15 +61,15 @@ def test_quantize_row_q8_0_bit_exact(cuda):
 
 def one_block_q4(d, byte):
     b = np.zeros(18, np.uint8)
-    b[0:2] = np.float16(d).view(np.uint8)
+    b[0:2] = np.array([d], np.float16).view(np.uint8)
     b[2:] = byte
     return b
 
 
 def one_block_q8(d, val):
     b = np.zeros(34, np.uint8)
-    b[0:2] = np.float16(d).view(np.uint8)
-    b[2:] = np.int8(val).view(np.uint8)
+    b[0:2] = np.array([d], np.float16).view(np.uint8)
+    b[2:] = np.array([val], np.int8).view(np.uint8)
     return b
 
 
