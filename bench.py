@@ -421,7 +421,7 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * GLOBAL_BATCH,
                 "d2h_bytes_per_step": 4 * GLOBAL_BATCH,
                 "api": "slm_model_decode_batch (host token/position arrays in, next tokens out)"},
-        "gpu_launches": model.launches_per_decode_step * K,
+        "gpu_launches": model.launches_per_decode_step(B) * K,
         "clocks": clk,
         "setup_s": round(setup_s, 1),
     }

@@ -212,7 +212,8 @@ int slm_model_decode_batch(slm_model *m, uint32_t n, const uint32_t *seqs,
  * step s feeds each row's argmax back as its next token at pos+1.
  * seqs/tokens/pos are device arrays of n entries (tokens and pos advance in
  * place); out_dev receives steps*n token ids (step-major).  Enqueued on the
- * model stream; captured in CUDA graphs. */
+ * model stream; captured in CUDA graphs.  The n sequences must be distinct
+ * (with 16 or more rows, two halves of the batch run concurrently). */
 int slm_model_decode_steps_device(slm_model *m, uint32_t n, const uint32_t *seqs_dev,
                                   int32_t *tokens_dev, uint32_t *pos_dev, uint32_t steps,
                                   int32_t *out_dev, uint32_t max_pos_hint);
@@ -259,8 +260,9 @@ enum {
 int slm_model_profile_decode(slm_model *m, uint32_t n, const uint32_t *seqs_dev,
                              int32_t *tokens_dev, uint32_t *pos_dev, uint32_t steps,
                              uint32_t max_pos_hint, float *phase_ms);
-/* Kernel launches one decode step issues (graph nodes of a decode step). */
-uint32_t slm_model_launches_per_decode_step(const slm_model *m);
+/* Kernel launches one decode step of n rows issues (the kernel nodes of its
+ * graph, the greedy advance included). */
+uint32_t slm_model_launches_per_decode_step(const slm_model *m, uint32_t n);
 
 #ifdef __cplusplus
 }

@@ -68,15 +68,24 @@ __device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
 // ---------------------------------------------------------------------------
 // Cranelift float semantics used by the JIT vector ops (src/jit/lower.rs).
 // ---------------------------------------------------------------------------
+// fmax/fmin: NaN when either input is NaN (as a + b), +0 over -0 for max and
+// -0 over +0 for min, else the larger / smaller.  Written as selects: the
+// early-return form compiles to branches that cost ~70 cycles per call.
+// For a == b the two bit patterns differ at most in the sign of a zero, so
+// AND (max) / OR (min) of the bits picks the right zero.
 __device__ __forceinline__ float cl_fmax(float a, float b) {
-    if (a != a || b != b) return __fadd_rn(a, b);
-    if (a == b) return signbit(a) ? b : a;
-    return a > b ? a : b;
+    const float nan = __fadd_rn(a, b);
+    const float eq = __int_as_float(__float_as_int(a) & __float_as_int(b));
+    float r = a > b ? a : b;
+    r = a == b ? eq : r;
+    return (a != a || b != b) ? nan : r;
 }
 __device__ __forceinline__ float cl_fmin(float a, float b) {
-    if (a != a || b != b) return __fadd_rn(a, b);
-    if (a == b) return signbit(a) ? a : b;
-    return a < b ? a : b;
+    const float nan = __fadd_rn(a, b);
+    const float eq = __int_as_float(__float_as_int(a) | __float_as_int(b));
+    float r = a < b ? a : b;
+    r = a == b ? eq : r;
+    return (a != a || b != b) ? nan : r;
 }
 
 // The reference's polynomial exp (src/jit/lower.rs:22-65): clamp to
@@ -84,7 +93,10 @@ __device__ __forceinline__ float cl_fmin(float a, float b) {
 // degree-5 Horner polynomial with separately rounded mul/add, times 2^n built
 // from exponent bits.
 __device__ __forceinline__ float exp_poly(float x) {
-    float xc = cl_fmin(cl_fmax(x, -87.3f), 88.3f);
+    // cl_fmin(cl_fmax(x, -87.3), 88.3) for constant, non-zero bounds
+    float xc = x > -87.3f ? x : -87.3f;
+    xc = xc < 88.3f ? xc : 88.3f;
+    xc = x != x ? __fadd_rn(__fadd_rn(x, -87.3f), 88.3f) : xc;
     float fx = __fmul_rn(xc, 1.44269504088896340736f);
     float n = rintf(fx);
     float n_hi = __fmul_rn(n, 0.69314575f);

@@ -1,6 +1,7 @@
 // kernels.h -- launchers of the sm_100a kernels (internal to libslm_b200).
 #pragma once
 
+#include <cuda.h>  // CUtensorMap
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -86,6 +87,8 @@ struct GemvArgs {
     QkvArgs qkv;
 };
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
+// Opt the GEMV kernels into `bytes` of dynamic shared memory (current device).
+void set_gemv_smem_limit(int bytes);
 
 // ---- attention (kernels_attn.cu)
 struct AttnArgs {
@@ -105,18 +108,29 @@ struct AttnArgs {
     float scale;             // 1/sqrt(head_dim) computed on the host
     Q8X q8_out;              // fused path: also quantize `out` (qs == null: no)
     bool write_probs;        // fused path: also store the probabilities in att
+    int32_t *err;            // set to 3 when a bounded wait gave up (may be null)
+    // fused path: V plane of row r in the tensor map = slot*z_slot + z_layer
+    long long z_slot, z_layer;
 };
-void launch_attention(const AttnArgs &a, cudaStream_t s);
+// vmap: the V tensor map of encode_v_map, or null for the three-phase path
+void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, cudaStream_t s);
 // the three phases of launch_attention, for callers that time them apart
 void launch_attn_scores(const AttnArgs &a, cudaStream_t s);
 void launch_attn_softmax(const AttnArgs &a, cudaStream_t s);
 void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
-// Two-kernel path with cp.async-staged K and V tiles (tiled scores, then
-// softmax + PV per (row, KV head)); same results as the three-phase path.
+// Two-kernel path (tiled scores, then softmax + PV per (row, KV head) with V
+// tiles through the TMA engine); same results as the three-phase path.
 // attention_fused_ok() says whether shapes and alignments allow it
-// (head_dim % 4, kv_mul <= 8, 16-byte bases, scores fit in shared memory).
+// (head_dim % 4 and <= 224, kv_mul <= 8, 16-byte bases, scores fit in
+// shared memory).
 bool attention_fused_ok(const AttnArgs &a);
-void launch_attn_fused(const AttnArgs &a, cudaStream_t s);
+void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s);
+// 3-D tensor map over `planes` consecutive [max_seq][kv_dim] f32 planes from
+// `base`, box = head_dim floats x 64 positions x 1 plane.  False when the
+// driver entry point is missing or the shape is not expressible (the caller
+// then uses the three-phase path).
+bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
+                  uint64_t planes, int head_dim);
 // Opt the attention kernels into `bytes` of dynamic shared memory (current device).
 void set_attention_smem_limit(int bytes);
 

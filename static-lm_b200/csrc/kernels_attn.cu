@@ -10,15 +10,21 @@
 //   1/sum                                          (graph.rs:168-179)
 //   out_i = sum_t p_t*v_t,i, sequential in t starting from 0.0
 //
-// The only freedom the numerics leave is which thread runs which chain, so
-// the work is split into three launches that each expose the parallelism of
-// their phase:
+// The only freedom the numerics leave is which thread runs which chain.
+// Two paths give identical results:
+//   fused (two launches): (A) tiled scores, K rows through the TMA engine,
+//            one thread per key running the kv_mul head chains; (B) per
+//            (row, KV head): softmax in shared memory, then PV with V tiles
+//            streamed by a 3-D tensor map into an mbarrier-guarded ring
+//   three-phase fallback (any shape):
 //   scores : one thread per (row, key position), kv_mul query heads per
 //            thread so every K row is loaded once per KV head group
 //   softmax: one CTA per (row, head); max in parallel, exp in parallel, the
 //            four lane chains on four threads over a shared-memory copy
 //   pv     : one thread per (row, head, dim) chain over t; a warp covers 32
 //            consecutive dims so each V row segment is one coalesced load
+// Packed f32x2 arithmetic is not used: measured on B200 it does not round
+// like separate mul.rn / add.rn.
 // Decode is the case of one row per sequence; prefill is rows = tokens with
 // p = start_pos + i, which reproduces the reference's per-token loop
 // (transformer.rs:563-593) exactly.
@@ -203,53 +209,109 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+
+// Fused path: V comes through a 3-D tensor map over the cache planes
+// (x = kv_dim floats, y = positions, z = plane), one TMA box of TT_V rows x
+// head_dim floats per stage.
+constexpr int TT_V = 64;
+constexpr int PV_THREADS = 256;
+
 struct FusedShape {
-    int tt;      // key rows per stage
+    int tt;      // V rows per stage (one TMA box)
     int lp;      // scores row stride (floats)
-    int rs;      // ring row stride (floats)
-    size_t smem; // bytes
+    size_t smem; // dynamic shared memory bytes (with 128 B of alignment slack)
 };
 
-__host__ __device__ inline FusedShape fused_shape(int kv_mul, int hd, int max_len, int tt) {
+__host__ __device__ inline FusedShape fused_shape(int kv_mul, int hd, int max_len) {
     FusedShape f;
-    f.tt = tt;
+    f.tt = TT_V;
     f.lp = (max_len + 31) / 32 * 32 + 4;
-    f.rs = hd + 4;
-    f.smem = sizeof(float) * ((size_t)kv_mul * f.lp + (size_t)FUSED_STAGES * tt * f.rs +
-                              (size_t)kv_mul * hd + 64);
+    f.smem = sizeof(float) * ((size_t)FUSED_STAGES * TT_V * hd + (size_t)kv_mul * f.lp +
+                              (size_t)kv_mul * hd + 64 + 8 * 32) +
+             128;
     return f;
 }
 
-// Copy `nrows` rows of hd floats (global stride ld floats) into shared
-// memory rows of stride rs with 16-byte cp.async, all threads of the CTA.
-// When the thread count is a multiple of the 16-byte chunks per row, each
-// thread keeps its column and walks rows without any division.
-__device__ __forceinline__ void stage_rows(float *dst, int rs, const float *src, size_t ld,
-                                           int nrows, int cpr, int tid, int nth) {
-    if (nth % cpr == 0) {
-        const int rstep = nth / cpr;
-        const int cc = tid % cpr;
-        for (int rr = tid / cpr; rr < nrows; rr += rstep)
-            cp_async16(dst + rr * rs + cc * 4, src + (size_t)rr * ld + cc * 4);
-    } else {
-        for (int c = tid; c < nrows * cpr; c += nth) {
-            const int rr = c / cpr, cc = c - rr * cpr;
-            cp_async16(dst + rr * rs + cc * 4, src + (size_t)rr * ld + cc * 4);
+// ---- mbarriers and bulk (TMA) copies, CTA scope ------------------------
+__device__ __forceinline__ unsigned smem_addr(const void *p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of `bar`, giving up after ~1 s (2e9 cycles) or as
+// soon as another thread of the CTA gave up (*abort set): on a timeout the
+// thread sets *abort and the kernel's error flag, and returns false.
+constexpr long long WAIT_LIMIT = 2000000000LL;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
+                                          int32_t *err) {
+    const long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - t0 > WAIT_LIMIT) {
+            *abort = 1;
+            if (err) atomicExch(err, 3);
+            return false;
         }
     }
+    return true;
+}
+// One row copy global -> shared through the TMA engine, completing bytes on bar.
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
 }
 
-// (A) scores: one CTA per (128 keys, KV head, row).  The 128 K rows are
-// copied with coalesced 16-byte cp.async into shared memory (rows padded to
-// hd+4 floats); thread t then runs the kv_mul query-head dot chains of key t
-// side by side (kv_mul-way ILP), each chain sequential in i.
+// One tile (box) of a 3-D tensor map global -> shared through the TMA
+// engine, completing its bytes on bar.  x is a multiple of 4 floats (16 B).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// (A) scores: one CTA per (128 keys, KV head, row).  The 128 K rows go
+// global -> shared through the TMA engine, one bulk copy per row (rows padded
+// to hd+4 floats), all completing on one mbarrier; thread t then runs the
+// kv_mul query-head dot chains of key t side by side (kv_mul-way ILP), each
+// chain sequential in i.
 constexpr int TILE_KEYS = 128;
 
 __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a) {
     extern __shared__ __align__(16) float smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int s_abort;
     const int r = blockIdx.z, g = blockIdx.y;
     const int kv_mul = a.num_heads / a.num_kv_heads;
-    const int hd = a.head_dim, rs = hd + 4, cpr = hd >> 2;
+    const int hd = a.head_dim, rs = hd + 4;
     const int L = row_len(a, r);
     const int t0 = blockIdx.x * TILE_KEYS;
     if (t0 >= L) return;  // CTA-uniform
@@ -258,12 +320,31 @@ __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a
     float *s_q = smem + TILE_KEYS * rs;         // [kv_mul][hd]
     const float *kb = a.k_base + row_slot(a, r) * a.slot_stride + a.layer_off +
                       (size_t)t0 * a.kv_dim + (size_t)g * hd;
-    stage_rows(s_k, rs, kb, (size_t)a.kv_dim, nrows, cpr, threadIdx.x, TILE_KEYS);
-    cp_async_commit();
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    // the K rows of this tile go through the TMA engine, one bulk copy per row
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar, (unsigned)nrows * (unsigned)hd * 4u);
+    if ((int)threadIdx.x < nrows)
+        bulk_copy(s_k + threadIdx.x * rs, kb + (size_t)threadIdx.x * a.kv_dim, (unsigned)hd * 4u, &bar);
     const float *qr = a.q + (size_t)r * a.ldq + (size_t)g * kv_mul * hd;
     for (int i = threadIdx.x; i < kv_mul * hd; i += TILE_KEYS) s_q[i] = qr[i];
-    cp_async_wait<0>();
+    const bool ok = mbar_wait(&bar, 0, &s_abort, a.err);
     __syncthreads();
+    if (!ok || s_abort) {
+        // bounded drain of the copies in flight before the shared memory goes away
+        if (threadIdx.x == 0) {
+            const long long tw = clock64();
+            while (!mbar_test(&bar, 0) && clock64() - tw < WAIT_LIMIT) {
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    const int cpr = hd >> 2;
     const int t = threadIdx.x;
     if (t >= nrows) return;
     const float4 *k4 = reinterpret_cast<const float4 *>(s_k + t * rs);
@@ -291,86 +372,149 @@ __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a
     }
 }
 
-// (B) softmax + PV: one CTA per (row, KV head).  The first V tiles are put
-// in flight through a multi-stage cp.async ring (rows padded to hd+4 floats)
-// before anything else; meanwhile the kv_mul score rows come from the scores
-// kernel's output into shared memory and the softmax runs there; then the PV
-// chains consume the V tiles, two dims per thread (two independent chains).
-// When q8_out is given, the output block that this CTA owns is quantized for
-// the Wo GEMV in the same kernel.
-__global__ void __launch_bounds__(1024) attn_softmax_pv_kernel(AttnArgs a, int tt, int lp) {
-    extern __shared__ __align__(16) float smem[];
+// (B) softmax + PV: one CTA per (row, KV head), warp-specialized.  One
+// producer thread owns every copy of V: each stage is one TMA box (TT_V
+// positions x head_dim floats of this KV head) of a 3-D tensor map over the
+// cache planes, landing densely in a ring of FUSED_STAGES stages guarded by
+// FULL/EMPTY mbarriers.  The first stages are issued before the softmax.  The
+// KVM score rows come from the scores kernel's output; the softmax runs in
+// shared memory with all warps; then consumer thread (head h, dims 2j, 2j+1)
+// runs its two chains side by side on float2 loads of V, each probability
+// load covering four positions.  When q8_out is
+// given, the output block this CTA owns is quantized for the Wo GEMV in the
+// same kernel.  Every mbarrier wait is bounded (mbar_wait).
+template <int KVM>
+__global__ void __launch_bounds__(1024)
+    attn_softmax_pv_kernel(AttnArgs a, int lp, const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar_full[FUSED_STAGES], bar_empty[FUSED_STAGES];
+    __shared__ int s_abort, s_issued;
+    // TMA destinations 128-byte aligned (the launch adds 128 B of slack)
+    float *smem = reinterpret_cast<float *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
+    constexpr int tt = TT_V;
+    const int nth = blockDim.x;
     const int g = blockIdx.x, r = blockIdx.y;
-    const int kv_mul = a.num_heads / a.num_kv_heads;
-    const int hd = a.head_dim, rs = hd + 4;
-    const int tid = threadIdx.x, nth = blockDim.x;
-    float *s_sc = smem;                          // [kv_mul][lp]
-    float *s_ring = s_sc + (size_t)kv_mul * lp;  // [STAGES][tt][rs]
-    float *s_out = s_ring + (size_t)FUSED_STAGES * tt * rs;  // [kv_mul*hd]
-    float *s_red = s_out + (size_t)kv_mul * hd;  // 64 floats
+    const int hd = a.head_dim;
+    const int tid = threadIdx.x;
+    float *s_ring = smem;                                   // [STAGES][tt][hd]
+    float *s_sc = s_ring + (size_t)FUSED_STAGES * tt * hd;  // [KVM][lp]
+    float *s_out = s_sc + (size_t)KVM * lp;                 // [KVM*hd]
+    float *s_red = s_out + (size_t)KVM * hd;                // 64 + 8*32 floats
     const int L = row_len(a, r);
     const int ntiles = (L + tt - 1) / tt;
-    const float *vb = a.v_base + row_slot(a, r) * a.slot_stride + a.layer_off + (size_t)g * hd;
-    const size_t ld = (size_t)a.kv_dim;
-    const int cpr = hd >> 2;
+    const int vx = g * hd;
+    const int vz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
+    const int n_pairs = KVM * (hd >> 1);     // consumer threads: (head, dim pair)
+    const int n_cons = (n_pairs + 31) >> 5;  // consumer warps
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nw = nth >> 5;
+    const bool producer = warp == n_cons;  // the launch has n_cons + 1 warps or more
+    const unsigned tile_bytes = (unsigned)tt * (unsigned)hd * 4u;
 
-    auto issue = [&](int tile) {
-        if (tile < ntiles) {
-            const int t0 = tile * tt;
-            const int nrows = L - t0 < tt ? L - t0 : tt;
-            stage_rows(s_ring + (size_t)(tile % FUSED_STAGES) * tt * rs, rs, vb + (size_t)t0 * ld,
-                       ld, nrows, cpr, tid, nth);
+    if (tid == 0) {
+        for (int st = 0; st < FUSED_STAGES; st++) {
+            mbar_init(&bar_full[st], 1);
+            mbar_init(&bar_empty[st], (unsigned)n_cons);
         }
-        cp_async_commit();
-    };
-#pragma unroll 1
-    for (int s = 0; s < FUSED_STAGES - 1; s++) issue(s);
+        s_abort = 0;
+        s_issued = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (producer && lane == 0) {
+        int k = 0;
+        for (; k < FUSED_STAGES && k < ntiles; k++) {
+            mbar_arrive_expect_tx(&bar_full[k], tile_bytes);
+            tma_load_3d(s_ring + (size_t)k * tt * hd, &vmap, vx, k * tt, vz, &bar_full[k]);
+        }
+        s_issued = k;
+    }
 
-    // scores of the kv_mul heads of this group
-    const float *att = a.att + ((size_t)r * a.num_heads + (size_t)g * kv_mul) * a.att_ld;
-    for (int h = 0; h < kv_mul; h++)
-        for (int t = tid; t < L; t += nth) s_sc[h * lp + t] = att[(size_t)h * a.att_ld + t];
+    // scores of the KVM heads of this group (cp.async, awaited before the softmax)
+    const float *att = a.att + ((size_t)r * a.num_heads + (size_t)g * KVM) * a.att_ld;
+    const bool vec = (a.att_ld & 3) == 0 && ((uintptr_t)att & 15) == 0;
+    if (vec) {
+        const int c4 = (L + 3) >> 2;
+        for (int h = 0; h < KVM; h++)
+            for (int c = tid; c < c4; c += nth)
+                cp_async16(s_sc + h * lp + 4 * c, att + (size_t)h * a.att_ld + 4 * c);
+    } else {
+        for (int h = 0; h < KVM; h++)
+            for (int t = tid; t < L; t += nth) s_sc[h * lp + t] = att[(size_t)h * a.att_ld + t];
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
 
     // ---- softmax per query head (graph.rs:168-179 order)
-    const int warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
-    for (int h = 0; h < kv_mul; h++) {
-        float m = -INFINITY;
-        for (int t = tid; t < L; t += nth) m = cl_fmax(m, s_sc[h * lp + t]);
-        for (int o = 16; o > 0; o >>= 1) m = cl_fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_red[warp] = m;
+    {
+        // maxima of all KVM heads with one pass and two barriers
+        float m[KVM];
+#pragma unroll
+        for (int h = 0; h < KVM; h++) m[h] = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < KVM; h++)
+            for (int t = tid; t < L; t += nth) m[h] = cl_fmax(m[h], s_sc[h * lp + t]);
+#pragma unroll
+        for (int h = 0; h < KVM; h++) {
+            for (int o = 16; o > 0; o >>= 1) m[h] = cl_fmax(m[h], __shfl_xor_sync(0xffffffffu, m[h], o));
+            if (lane == 0) s_red[64 + h * 32 + warp] = m[h];
+        }
         __syncthreads();
-        if (tid == 0) {
-            float mm = s_red[0];
-            for (int w = 1; w < nw; w++) mm = cl_fmax(mm, s_red[w]);
-            s_red[32 + h] = mm;
+        if (tid < KVM) {
+            float mm = s_red[64 + tid * 32];
+            for (int w = 1; w < nw; w++) mm = cl_fmax(mm, s_red[64 + tid * 32 + w]);
+            s_red[32 + tid] = mm;
         }
         __syncthreads();
     }
-    for (int h = 0; h < kv_mul; h++) {
+    // exp(s - max), four independent elements per iteration
+    for (int h = 0; h < KVM; h++) {
         const float mx = s_red[32 + h];
-        for (int t = tid; t < L; t += nth)
-            s_sc[h * lp + t] = exp_poly(__fsub_rn(s_sc[h * lp + t], mx));
+        float *row = s_sc + h * lp;
+        int t = tid;
+        for (; t + 3 * nth < L; t += 4 * nth) {
+            const float x0 = row[t], x1 = row[t + nth], x2 = row[t + 2 * nth], x3 = row[t + 3 * nth];
+            const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
+            const float e2 = exp_poly(__fsub_rn(x2, mx)), e3 = exp_poly(__fsub_rn(x3, mx));
+            row[t] = e0;
+            row[t + nth] = e1;
+            row[t + 2 * nth] = e2;
+            row[t + 3 * nth] = e3;
+        }
+        for (; t < L; t += nth) row[t] = exp_poly(__fsub_rn(row[t], mx));
     }
     __syncthreads();
+    // four lane chains per head over [0, L & ~3): the next 8 values are
+    // loaded before the current 8 are added
     const int vl = L & ~3;
-    if (tid < 4 * kv_mul) {
+    if (tid < 4 * KVM) {
         const int h = tid >> 2, l = tid & 3;
         const float *e = s_sc + h * lp;
         float acc = 0.0f;
         int i = l;
-        for (; i + 28 < vl; i += 32) {
-            float v[8];
+        float cur[8], nxt[8];
+        const int nfull = (vl - l + 3) / 4 / 8;  // full groups of 8 steps
+        if (nfull > 0) {
 #pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = e[i + 4 * u];
+            for (int u = 0; u < 8; u++) cur[u] = e[i + 4 * u];
+            for (int gi = 0; gi < nfull; gi++) {
+                if (gi + 1 < nfull) {
 #pragma unroll
-            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
+                    for (int u = 0; u < 8; u++) nxt[u] = e[i + 32 + 4 * u];
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, cur[u]);
+#pragma unroll
+                for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+                i += 32;
+            }
         }
         for (; i < vl; i += 4) acc = __fadd_rn(acc, e[i]);
-        s_red[tid] = acc;  // [0, 4*kv_mul) with kv_mul <= 8 stays below 32
+        s_red[tid] = acc;  // [0, 4*KVM) with KVM <= 8 stays below 32
     }
     __syncthreads();
-    if (tid < kv_mul) {
+    if (tid < KVM) {
         const float *e = s_sc + tid * lp;
         float sum = __fadd_rn(__fadd_rn(s_red[4 * tid], s_red[4 * tid + 1]),
                               __fadd_rn(s_red[4 * tid + 2], s_red[4 * tid + 3]));
@@ -378,108 +522,232 @@ __global__ void __launch_bounds__(1024) attn_softmax_pv_kernel(AttnArgs a, int t
         s_red[48 + tid] = __fdiv_rn(1.0f, sum);
     }
     __syncthreads();
-    for (int h = 0; h < kv_mul; h++) {
+    for (int h = 0; h < KVM; h++) {
         const float inv = s_red[48 + h];
+        float *row = s_sc + h * lp;
         float *prow = a.write_probs
-                          ? a.att + ((size_t)r * a.num_heads + g * kv_mul + h) * a.att_ld
+                          ? a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld
                           : nullptr;
-        for (int t = tid; t < L; t += nth) {
-            const float pr = __fmul_rn(s_sc[h * lp + t], inv);
-            s_sc[h * lp + t] = pr;
+        int t = tid;
+        for (; t + 3 * nth < L; t += 4 * nth) {
+            const float p0 = __fmul_rn(row[t], inv), p1 = __fmul_rn(row[t + nth], inv);
+            const float p2 = __fmul_rn(row[t + 2 * nth], inv), p3 = __fmul_rn(row[t + 3 * nth], inv);
+            row[t] = p0;
+            row[t + nth] = p1;
+            row[t + 2 * nth] = p2;
+            row[t + 3 * nth] = p3;
+            if (prow) {
+                prow[t] = p0;
+                prow[t + nth] = p1;
+                prow[t + 2 * nth] = p2;
+                prow[t + 3 * nth] = p3;
+            }
+        }
+        for (; t < L; t += nth) {
+            const float pr = __fmul_rn(row[t], inv);
+            row[t] = pr;
             if (prow) prow[t] = pr;
         }
     }
 
-    // ---- out = sum_t p_t * v_t (sequential in t from 0.0); thread = (head,
-    // pair of dims): two independent chains
-    const int half = hd >> 1;
-    const int hl = tid / half, i2 = tid - (tid / half) * half;
-    const bool active = tid < kv_mul * half;
-    float acc0 = 0.0f, acc1 = 0.0f;
+    // ---- out = sum_t p_t * v_t (sequential in t from 0.0)
+    __syncthreads();  // probabilities complete
+    if (producer) {
 #pragma unroll 1
-    for (int tile = 0; tile < ntiles; tile++) {
-        cp_async_wait<FUSED_STAGES - 2>();
-        __syncthreads();
-        issue(tile + FUSED_STAGES - 1);
+        for (int k = FUSED_STAGES; k < ntiles; k++) {
+            // the stage is free once every consumer warp released tile k - STAGES
+            if (!mbar_wait(&bar_empty[k % FUSED_STAGES], (unsigned)((k / FUSED_STAGES) - 1) & 1u,
+                           &s_abort, a.err))
+                break;
+            if (lane == 0) {
+                const int st = k % FUSED_STAGES;
+                mbar_arrive_expect_tx(&bar_full[st], tile_bytes);
+                tma_load_3d(s_ring + (size_t)st * tt * hd, &vmap, vx, k * tt, vz, &bar_full[st]);
+                s_issued = k + 1;
+            }
+            __syncwarp();
+        }
+    } else if (warp < n_cons) {
+        const bool active = tid < n_pairs;
+        const int hl = tid / (hd >> 1), j2 = 2 * (tid - hl * (hd >> 1));
+        float acc0 = 0.0f, acc1 = 0.0f;  // out[hl][j2], out[hl][j2 + 1]
+#pragma unroll 1
+        for (int k = 0; k < ntiles; k++) {
+            if (!mbar_wait(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u, &s_abort,
+                           a.err))
+                break;
+            if (active) {
+                const float2 *vt = reinterpret_cast<const float2 *>(
+                    s_ring + (size_t)(k % FUSED_STAGES) * tt * hd + j2);
+                const int hs = hd >> 1;  // row stride in float pairs
+                const float *pp = s_sc + hl * lp + k * tt;
+                const int nrows = L - k * tt < tt ? L - k * tt : tt;
+                if (nrows == tt) {
+                    // full tile: the loads of positions 4j+4..4j+7 are in
+                    // flight while positions 4j..4j+3 are added
+                    float4 pc = *reinterpret_cast<const float4 *>(pp);
+                    float2 vc[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) vc[u] = vt[u * hs];
+#pragma unroll
+                    for (int j = 0; j < tt / 4; j++) {
+                        float4 pn;
+                        float2 vn[4];
+                        if (j + 1 < tt / 4) {
+                            pn = *reinterpret_cast<const float4 *>(pp + 4 * j + 4);
+#pragma unroll
+                            for (int u = 0; u < 4; u++) vn[u] = vt[(4 * j + 4 + u) * hs];
+                        }
+                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.x, vc[0].x));
+                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.x, vc[0].y));
+                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.y, vc[1].x));
+                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.y, vc[1].y));
+                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.z, vc[2].x));
+                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.z, vc[2].y));
+                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.w, vc[3].x));
+                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.w, vc[3].y));
+                        if (j + 1 < tt / 4) {
+                            pc = pn;
+#pragma unroll
+                            for (int u = 0; u < 4; u++) vc[u] = vn[u];
+                        }
+                    }
+                } else {
+                    for (int tl = 0; tl < nrows; tl++) {
+                        const float pr = pp[tl];
+                        const float2 vv = vt[tl * hs];
+                        acc0 = __fadd_rn(acc0, __fmul_rn(pr, vv.x));
+                        acc1 = __fadd_rn(acc1, __fmul_rn(pr, vv.y));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[k % FUSED_STAGES]);
+        }
         if (active) {
-            const float *vt = s_ring + (size_t)(tile % FUSED_STAGES) * tt * rs + 2 * i2;
-            const float *pp = s_sc + hl * lp + tile * tt;
-            const int t0 = tile * tt;
-            const int nrows = L - t0 < tt ? L - t0 : tt;
-            int tl = 0;
-            for (; tl + 4 <= nrows; tl += 4) {
-                const float4 p4 = *reinterpret_cast<const float4 *>(pp + tl);
-                const float2 v0 = *reinterpret_cast<const float2 *>(vt + (tl + 0) * rs);
-                const float2 v1 = *reinterpret_cast<const float2 *>(vt + (tl + 1) * rs);
-                const float2 v2 = *reinterpret_cast<const float2 *>(vt + (tl + 2) * rs);
-                const float2 v3 = *reinterpret_cast<const float2 *>(vt + (tl + 3) * rs);
-                acc0 = __fadd_rn(acc0, __fmul_rn(p4.x, v0.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(p4.x, v0.y));
-                acc0 = __fadd_rn(acc0, __fmul_rn(p4.y, v1.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(p4.y, v1.y));
-                acc0 = __fadd_rn(acc0, __fmul_rn(p4.z, v2.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(p4.z, v2.y));
-                acc0 = __fadd_rn(acc0, __fmul_rn(p4.w, v3.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(p4.w, v3.y));
-            }
-            for (; tl < nrows; tl++) {
-                const float2 vv = *reinterpret_cast<const float2 *>(vt + tl * rs);
-                acc0 = __fadd_rn(acc0, __fmul_rn(pp[tl], vv.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(pp[tl], vv.y));
-            }
+            s_out[hl * hd + j2] = acc0;
+            s_out[hl * hd + j2 + 1] = acc1;
         }
     }
-    cp_async_wait<0>();
-    if (active) {
-        s_out[hl * hd + 2 * i2] = acc0;
-        s_out[hl * hd + 2 * i2 + 1] = acc1;
-    }
     __syncthreads();
-    float *orow = a.out + (size_t)r * a.ldo + (size_t)g * kv_mul * hd;
-    for (int k = tid; k < kv_mul * hd; k += nth) orow[k] = s_out[k];
+    if (s_abort) {
+        // a wait gave up: let the copies already issued land (bounded) before
+        // the shared memory is released, and leave the outputs untouched
+        if (tid == 0) {
+            // the last tile issued into each stage is the one whose phase is pending
+            const int n_iss = s_issued;
+            for (int k = n_iss - FUSED_STAGES < 0 ? 0 : n_iss - FUSED_STAGES; k < n_iss; k++) {
+                const long long t0 = clock64();
+                while (!mbar_test(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u) &&
+                       clock64() - t0 < WAIT_LIMIT) {
+                }
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    float *orow = a.out + (size_t)r * a.ldo + (size_t)g * KVM * hd;
+    for (int k = tid; k < KVM * hd; k += nth) orow[k] = s_out[k];
     // Q8_0 of the attention output for the Wo GEMV: this CTA owns the
-    // kv_mul*hd consecutive dims from g*kv_mul*hd, one 32-element block per
-    // warp when kv_mul*hd is a multiple of 32 (checked by the host)
+    // KVM*hd consecutive dims from g*KVM*hd, one 32-element block per warp
+    // when KVM*hd is a multiple of 32 (checked by the host)
     if (a.q8_out.qs) {
         const int nbr = a.dim / 32;
-        for (int blk = warp; blk < (kv_mul * hd) / 32; blk += nw)
+        for (int blk = warp; blk < (KVM * hd) / 32; blk += nw)
             q8x_store_block(s_out[blk * 32 + lane], a.q8_out,
-                            (size_t)r * nbr + (size_t)(g * kv_mul * hd) / 32 + blk, lane);
+                            (size_t)r * nbr + (size_t)(g * KVM * hd) / 32 + blk, lane);
     }
+}
+
+template <int KVM>
+void launch_softmax_pv(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s) {
+    const FusedShape f = fused_shape(KVM, a.head_dim, a.max_len);
+    dim3 grid(a.num_kv_heads, a.rows);
+    // consumer warps (one thread per head and dim pair) plus the producer warp
+    int nth = (KVM * (a.head_dim / 2) + 31) / 32 * 32 + 32;
+    nth = nth < PV_THREADS ? PV_THREADS : nth;
+    attn_softmax_pv_kernel<KVM><<<grid, nth, f.smem, s>>>(a, f.lp, vmap);
+}
+
+template <int KVM>
+void set_softmax_pv_smem(int bytes) {
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         bytes);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no -lcuda)
+EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (EncodeTiledFn) nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
 }
 
 }  // namespace
 
+bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
+                  uint64_t planes, int head_dim) {
+    const EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || !base || ((uintptr_t)base & 15) || (kv_dim & 3) || (head_dim & 3) ||
+        head_dim > 256 || head_dim > kv_dim || max_seq <= 0 || planes == 0 ||
+        planes > 0x7fffffffULL)
+        return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kv_dim, (cuuint64_t)max_seq, (cuuint64_t)planes};
+    const cuuint64_t strides[2] = {(cuuint64_t)kv_dim * 4, (cuuint64_t)kv_dim * 4 * (cuuint64_t)max_seq};
+    const cuuint32_t box[3] = {(cuuint32_t)head_dim, (cuuint32_t)TT_V, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool attention_fused_ok(const AttnArgs &a) {
     const int kv_mul = a.num_heads / a.num_kv_heads;
-    if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 1024) return false;
+    if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 992) return false;
     if (((uintptr_t)a.k_base | (uintptr_t)a.v_base) & 15) return false;
     if (!a.att) return false;  // the scores go through att
     if ((a.slot_stride | a.layer_off) & 3) return false;
-    return fused_shape(kv_mul, a.head_dim, a.max_len, 64).smem <= FUSED_SMEM_MAX ||
-           fused_shape(kv_mul, a.head_dim, a.max_len, 16).smem <= FUSED_SMEM_MAX;
+    const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
+    return fused_shape(kv_mul, a.head_dim, a.max_len).smem <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
 }
 
-void launch_attn_fused(const AttnArgs &a, cudaStream_t s) {
+void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s) {
     if (a.rows <= 0) return;
     const int kv_mul = a.num_heads / a.num_kv_heads;
     const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
     dim3 g1((a.max_len + TILE_KEYS - 1) / TILE_KEYS, a.num_kv_heads, a.rows);
     attn_scores_tiled_kernel<<<g1, TILE_KEYS, sk, s>>>(a);
-    int tt = 64;
-    FusedShape f = fused_shape(kv_mul, a.head_dim, a.max_len, tt);
-    while (f.smem > FUSED_SMEM_MAX && tt > 16) {
-        tt >>= 1;
-        f = fused_shape(kv_mul, a.head_dim, a.max_len, tt);
+    switch (kv_mul) {
+        case 1: launch_softmax_pv<1>(a, vmap, s); break;
+        case 2: launch_softmax_pv<2>(a, vmap, s); break;
+        case 3: launch_softmax_pv<3>(a, vmap, s); break;
+        case 4: launch_softmax_pv<4>(a, vmap, s); break;
+        case 5: launch_softmax_pv<5>(a, vmap, s); break;
+        case 6: launch_softmax_pv<6>(a, vmap, s); break;
+        case 7: launch_softmax_pv<7>(a, vmap, s); break;
+        default: launch_softmax_pv<8>(a, vmap, s); break;
     }
-    int nth = (kv_mul * (a.head_dim / 2) + 31) / 32 * 32;
-    nth = nth < 256 ? 256 : nth;
-    dim3 grid(a.num_kv_heads, a.rows);
-    attn_softmax_pv_kernel<<<grid, nth, f.smem, s>>>(a, tt, f.lp);
 }
 
 void set_attention_smem_limit(int bytes) {
-    cudaFuncSetAttribute(attn_softmax_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    set_softmax_pv_smem<1>(bytes);
+    set_softmax_pv_smem<2>(bytes);
+    set_softmax_pv_smem<3>(bytes);
+    set_softmax_pv_smem<4>(bytes);
+    set_softmax_pv_smem<5>(bytes);
+    set_softmax_pv_smem<6>(bytes);
+    set_softmax_pv_smem<7>(bytes);
+    set_softmax_pv_smem<8>(bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
@@ -504,9 +772,9 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s) {
     attn_pv_kernel<<<g, 32 * kv_mul, 0, s>>>(a);
 }
 
-void launch_attention(const AttnArgs &a, cudaStream_t s) {
-    if (attention_fused_ok(a)) {
-        launch_attn_fused(a, s);
+void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, cudaStream_t s) {
+    if (vmap && attention_fused_ok(a)) {
+        launch_attn_fused(a, *vmap, s);
         return;
     }
     launch_attn_scores(a, s);

@@ -28,34 +28,23 @@ namespace slm {
 
 namespace {
 
-struct WBlock {
-    uint4 q;
-    unsigned short d;
-};
-
-__device__ __forceinline__ WBlock load_wblock(const uint8_t *w, int tile, int nb, int j, int lane) {
-    const uint8_t *tp = w + tile_offset((size_t)tile, nb, j);
-    WBlock b;
-    b.q = __ldg(reinterpret_cast<const uint4 *>(tp) + lane);
-    b.d = __ldg(reinterpret_cast<const unsigned short *>(tp + 512) + lane);
-    return b;
-}
-
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
     unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc));
 }
 
 constexpr int JC = 64;   // activation blocks per shared-memory chunk (multiple of PF)
-constexpr int PF = 4;    // weight blocks in flight per lane
 
 template <int BT, int EPI>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, int units) {
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    constexpr int PF = 8;  // weight-ring depth (launch_bt sizes shared memory for 8)
     extern __shared__ __align__(16) unsigned char smem[];
     int8_t *s_qs = (int8_t *)smem;                    // [BT][JC][32]
     int32_t *s_c = (int32_t *)(smem + BT * JC * 32);  // [BT][JC][8]
     float *s_d = (float *)(smem + BT * JC * 64);      // [BT][JC]
+    // per-warp rings of weight blocks: [warp][RPT][PF][576 bytes]
+    uint8_t *s_w = smem + BT * JC * 68 + (threadIdx.x >> 5) * (RPT * PF * TILE_BYTES);
 
     const int lane = threadIdx.x & 31;
     const int unit = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -75,14 +64,23 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, 
 #pragma unroll
             for (int k = 0; k < 8; k++) acc[t][b][k] = 0.0f;
 
-    // weight blocks j..j+PF-1 are in flight while block j is consumed
-    WBlock ring[RPT][PF];
+    // weight blocks j+1..j+PF-1 are in flight (cp.async into this warp's
+    // shared-memory ring) while block j is consumed; lane l copies row l's
+    // 16 nibble bytes, lanes 0..3 the 64 bytes of scales
+    auto fetch = [&](int j) {
+        if (j < nb) {
+#pragma unroll
+            for (int t = 0; t < RPT; t++) {
+                const uint8_t *tp = a.w + tile_offset((size_t)tile[t], nb, j);
+                uint8_t *slot = s_w + (t * PF + j % PF) * TILE_BYTES;
+                cp_async16(slot + lane * 16, tp + lane * 16);
+                if (lane < 4) cp_async16(slot + 512 + lane * 16, tp + 512 + lane * 16);
+            }
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    };
     if (live) {
-#pragma unroll
-        for (int t = 0; t < RPT; t++)
-#pragma unroll
-            for (int u = 0; u < PF; u++)
-                if (u < nb) ring[t][u] = load_wblock(a.w, tile[t], nb, u, lane);
+        for (int u = 0; u < PF - 1; u++) fetch(u);
     }
 
     for (int jc = 0; jc < nb; jc += JC) {
@@ -116,50 +114,50 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, 
         __syncthreads();
         if (!live) continue;
 
-        for (int jl0 = 0; jl0 < jn; jl0 += PF) {
+        for (int jl = 0; jl < jn; jl++) {
+            const int j = jc + jl;
+            fetch(j + PF - 1);
+            asm volatile("cp.async.wait_group %0;\n" ::"n"(PF - 1));
+            __syncwarp();
+            unsigned lo[RPT][4], hi[RPT][4];
+            float dw[RPT];
 #pragma unroll
-            for (int u = 0; u < PF; u++) {
-                const int jl = jl0 + u;
-                const int j = jc + jl;
-                if (jl >= jn) break;  // warp-uniform (last chunk only)
-                unsigned lo[RPT][4], hi[RPT][4];
-                float dw[RPT];
+            for (int t = 0; t < RPT; t++) {
+                const uint8_t *slot = s_w + (t * PF + j % PF) * TILE_BYTES;
+                const uint4 q = *reinterpret_cast<const uint4 *>(slot + lane * 16);
+                dw[t] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(slot + 512 + lane * 2)));
+                const unsigned qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    lo[t][k] = qw[k] & 0x0F0F0F0Fu;
+                    hi[t][k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
+                }
+            }
+            __syncwarp();  // the slot may be refilled by the next fetch
+#pragma unroll
+            for (int b = 0; b < BT; b++) {
+                const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[0];
+                const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[1];
+                const int4 c0 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[0];
+                const int4 c1 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[1];
+                const float da = s_d[b * JC + jl];
+                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
                 for (int t = 0; t < RPT; t++) {
-                    const WBlock cur = ring[t][u];
-                    if (j + PF < nb) ring[t][u] = load_wblock(a.w, tile[t], nb, j + PF, lane);
-                    dw[t] = __half2float(__ushort_as_half(cur.d));
-                    const unsigned qw[4] = {cur.q.x, cur.q.y, cur.q.z, cur.q.w};
+                    const float d = __fmul_rn(dw[t], da);
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        lo[t][k] = qw[k] & 0x0F0F0F0Fu;
-                        hi[t][k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
-                    }
-                }
-#pragma unroll
-                for (int b = 0; b < BT; b++) {
-                    const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[0];
-                    const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[1];
-                    const int4 c0 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[0];
-                    const int4 c1 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[1];
-                    const float da = s_d[b * JC + jl];
-                    const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                    for (int t = 0; t < RPT; t++) {
-                        const float d = __fmul_rn(dw[t], da);
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
-                            acc[t][b][k] = __fmaf_rn(d, f0, acc[t][b][k]);
-                            float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
-                            acc[t][b][4 + k] = __fmaf_rn(d, f1, acc[t][b][4 + k]);
-                        }
+                        float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
+                        acc[t][b][k] = __fmaf_rn(d, f0, acc[t][b][k]);
+                        float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
+                        acc[t][b][4 + k] = __fmaf_rn(d, f1, acc[t][b][4 + k]);
                     }
                 }
             }
         }
     }
+    asm volatile("cp.async.wait_group 0;\n" ::);
     if (!live) return;
 
     // ---- epilogue
@@ -237,13 +235,15 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, 
     }
 }
 
-constexpr int TARGET_WARPS = 148 * 8;
+constexpr int TARGET_WARPS = 148 * 4;
 
 template <int BT, int EPI>
 void launch_bt(const GemvArgs &a, int total_tiles, int units, cudaStream_t s) {
     const int nbt = (a.batch + BT - 1) / BT;
     dim3 grid((unsigned)((units + 3) / 4), (unsigned)nbt);
-    gemv_kernel<BT, EPI><<<grid, 128, (size_t)BT * JC * 68, s>>>(a, total_tiles, units);
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    const size_t smem = (size_t)BT * JC * 68 + 4 * (size_t)RPT * 8 * TILE_BYTES;
+    gemv_kernel<BT, EPI><<<grid, 128, smem, s>>>(a, total_tiles, units);
 }
 
 template <int EPI>
@@ -260,7 +260,21 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
         launch_bt<1, EPI>(a, total_tiles, units, s);
 }
 
+template <int EPI>
+void set_limits(int bytes) {
+    cudaFuncSetAttribute(gemv_kernel<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(gemv_kernel<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(gemv_kernel<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 }  // namespace
+
+void set_gemv_smem_limit(int bytes) {
+    set_limits<EPI_STORE>(bytes);
+    set_limits<EPI_RESIDUAL>(bytes);
+    set_limits<EPI_QKV>(bytes);
+    set_limits<EPI_SWIGLU_Q8>(bytes);
+}
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s) {
     if (a.batch <= 0 || a.rows <= 0) return;

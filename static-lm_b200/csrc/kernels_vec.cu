@@ -17,66 +17,70 @@ namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
 
-// One warp (one CTA) per row: the row is staged in shared memory with
-// coalesced loads, lanes 0..3 run the four sum-of-squares chains from there;
-// rms = 1/sqrt(sum(x^2) * (1/n) + eps); y = (x*rms)*w; each full 32-element
-// block of y is quantized to Q8X.
-__global__ void __launch_bounds__(32) rmsnorm_q8_kernel(const float *__restrict__ x, size_t ldx,
-                                                        const float *__restrict__ w, int n,
-                                                        float eps, float inv_n,
-                                                        float *__restrict__ y, size_t ldy, Q8X q8,
-                                                        int rows, int do_q8) {
+// One CTA (8 warps) per row: the row and the weights are staged in shared
+// memory with coalesced loads; lanes 0..3 of warp 0 run the four
+// sum-of-squares chains; rms = 1/sqrt(sum(x^2) * (1/n) + eps); then the
+// warps share the 32-element blocks of y = (x*rms)*w, each quantized to Q8X.
+constexpr int NORM_THREADS = 256;
+
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_q8_kernel(
+    const float *__restrict__ x, size_t ldx, const float *__restrict__ w, int n, float eps,
+    float inv_n, float *__restrict__ y, size_t ldy, Q8X q8, int rows, int do_q8) {
     extern __shared__ __align__(16) float s_x[];  // [n] row, then [n] weights
+    __shared__ float s_rms;
     float *s_w = s_x + ((n + 3) & ~3);
-    const int lane = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = blockIdx.x;
     if (r >= rows) return;
     const float *xr = x + (size_t)r * ldx;
     if ((n & 3) == 0 && (((uintptr_t)xr | (uintptr_t)w) & 15) == 0) {
-        for (int i = lane; i < n / 4; i += 32) {
+        for (int i = tid; i < n / 4; i += NORM_THREADS) {
             reinterpret_cast<float4 *>(s_x)[i] = __ldg(reinterpret_cast<const float4 *>(xr) + i);
             reinterpret_cast<float4 *>(s_w)[i] = __ldg(reinterpret_cast<const float4 *>(w) + i);
         }
     } else {
-        for (int i = lane; i < n; i += 32) {
+        for (int i = tid; i < n; i += NORM_THREADS) {
             s_x[i] = xr[i];
             s_w[i] = w[i];
         }
     }
-    __syncwarp();
-    const int vl = n & ~3;
-    float acc = 0.0f;
-    if (lane < 4) {
-        int i = lane;
-        for (; i + 28 < vl; i += 32) {
-            float v[8];
+    __syncthreads();
+    if (warp == 0) {
+        const int vl = n & ~3;
+        float acc = 0.0f;
+        if (lane < 4) {
+            int i = lane;
+            for (; i + 28 < vl; i += 32) {
+                float v[8];
 #pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = s_x[i + 4 * u];
+                for (int u = 0; u < 8; u++) v[u] = s_x[i + 4 * u];
 #pragma unroll
-            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+                for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+            }
+            for (; i < vl; i += 4) acc = __fadd_rn(acc, __fmul_rn(s_x[i], s_x[i]));
         }
-        for (; i < vl; i += 4) acc = __fadd_rn(acc, __fmul_rn(s_x[i], s_x[i]));
+        float a1 = __shfl_sync(FULL, acc, 1);
+        float a2 = __shfl_sync(FULL, acc, 2);
+        float a3 = __shfl_sync(FULL, acc, 3);
+        if (lane == 0) {
+            float sum = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+            for (int i = vl; i < n; i++) sum = __fadd_rn(sum, __fmul_rn(s_x[i], s_x[i]));
+            float mean = __fmul_rn(sum, inv_n);
+            float var = __fadd_rn(mean, eps);
+            s_rms = __fdiv_rn(1.0f, __fsqrt_rn(var));
+        }
     }
-    float a1 = __shfl_sync(FULL, acc, 1);
-    float a2 = __shfl_sync(FULL, acc, 2);
-    float a3 = __shfl_sync(FULL, acc, 3);
-    float s = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
-    if (lane == 0)
-        for (int i = vl; i < n; i++) s = __fadd_rn(s, __fmul_rn(s_x[i], s_x[i]));
-    s = __shfl_sync(FULL, s, 0);
-    float mean = __fmul_rn(s, inv_n);
-    float var = __fadd_rn(mean, eps);
-    float sd = __fsqrt_rn(var);
-    float rms = __fdiv_rn(1.0f, sd);
-    int nb = n >> 5;
-    for (int j = 0; j < nb; j++) {
-        int i = j * 32 + lane;
-        float o = __fmul_rn(__fmul_rn(s_x[i], rms), s_w[i]);
+    __syncthreads();
+    const float rms = s_rms;
+    const int nb = n >> 5;
+    for (int j = warp; j < nb; j += NORM_THREADS / 32) {
+        const int i = j * 32 + lane;
+        const float o = __fmul_rn(__fmul_rn(s_x[i], rms), s_w[i]);
         if (y) y[(size_t)r * ldy + i] = o;
         if (do_q8) q8x_store_block(o, q8, (size_t)r * nb + j, lane);
     }
-    int i = nb * 32 + lane;
-    if (y && i < n) y[(size_t)r * ldy + i] = __fmul_rn(__fmul_rn(s_x[i], rms), s_w[i]);
+    for (int i = nb * 32 + tid; i < n; i += NORM_THREADS)
+        if (y) y[(size_t)r * ldy + i] = __fmul_rn(__fmul_rn(s_x[i], rms), s_w[i]);
 }
 
 // One warp per (row, block).
@@ -339,8 +343,8 @@ void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float 
     if (rows <= 0) return;
     float inv_n = 1.0f / (float)n;
     size_t smem = sizeof(float) * (2 * (size_t)((n + 3) & ~3));
-    rmsnorm_q8_kernel<<<rows, 32, smem, s>>>(x, ldx, w, n, eps, inv_n, y, ldy, q8, rows,
-                                             q8.qs != nullptr);
+    rmsnorm_q8_kernel<<<rows, NORM_THREADS, smem, s>>>(x, ldx, w, n, eps, inv_n, y, ldy, q8, rows,
+                                                       q8.qs != nullptr);
 }
 
 void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s) {

@@ -256,6 +256,7 @@ namespace {
 
 int gemm_into(const slm_qmatrix *w, Q8X x, float *out, uint64_t batch, uint64_t rows,
               uint64_t cols, cudaStream_t st) {
+    ensure_kernel_attributes();
     GemvArgs g{};
     g.w = w->tiles;
     g.rows = (int)rows;
@@ -458,7 +459,10 @@ SLM_EXPORT int slm_causal_attention(const float *q, const float *k, const float 
     a.ldo = cfg->dim;
     a.rows = 1;
     a.max_len = (int)pos + 1;
-    launch_attention(a, (cudaStream_t)stream);
+    // one [max_seq][kv_dim] plane of V: z = 0 for every row
+    CUtensorMap vmap;
+    const bool have_map = encode_v_map(&vmap, v, a.kv_dim, a.max_seq, 1, a.head_dim);
+    launch_attention(a, have_map ? &vmap : nullptr, (cudaStream_t)stream);
     return launch_check("attention kernels");
 }
 
@@ -501,7 +505,7 @@ struct slm_model {
     slm_arena *arena = nullptr;
     // arena views
     float *rope_cos, *rope_sin, *x, *x_mid, *xb, *q, *logits, *att, *kv, *ybuf, *emb;
-    void *q8a, *q8b;
+    void *q8a[2], *q8b[2];  // Q8X scratch pairs of the two decode parts
     uint64_t q8_blocks = 0;
     int32_t *d_tok, *d_pos, *d_slot, *d_next, *d_err;
     uint64_t slot_stride = 0, layer_stride = 0, v_off = 0;
@@ -509,6 +513,11 @@ struct slm_model {
     std::map<std::tuple<int, int>, cudaGraphExec_t> graphs;
     bool use_graphs = true;
     bool use_fused_attention = true;
+    bool split_decode = true;
+    cudaStream_t stream2 = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
+    bool have_vmap = false;
 };
 
 namespace {
@@ -571,23 +580,33 @@ inline void mark(Profiler *p, int ph) {
     if (p) p->mark(ph);
 }
 
-// Enqueue one forward pass over `n` activation rows already holding token
-// ids / slots / positions in d_tok / d_slot / d_pos.
-void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *prof = nullptr) {
-    cudaStream_t st = m->stream;
+// Enqueue one forward pass over the `n` activation rows [row0, row0+n),
+// which already hold token ids / slots / positions in d_tok / d_slot / d_pos,
+// on stream `st` with the Q8 scratch pair `part` (0 or 1).  Rows of
+// different sequences are independent, so disjoint row ranges can run on
+// different streams at the same time.
+void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, cudaStream_t st,
+                     int part, Profiler *prof = nullptr) {
     const slm_config &c = m->cfg;
     const int d = (int)c.dim, h = (int)c.hidden_dim;
+    const size_t r0 = (size_t)row0;
+    float *x = m->x + r0 * d, *x_mid = m->x_mid + r0 * d, *xb = m->xb + r0 * d;
+    float *q = m->q + r0 * d;
+    int32_t *tok = m->d_tok + r0, *pos = m->d_pos + r0, *slot = m->d_slot + r0;
+    int32_t *next = m->d_next + r0;
+    float *att = m->att + r0 * c.num_heads * c.max_seq_len;
+    float *logits = m->logits + r0 * m->vocab;
     mark(prof, -1);
-    launch_embed(m->embd.tiles, d / QK, m->d_tok, m->vocab, m->x, d, n, m->d_err, st);
+    launch_embed(m->embd.tiles, d / QK, tok, m->vocab, x, d, n, m->d_err, st);
     mark(prof, SLM_PHASE_EMBED);
 
     QkvArgs qa{};
-    qa.q = m->q;
+    qa.q = q;
     qa.ldq = d;
     qa.k_base = m->kv;
     qa.v_base = m->kv + m->v_off;
-    qa.slot = m->d_slot;
-    qa.pos = m->d_pos;
+    qa.slot = slot;
+    qa.pos = pos;
     qa.slot_stride = m->slot_stride;
     qa.dim = d;
     qa.kv_dim = m->kvd;
@@ -598,22 +617,24 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
     qa.err = m->d_err;
 
     AttnArgs aa = attn_args_for(&c);
-    aa.q = m->q;
+    aa.q = q;
     aa.ldq = d;
     aa.k_base = m->kv;
     aa.v_base = m->kv + m->v_off;
-    aa.slot = m->d_slot;
-    aa.pos = m->d_pos;
+    aa.slot = slot;
+    aa.pos = pos;
     aa.slot_stride = m->slot_stride;
-    aa.att = m->att;
+    aa.att = att;
     aa.att_ld = c.max_seq_len;
-    aa.out = m->xb;
+    aa.out = xb;
     aa.ldo = d;
     aa.rows = n;
     aa.max_len = max_len;
+    aa.err = m->d_err;
+    aa.z_slot = 2LL * m->L;  // planes [slot][layer][K|V] from the first V plane
 
-    Q8X qa8 = q8view(m->q8a, m->q8_blocks), qb8 = q8view(m->q8b, m->q8_blocks);
-    const bool fused = m->use_fused_attention && attention_fused_ok(aa);
+    Q8X qa8 = q8view(m->q8a[part], m->q8_blocks), qb8 = q8view(m->q8b[part], m->q8_blocks);
+    const bool fused = m->use_fused_attention && m->have_vmap && attention_fused_ok(aa);
     if (fused) {
         aa.write_probs = false;  // probabilities stay in shared memory
         const int kv_mul = (int)(c.num_heads / c.num_kv_heads);
@@ -622,7 +643,7 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
     for (int l = 0; l < m->L; l++) {
         const LayerDev &ld = m->layers[l];
         // rmsnorm(x) -> Q8 (transformer.rs:411, kernels.rs:301)
-        launch_rmsnorm_q8(m->x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
+        launch_rmsnorm_q8(x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
         mark(prof, SLM_PHASE_RMSNORM);
         // Wq/Wk/Wv + RoPE + KV append (transformer.rs:413-428)
         GemvArgs g{};
@@ -638,12 +659,13 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
         mark(prof, SLM_PHASE_QKV);
         // attention (transformer.rs:430-443)
         aa.layer_off = (size_t)l * m->layer_stride;
+        aa.z_layer = 2LL * l;
         if (fused) {
-            // scores, softmax, PV and the Q8_0 of the output in one kernel
-            launch_attn_fused(aa, st);
+            // scores, then softmax + PV + the Q8_0 of the output
+            launch_attn_fused(aa, m->vmap, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
             if (!aa.q8_out.qs) {
-                launch_quantize_q8x(m->xb, d, d, qb8, n, st);
+                launch_quantize_q8x(xb, d, d, qb8, n, st);
                 mark(prof, SLM_PHASE_QUANTIZE);
             }
         } else {
@@ -653,7 +675,7 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
             mark(prof, SLM_PHASE_ATTN_SOFTMAX);
             launch_attn_pv(aa, st);
             mark(prof, SLM_PHASE_ATTN_PV);
-            launch_quantize_q8x(m->xb, d, d, qb8, n, st);
+            launch_quantize_q8x(xb, d, d, qb8, n, st);
             mark(prof, SLM_PHASE_QUANTIZE);
         }
         // Wo + residual (transformer.rs:445-446)
@@ -664,14 +686,14 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
         g.x = qb8;
         g.batch = n;
         g.epi = EPI_RESIDUAL;
-        g.out = m->x_mid;
+        g.out = x_mid;
         g.ld_out = d;
-        g.res = m->x;
+        g.res = x;
         g.ld_res = d;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_WO);
         // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
-        launch_rmsnorm_q8(m->x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
+        launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
         mark(prof, SLM_PHASE_RMSNORM);
         g = GemvArgs{};
         g.w = ld.wgu.tiles;
@@ -691,16 +713,16 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
         g.x = qb8;
         g.batch = n;
         g.epi = EPI_RESIDUAL;
-        g.out = m->x;
+        g.out = x;
         g.ld_out = d;
-        g.res = m->x_mid;
+        g.res = x_mid;
         g.ld_res = d;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_DOWN);
     }
     if (kind == STEP_EMBED) return;
     // final RMSNorm + lm_head + argmax (transformer.rs:776-794 / 835-853)
-    const float *xs = kind == STEP_PREFILL ? m->x + (size_t)(n - 1) * d : m->x;
+    const float *xs = kind == STEP_PREFILL ? x + (size_t)(n - 1) * d : x;
     int rows = kind == STEP_PREFILL ? 1 : n;
     launch_rmsnorm_q8(xs, d, m->out_norm, d, c.rms_eps, nullptr, 0, qa8, rows, st);
     mark(prof, SLM_PHASE_RMSNORM);
@@ -711,11 +733,11 @@ void enqueue_forward(slm_model *m, int n, int max_len, StepKind kind, Profiler *
     g.x = qa8;
     g.batch = rows;
     g.epi = EPI_STORE;
-    g.out = m->logits;
+    g.out = logits;
     g.ld_out = m->vocab;
     launch_gemv(g, st);
     mark(prof, SLM_PHASE_LM_HEAD);
-    launch_argmax(m->logits, m->vocab, m->vocab, m->d_next, rows, st);
+    launch_argmax(logits, m->vocab, m->vocab, next, rows, st);
     mark(prof, SLM_PHASE_ARGMAX);
 }
 
@@ -729,12 +751,36 @@ uint32_t decode_launches(const slm_model *m) {
         const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
         attn = ((kv_mul * m->hd) % 32 == 0) ? 1 : 2;
     }
-    return 1u + (6u + attn) * (uint32_t)m->L + 3u + 1u;
+    return 1u + (6u + attn) * (uint32_t)m->L + 3u;
 }
+
+// Decode rows split into two halves on two streams when the batch is large
+// enough for both halves to fill the GPU's latency gaps.
+int decode_parts(const slm_model *m, int n) { return (m->split_decode && n >= 16) ? 2 : 1; }
 
 int len_bucket(const slm_model *m, int max_len) {
     int b = (max_len + 255) / 256 * 256;
     return std::min<int>(b, (int)m->cfg.max_seq_len);
+}
+
+// Enqueue a decode step of rows [0, n) (and the greedy advance): with two
+// parts, rows [0, n/2) run on the model stream and [n/2, n) on the second
+// stream, forked and joined with events so that a graph capture records two
+// parallel branches.
+void enqueue_decode(slm_model *m, int n, int bucket, bool advance) {
+    const int parts = decode_parts(m, n);
+    if (parts == 1) {
+        enqueue_forward(m, 0, n, bucket, STEP_DECODE, m->stream, 0);
+    } else {
+        const int na = n / 2;
+        cudaEventRecord(m->ev_fork, m->stream);
+        cudaStreamWaitEvent(m->stream2, m->ev_fork, 0);
+        enqueue_forward(m, 0, na, bucket, STEP_DECODE, m->stream, 0);
+        enqueue_forward(m, na, n - na, bucket, STEP_DECODE, m->stream2, 1);
+        cudaEventRecord(m->ev_join, m->stream2);
+        cudaStreamWaitEvent(m->stream, m->ev_join, 0);
+    }
+    if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
 }
 
 // Run a decode step (optionally followed by the greedy advance) through a
@@ -742,8 +788,7 @@ int len_bucket(const slm_model *m, int max_len) {
 int run_decode(slm_model *m, int n, int max_len, bool advance) {
     int bucket = len_bucket(m, max_len);
     if (!m->use_graphs) {
-        enqueue_forward(m, n, bucket, STEP_DECODE);
-        if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
+        enqueue_decode(m, n, bucket, advance);
         return launch_check("decode step");
     }
     auto key = std::make_tuple(n * 2 + (advance ? 1 : 0), bucket);
@@ -751,8 +796,7 @@ int run_decode(slm_model *m, int n, int max_len, bool advance) {
     if (it == m->graphs.end()) {
         cudaGraph_t graph = nullptr;
         CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        enqueue_forward(m, n, bucket, STEP_DECODE);
-        if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
+        enqueue_decode(m, n, bucket, advance);
         cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
         if (e != cudaSuccess) {
             cudaGetLastError();
@@ -775,8 +819,9 @@ int read_device_error(slm_model *m) {
     if (err) {
         CUDA_TRY(cudaMemsetAsync(m->d_err, 0, 4, m->stream));
         CUDA_TRY(cudaStreamSynchronize(m->stream));
-        return fail(SLM_ERR_DEVICE_INPUT, err == 1 ? "token_id out of vocabulary bounds"
-                                                   : "sequence position out of bounds");
+        return fail(SLM_ERR_DEVICE_INPUT, err == 1   ? "token_id out of vocabulary bounds"
+                                          : err == 2 ? "sequence position out of bounds"
+                                                     : "a device wait timed out");
     }
     return SLM_OK;
 }
@@ -800,6 +845,7 @@ void ensure_kernel_attributes() {
     if (dev < 31 && (done_mask & (1 << dev))) return;
     slm::set_attention_smem_limit(200 * 1024);
     slm::set_rmsnorm_smem_limit(200 * 1024);
+    slm::set_gemv_smem_limit(96 * 1024);
     if (dev < 31) done_mask |= 1 << dev;
 }
 }  // namespace
@@ -837,6 +883,9 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         return rc;
     };
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream2, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming);
     if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, cudaGetErrorString(e)));
 
     // ---- weights: one device buffer
@@ -894,8 +943,7 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     add_f(d);                                  // embedding accumulator
     add_f(S * V);                              // logits
     add_f(R * cfg->num_heads * T);             // att
-    add_f(q8f);
-    add_f(q8f);
+    for (int i = 0; i < 4; i++) add_f(q8f);
     for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
     add_f(S * m->slot_stride);                 // KV
     rc = slm_arena_create(device, cap + a16, &m->arena);
@@ -910,10 +958,12 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         (rc = alloc_view(m, d, &m->emb)) || (rc = alloc_view(m, S * V, &m->logits)) ||
         (rc = alloc_view(m, R * cfg->num_heads * T, &m->att)))
         return cleanup(rc);
-    if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
-    m->q8a = p;
-    if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
-    m->q8b = p;
+    for (int i = 0; i < 2; i++) {
+        if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
+        m->q8a[i] = p;
+        if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
+        m->q8b[i] = p;
+    }
     int32_t **ints[] = {&m->d_tok, &m->d_pos, &m->d_slot, &m->d_next, &m->d_err};
     for (auto ip : ints) {
         if ((rc = alloc_view(m, R, &p))) return cleanup(rc);
@@ -928,6 +978,12 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->use_graphs = !(env && env[0] == '1');
     env = getenv("SLM_ATTENTION_3PASS");
     m->use_fused_attention = !(env && env[0] == '1');
+    env = getenv("SLM_DECODE_ONE_STREAM");
+    m->split_decode = !(env && env[0] == '1');
+    // every V plane of the cache, addressed from the first one: plane
+    // (slot, layer) sits at z = slot*2L + 2*layer, the last at S*2L - 2
+    m->have_vmap = encode_v_map(&m->vmap, m->kv + m->v_off, m->kvd, (int)cfg->max_seq_len,
+                                (uint64_t)S * 2 * m->L - 1, m->hd);
     *out = m;
     return SLM_OK;
 }
@@ -936,7 +992,11 @@ SLM_EXPORT void slm_model_destroy(slm_model *m) {
     if (!m) return;
     DeviceScope ds(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->stream2) cudaStreamSynchronize(m->stream2);
     for (auto &kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    if (m->ev_fork) cudaEventDestroy(m->ev_fork);
+    if (m->ev_join) cudaEventDestroy(m->ev_join);
+    if (m->stream2) cudaStreamDestroy(m->stream2);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->arena) slm_arena_destroy(m->arena);
     if (m->wbuf) cudaFree(m->wbuf);
@@ -1023,7 +1083,7 @@ SLM_EXPORT int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_
     TRY(check_tokens(m, (int)n, tokens));
     DeviceScope ds(m->device);
     TRY(stage_rows(m, (int)n, tokens, nullptr, seq, nullptr, start_pos));
-    enqueue_forward(m, (int)n, (int)(start_pos + n), STEP_PREFILL);
+    enqueue_forward(m, 0, (int)n, (int)(start_pos + n), STEP_PREFILL, m->stream, 0);
     TRY(launch_check("prefill"));
     return fetch_next(m, 1, next);
 }
@@ -1066,7 +1126,7 @@ SLM_EXPORT int slm_model_embed_tokens(slm_model *m, uint32_t seq, const int32_t 
     DeviceScope ds(m->device);
     const int d = (int)m->cfg.dim;
     TRY(stage_rows(m, (int)n, tokens, nullptr, seq, nullptr, 0));
-    enqueue_forward(m, (int)n, (int)n, STEP_EMBED);
+    enqueue_forward(m, 0, (int)n, (int)n, STEP_EMBED, m->stream, 0);
     Q8X none{};
     launch_rmsnorm_q8(m->x, d, m->out_norm, d, m->cfg.rms_eps, m->ybuf, d, none, (int)n, m->stream);
     launch_mean_pool(m->ybuf, d, (int)n, d, 1.0f / (float)n, m->emb, m->stream);
@@ -1160,8 +1220,8 @@ SLM_EXPORT int slm_model_read_hidden(slm_model *m, uint32_t row, float *host) {
     return SLM_OK;
 }
 
-SLM_EXPORT uint32_t slm_model_launches_per_decode_step(const slm_model *m) {
-    return m ? decode_launches(m) : 0;
+SLM_EXPORT uint32_t slm_model_launches_per_decode_step(const slm_model *m, uint32_t n) {
+    return m ? decode_launches(m) * (uint32_t)decode_parts(m, (int)n) + 1u : 0;
 }
 
 SLM_EXPORT int slm_model_kv_write_device(slm_model *m, uint32_t seq, uint32_t layer,
@@ -1200,7 +1260,8 @@ SLM_EXPORT int slm_model_profile_decode(slm_model *m, uint32_t n, const uint32_t
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_pos, pos_dev, n * 4, cudaMemcpyDeviceToDevice, st);
     for (uint32_t s = 0; s < steps && e == cudaSuccess && rc == SLM_OK; s++) {
         prof.n = 0;
-        enqueue_forward(m, (int)n, len_bucket(m, (int)(max_pos_hint + s + 1)), STEP_DECODE, &prof);
+        enqueue_forward(m, 0, (int)n, len_bucket(m, (int)(max_pos_hint + s + 1)), STEP_DECODE,
+                        st, 0, &prof);
         launch_advance(m->d_tok, m->d_pos, m->d_next, (int)n, st);
         prof.mark(SLM_PHASE_ADVANCE);
         e = cudaStreamSynchronize(st);

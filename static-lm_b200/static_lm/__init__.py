@@ -250,9 +250,8 @@ class Model:
                                        max_pos_hint, ms)
         return {name: float(ms[i]) for i, name in enumerate(PHASES)}
 
-    @property
-    def launches_per_decode_step(self) -> int:
-        return int(lib().slm_model_launches_per_decode_step(self.h))
+    def launches_per_decode_step(self, n: int) -> int:
+        return int(lib().slm_model_launches_per_decode_step(self.h, n))
 
     def kv_read(self, seq: int, layer: int, which: int, row0: int, nrows: int) -> np.ndarray:
         out = np.zeros(nrows * self.kv_dim, dtype=np.float32)

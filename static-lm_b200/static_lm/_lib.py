@@ -109,7 +109,7 @@ SIGNATURES = {
     "slm_model_kv_write_device": (C.c_int, [_V, _U32, _U32, _U32, _U32, _U32, _V], True),
     "slm_model_profile_decode": (C.c_int, [_V, _U32, _V, _V, _V, _U32, _U32,
                                            C.POINTER(C.c_float)], True),
-    "slm_model_launches_per_decode_step": (_U32, [_V], False),
+    "slm_model_launches_per_decode_step": (_U32, [_V, _U32], False),
 }
 
 PHASES = ["embed", "rmsnorm_q8", "qkv_gemv_rope", "attn_scores", "attn_softmax", "attn_pv",

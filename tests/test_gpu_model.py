@@ -127,6 +127,28 @@ def test_decode_steps_device_matches_host_loop(cuda):
     assert pd.cpu().tolist() == [p + steps for p in pos]
 
 
+def test_two_stream_decode_matches_one_stream(cuda):
+    cfg, layers, vocab = synth.config("cfg1")
+    w = synth.synth_model(cfg, layers, vocab, seed=6)
+    B = 20
+    os.environ["SLM_DECODE_ONE_STREAM"] = "1"
+    try:
+        one = S.Model(cfg, w, max_sequences=B, max_rows=B)
+    finally:
+        del os.environ["SLM_DECODE_ONE_STREAM"]
+    two = S.Model(cfg, w, max_sequences=B, max_rows=B)
+    assert two.launches_per_decode_step(B) > one.launches_per_decode_step(B)
+    toks = [(s * 37 + 1) % vocab for s in range(B)]
+    pos = [0] * B
+    for _ in range(3):
+        a = one.decode_batch(list(range(B)), toks, pos)
+        b = two.decode_batch(list(range(B)), toks, pos)
+        assert list(a) == list(b)
+        for r in (0, B // 2, B - 1):
+            assert np.array_equal(one.logits(r), two.logits(r))
+        toks, pos = list(a), [p + 1 for p in pos]
+
+
 def test_graphs_and_eager_agree(cuda):
     cfg, w = small_weights()
     os.environ["SLM_DISABLE_GRAPHS"] = "1"
@@ -161,7 +183,7 @@ def test_fused_and_three_pass_attention_agree(cuda):
     assert list(a) == list(b)
     for r in range(2):
         assert np.array_equal(three.logits(r), fused.logits(r))
-    assert fused.launches_per_decode_step < three.launches_per_decode_step
+    assert fused.launches_per_decode_step(2) < three.launches_per_decode_step(2)
 
 
 def test_cfg3_shape_prefilled_kv_decode(cuda):
