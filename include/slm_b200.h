@@ -121,6 +121,23 @@ int slm_gemm_q4_0(const slm_qmatrix *w, const void *inputs_q8_dev, float *output
                   uint64_t batch, uint64_t rows, uint64_t cols, void *scratch_dev,
                   uint64_t scratch_bytes, void *stream);
 uint64_t slm_gemm_q4_0_scratch_bytes(uint64_t batch, uint64_t cols);
+/* No counterpart in the reference.  The same product as slm_gemm_q4_0_arena
+ * (output[b*rows + r] = dot(W[r], q8(inputs[b]))) for callers that must not
+ * allocate device memory on this path: a host running under a device-memory
+ * budget fixed at start-up, or one that keeps cudaMalloc/cudaFree (which can
+ * synchronize the device and stall every stream) off its serving loop.  The
+ * Q8_0 activations go to a static buffer of SLM_NOALLOC_SCRATCH_BYTES in
+ * the library's device image, so batch*cols/32 blocks of 68 bytes must fit:
+ * batch*cols <= 1,973,760; larger sizes return SLM_ERR_CAPACITY.  The first
+ * call on a device looks the buffer's address up (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the one
+ * buffer: calls that overlap on the GPU (different streams, or different
+ * host threads without ordering) race on it and must be serialized by the
+ * caller.  inputs_dev is [batch][cols] f32, output_dev [batch][rows] f32,
+ * both device memory on the weights' device. */
+#define SLM_NOALLOC_SCRATCH_BYTES (4u << 20)
+int slm_gemm_q4_0_f32_noalloc(const slm_qmatrix *w, const float *inputs_dev, float *output_dev,
+                              uint64_t batch, uint64_t rows, uint64_t cols, void *stream);
 /* quantize_row_q8_0 (src/quant/blocks.rs:102-123) into BlockQ8_0 (34 B). */
 int slm_quantize_row_q8_0(const float *src_dev, void *dst_blocks_dev, uint64_t n, void *stream);
 

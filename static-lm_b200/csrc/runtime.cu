@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -331,6 +332,60 @@ SLM_EXPORT int slm_gemm_q4_0(const slm_qmatrix *w, const void *xq, float *out, u
     launch_q8_ref_to_q8x(xq, x, blocks, st);
     TRY(launch_check("q8 conversion kernel"));
     return gemm_into(w, x, out, batch, rows, cols, st);
+}
+
+// ---- the allocation-free GEMM: Q8 activations in a static device buffer
+
+namespace {
+
+// Lives in this library's device image on every device that loads it; the
+// quantize kernel writes every block the GEMV then reads, so nothing in it
+// has to start at zero and stale contents from an earlier call are never read.
+static __device__ __align__(256) unsigned char g_noalloc_q8[SLM_NOALLOC_SCRATCH_BYTES];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[NOALLOC_MAX_DEVICES];  // device address per device, null until looked up
+
+// The buffer's address on the current device (looked up once per device,
+// with that device current).
+int noalloc_scratch(int device, void **out) {
+    if (device < 0 || device >= NOALLOC_MAX_DEVICES)
+        return fail(SLM_ERR_INVALID_ARG, "device ordinal out of range for the static scratch");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_q8);
+        if (e != cudaSuccess)
+            return fail(SLM_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_noalloc_ptr[device] = p;
+    }
+    *out = g_noalloc_ptr[device];
+    return SLM_OK;
+}
+
+}  // namespace
+
+SLM_EXPORT int slm_gemm_q4_0_f32_noalloc(const slm_qmatrix *w, const float *inputs_dev,
+                                         float *output_dev, uint64_t batch, uint64_t rows,
+                                         uint64_t cols, void *stream) {
+    TRY(check_gemm_shape(w, batch, rows, cols));
+    if (batch == 0 || rows == 0) return SLM_OK;
+    if (!inputs_dev || !output_dev) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    const uint64_t blocks = batch * (cols / QK);
+    if (q8x_bytes(blocks) > SLM_NOALLOC_SCRATCH_BYTES)
+        return fail(SLM_ERR_CAPACITY,
+                    "batch*cols needs " + std::to_string(q8x_bytes(blocks)) +
+                        " bytes of Q8 scratch; the static buffer holds " +
+                        std::to_string(SLM_NOALLOC_SCRATCH_BYTES));
+    DeviceScope ds(w->device);
+    void *scratch = nullptr;
+    TRY(noalloc_scratch(w->device, &scratch));
+    cudaStream_t st = (cudaStream_t)stream;
+    Q8X x = q8x_view(scratch, blocks);
+    launch_quantize_q8x(inputs_dev, cols, (int)cols, x, (int)batch, st);
+    TRY(launch_check("quantize kernel"));
+    return gemm_into(w, x, output_dev, batch, rows, cols, st);
 }
 
 SLM_EXPORT int slm_quantize_row_q8_0(const float *src, void *dst, uint64_t n, void *stream) {

@@ -81,6 +81,7 @@ SIGNATURES = {
     "slm_gemm_q4_0_arena": (C.c_int, [_V, _V, Slice, Slice, Slice, _U64, _U64, _U64, _V], True),
     "slm_gemm_q4_0": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V, _U64, _V], True),
     "slm_gemm_q4_0_scratch_bytes": (_U64, [_U64, _U64], False),
+    "slm_gemm_q4_0_f32_noalloc": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V], True),
     "slm_quantize_row_q8_0": (C.c_int, [_V, _V, _U64, _V], True),
     "slm_exec_rmsnorm": (C.c_int, [C.POINTER(_V), _V, _U64, C.c_float, _V], True),
     "slm_exec_softmax": (C.c_int, [C.POINTER(_V), _V, _U64, _V], True),
