@@ -20,11 +20,9 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "--fm
 
 def build(verbose: bool = False, extra=None) -> str:
     srcs = [os.path.join(CSRC, s) for s in SOURCES]
-    newest = max(os.path.getmtime(p) for p in srcs + [os.path.join(CSRC, "kernels.h"),
-                                                      os.path.join(CSRC, "common.cuh"),
-                                                      os.path.join(HERE, "..", "include",
-                                                                   "slm_b200.h"),
-                                                      os.path.abspath(__file__)])
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
+    newest = max(os.path.getmtime(p) for p in srcs + headers +
+                 [os.path.join(HERE, "..", "include", "slm_b200.h"), os.path.abspath(__file__)])
     if os.path.exists(OUT) and os.path.getmtime(OUT) >= newest and not extra:
         return OUT
     cmd = [NVCC] + FLAGS + (extra or []) + ["-o", OUT] + srcs

@@ -1,0 +1,87 @@
+// async.cuh -- asynchronous copies and mbarriers (sm_100a, CTA scope),
+// shared by the GEMV and attention kernels.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace slm {
+
+// 16-byte global -> shared copy through the LSU (cp.async, L2 only).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---- mbarriers and bulk (TMA) copies ------------------------------------
+__device__ __forceinline__ unsigned smem_addr(const void *p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of `bar`, giving up after ~1 s (2e9 cycles) or as
+// soon as another thread of the CTA gave up (*abort set): on a timeout the
+// thread sets *abort and the kernel's error flag, and returns false.
+constexpr long long WAIT_LIMIT = 2000000000LL;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
+                                          int32_t *err) {
+    const long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - t0 > WAIT_LIMIT) {
+            *abort = 1;
+            if (err) atomicExch(err, 3);
+            return false;
+        }
+    }
+    return true;
+}
+// One row copy global -> shared through the TMA engine, completing bytes on bar.
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// One tile (box) of a 3-D tensor map global -> shared through the TMA
+// engine, completing its bytes on bar.  x is a multiple of 4 floats (16 B).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+}  // namespace slm

@@ -153,4 +153,36 @@ __device__ __forceinline__ void q8x_store_block(float v, Q8X out, size_t blk, in
     if (lane == 0) out.d[blk] = __half2float(__float2half_rn(d));
 }
 
+// One thread quantizes a whole block: v(i) gives element i of the block
+// (i = 0..31; called twice per element), the result lands in Q8X block blk.
+// Same bytes as q8x_store_block: amax over |v| (order-free), d = amax/127,
+// id = 127/amax (0 for amax == 0), q = clamp(round(v*id)), lane constant k
+// from elements 4k..4k+3, f16-rounded d.  The 16-byte groups are visited
+// starting at `rot` (0..7) so that threads of a warp working on different
+// blocks spread over the shared-memory banks.
+template <typename F>
+__device__ __forceinline__ void q8x_store_block_thread(F v, Q8X out, size_t blk, int rot) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int g = (u + rot) & 7;
+#pragma unroll
+        for (int e = 0; e < 4; e++) amax = fmaxf(amax, fabsf(v(4 * g + e)));
+    }
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int g = (u + rot) & 7;
+        int q[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) q[e] = q8_round(__fmul_rn(v(4 * g + e), id));
+        const unsigned word = (unsigned)(q[0] & 0xff) | ((unsigned)(q[1] & 0xff) << 8) |
+                              ((unsigned)(q[2] & 0xff) << 16) | ((unsigned)(q[3] & 0xff) << 24);
+        reinterpret_cast<unsigned *>(out.qs + blk * 32)[g] = word;
+        out.c[blk * 8 + g] = MAGIC_I - 8 * (q[0] + q[1] + q[2] + q[3]);
+    }
+    out.d[blk] = __half2float(__float2half_rn(d));
+}
+
 }  // namespace slm

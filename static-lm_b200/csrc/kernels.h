@@ -85,8 +85,19 @@ struct GemvArgs {
     size_t ld_res;
     Q8X q8_out;              // EPI_SWIGLU_Q8 destination (nb_out = h/32 blocks per row)
     QkvArgs qkv;
+    // Fused RMSNorm prologue (graph.rs:141-155): when nx is set, the
+    // activations are rmsnorm(nx rows, nw, eps) quantized to Q8_0 inside the
+    // kernel and `x` is not read.  Only valid when gemv_fuses_norm() is true.
+    const float *nx;
+    size_t ld_nx;
+    const float *nw;
+    float eps, inv_n;
+    int32_t *err;            // set to 3 when a bounded copy wait gave up (may be null)
 };
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
+// Whether launch_gemv stages whole weight tiles for this shape (and can then
+// run the RMSNorm prologue); false for tiles too large for shared memory.
+bool gemv_fuses_norm(int rows, int nb, int epi, int batch);
 // Opt the GEMV kernels into `bytes` of dynamic shared memory (current device).
 void set_gemv_smem_limit(int bytes);
 
@@ -112,8 +123,10 @@ struct AttnArgs {
     // fused path: V plane of row r in the tensor map = slot*z_slot + z_layer
     long long z_slot, z_layer;
 };
-// vmap: the V tensor map of encode_v_map, or null for the three-phase path
-void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, cudaStream_t s);
+// vmap: the V tensor map of encode_v_map, or null for the three-phase path;
+// kmap: the K tensor map of encode_k_map, or null (per-row K copies)
+void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
+                      cudaStream_t s);
 // the three phases of launch_attention, for callers that time them apart
 void launch_attn_scores(const AttnArgs &a, cudaStream_t s);
 void launch_attn_softmax(const AttnArgs &a, cudaStream_t s);
@@ -124,12 +137,17 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
 // (head_dim % 4 and <= 224, kv_mul <= 8, 16-byte bases, scores fit in
 // shared memory).
 bool attention_fused_ok(const AttnArgs &a);
-void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s);
+void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
+                       cudaStream_t s);
 // 3-D tensor map over `planes` consecutive [max_seq][kv_dim] f32 planes from
 // `base`, box = head_dim floats x 64 positions x 1 plane.  False when the
 // driver entry point is missing or the shape is not expressible (the caller
 // then uses the three-phase path).
 bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
+                  uint64_t planes, int head_dim);
+// The same planes for K, box = 32 floats x 128 positions with the 128-byte
+// swizzle (head_dim % 32 == 0 only).
+bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
                   uint64_t planes, int head_dim);
 // Opt the attention kernels into `bytes` of dynamic shared memory (current device).
 void set_attention_smem_limit(int bytes);

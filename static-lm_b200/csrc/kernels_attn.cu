@@ -28,6 +28,7 @@
 // Decode is the case of one row per sequence; prefill is rows = tokens with
 // p = start_pos + i, which reproduces the reference's per-token loop
 // (transformer.rs:563-593) exactly.
+#include "async.cuh"
 #include "kernels.h"
 
 namespace slm {
@@ -199,17 +200,6 @@ __global__ void __launch_bounds__(1024) attn_pv_kernel(AttnArgs a) {
 // the three-kernel path above, so results are identical.
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
-    unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
-
 // Fused path: V comes through a 3-D tensor map over the cache planes
 // (x = kv_dim floats, y = positions, z = plane), one TMA box of TT_V rows x
 // head_dim floats per stage.
@@ -230,72 +220,6 @@ __host__ __device__ inline FusedShape fused_shape(int kv_mul, int hd, int max_le
                               (size_t)kv_mul * hd + 64 + 8 * 32) +
              128;
     return f;
-}
-
-// ---- mbarriers and bulk (TMA) copies, CTA scope ------------------------
-__device__ __forceinline__ unsigned smem_addr(const void *p) {
-    return (unsigned)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_fence_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
-    unsigned ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for phase `parity` of `bar`, giving up after ~1 s (2e9 cycles) or as
-// soon as another thread of the CTA gave up (*abort set): on a timeout the
-// thread sets *abort and the kernel's error flag, and returns false.
-constexpr long long WAIT_LIMIT = 2000000000LL;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
-                                          int32_t *err) {
-    const long long t0 = clock64();
-    while (!mbar_test(bar, parity)) {
-        if (*abort) return false;
-        if (clock64() - t0 > WAIT_LIMIT) {
-            *abort = 1;
-            if (err) atomicExch(err, 3);
-            return false;
-        }
-    }
-    return true;
-}
-// One row copy global -> shared through the TMA engine, completing bytes on bar.
-__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
-                                          uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
-            "r"(smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// One tile (box) of a 3-D tensor map global -> shared through the TMA
-// engine, completing its bytes on bar.  x is a multiple of 4 floats (16 B).
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
-                                            uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-        : "memory");
 }
 
 // (A) scores: one CTA per (128 keys, KV head, row).  The 128 K rows go
@@ -363,6 +287,87 @@ __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a
                     dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.y, kk.y));
                     dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.z, kk.z));
                     dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.w, kk.w));
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (u < nh) att[(size_t)(h0 + u) * a.att_ld] = __fmul_rn(dot[u], a.scale);
+    }
+}
+
+// (A') scores with K through a tensor map: the same CTA shape and chains as
+// (A), but the 128 K rows x head_dim floats arrive as head_dim/32 TMA boxes of
+// [128 rows][32 floats] in the 128-byte swizzled layout (16-byte chunk c of
+// row t stored at chunk c ^ (t & 7)), one instruction per box instead of one
+// bulk copy per row.  Thread t reads its row's chunks through the same XOR,
+// so the eight rows of a quarter-warp hit eight different bank groups.
+__global__ void __launch_bounds__(TILE_KEYS)
+    attn_scores_tma_kernel(AttnArgs a, const __grid_constant__ CUtensorMap kmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int s_abort;
+    // swizzled TMA destinations must be 1024-byte aligned (1 KB of slack)
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int r = blockIdx.z, g = blockIdx.y;
+    const int kv_mul = a.num_heads / a.num_kv_heads;
+    const int hd = a.head_dim, nbox = hd >> 5;
+    const int L = row_len(a, r);
+    const int t0 = blockIdx.x * TILE_KEYS;
+    if (t0 >= L) return;  // CTA-uniform
+    const int nrows = L - t0 < TILE_KEYS ? L - t0 : TILE_KEYS;
+    const unsigned char *s_k = base;                                          // [nbox][128][128 B]
+    float *s_q = reinterpret_cast<float *>(base + (size_t)nbox * TILE_KEYS * 128);  // [kv_mul][hd]
+    const int kz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, (unsigned)nbox * TILE_KEYS * 128u);
+        for (int b = 0; b < nbox; b++)
+            tma_load_3d(const_cast<unsigned char *>(s_k) + (size_t)b * TILE_KEYS * 128, &kmap,
+                        g * hd + 32 * b, t0, kz, &bar);
+    }
+    const float *qr = a.q + (size_t)r * a.ldq + (size_t)g * kv_mul * hd;
+    for (int i = threadIdx.x; i < kv_mul * hd; i += TILE_KEYS) s_q[i] = qr[i];
+    const bool ok = mbar_wait(&bar, 0, &s_abort, a.err);
+    __syncthreads();
+    if (!ok || s_abort) {
+        // bounded drain of the copies in flight before the shared memory goes away
+        if (threadIdx.x == 0) {
+            const long long tw = clock64();
+            while (!mbar_test(&bar, 0) && clock64() - tw < WAIT_LIMIT) {
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    const int t = threadIdx.x;
+    if (t >= nrows) return;
+    const unsigned sw = (unsigned)(t & 7);
+    float *att = a.att + ((size_t)r * a.num_heads + (size_t)g * kv_mul) * a.att_ld + t0 + t;
+    for (int h0 = 0; h0 < kv_mul; h0 += 4) {
+        const int nh = kv_mul - h0 < 4 ? kv_mul - h0 : 4;
+        float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float4 *q4 = reinterpret_cast<const float4 *>(s_q + h0 * hd);
+        for (int b = 0; b < nbox; b++) {
+            const unsigned char *row = s_k + (size_t)b * TILE_KEYS * 128 + (size_t)t * 128;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const float4 kk = *reinterpret_cast<const float4 *>(row + ((c ^ sw) << 4));
+                const int v = b * 8 + c;  // float4 index within the head
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (u < nh) {
+                        const float4 qq = q4[u * (hd >> 2) + v];
+                        dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.x, kk.x));
+                        dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.y, kk.y));
+                        dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.z, kk.z));
+                        dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.w, kk.w));
+                    }
                 }
             }
         }
@@ -711,6 +716,21 @@ bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
+                  uint64_t planes, int head_dim) {
+    const EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || !base || ((uintptr_t)base & 15) || (kv_dim & 3) || (head_dim & 31) ||
+        head_dim > kv_dim || max_seq <= 0 || planes == 0 || planes > 0x7fffffffULL)
+        return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kv_dim, (cuuint64_t)max_seq, (cuuint64_t)planes};
+    const cuuint64_t strides[2] = {(cuuint64_t)kv_dim * 4, (cuuint64_t)kv_dim * 4 * (cuuint64_t)max_seq};
+    const cuuint32_t box[3] = {32, (cuuint32_t)TILE_KEYS, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool attention_fused_ok(const AttnArgs &a) {
     const int kv_mul = a.num_heads / a.num_kv_heads;
     if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 992) return false;
@@ -721,12 +741,19 @@ bool attention_fused_ok(const AttnArgs &a) {
     return fused_shape(kv_mul, a.head_dim, a.max_len).smem <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
 }
 
-void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s) {
+void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
+                       cudaStream_t s) {
     if (a.rows <= 0) return;
     const int kv_mul = a.num_heads / a.num_kv_heads;
-    const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
     dim3 g1((a.max_len + TILE_KEYS - 1) / TILE_KEYS, a.num_kv_heads, a.rows);
-    attn_scores_tiled_kernel<<<g1, TILE_KEYS, sk, s>>>(a);
+    if (kmap && a.head_dim % 32 == 0) {
+        const size_t sk = (size_t)(a.head_dim / 32) * TILE_KEYS * 128 +
+                          sizeof(float) * (size_t)kv_mul * a.head_dim + 1024;
+        attn_scores_tma_kernel<<<g1, TILE_KEYS, sk, s>>>(a, *kmap);
+    } else {
+        const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
+        attn_scores_tiled_kernel<<<g1, TILE_KEYS, sk, s>>>(a);
+    }
     switch (kv_mul) {
         case 1: launch_softmax_pv<1>(a, vmap, s); break;
         case 2: launch_softmax_pv<2>(a, vmap, s); break;
@@ -749,6 +776,7 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<7>(bytes);
     set_softmax_pv_smem<8>(bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
@@ -772,9 +800,10 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s) {
     attn_pv_kernel<<<g, 32 * kv_mul, 0, s>>>(a);
 }
 
-void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, cudaStream_t s) {
+void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
+                      cudaStream_t s) {
     if (vmap && attention_fused_ok(a)) {
-        launch_attn_fused(a, *vmap, s);
+        launch_attn_fused(a, *vmap, kmap, s);
         return;
     }
     launch_attn_scores(a, s);

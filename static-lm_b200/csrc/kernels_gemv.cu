@@ -22,18 +22,138 @@
 // the activation bytes, seeded with c_k = 0x4B400000 - 8*sum(a): the result
 // is the bit pattern of 12582912 + isum_k, so isum_k as f32 costs one exact
 // subtraction instead of an int->float conversion.
+#include "async.cuh"
 #include "kernels.h"
 
 namespace slm {
 
 namespace {
 
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
-    unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc));
+constexpr int JC = 64;   // activation blocks per shared-memory chunk (multiple of PF)
+
+// One weight block j of RPT tiles (lane = row) against BT activation blocks:
+// acc[t][b][k] = fma(dw*da, isum_k, acc[t][b][k]) for the 8 lanes k.
+// slot[t] points at the block's 576 bytes; qs/c/d at activation row 0's block,
+// rows `astride` blocks apart.
+template <int RPT, int BT>
+__device__ __forceinline__ void block_dot(float (&acc)[RPT][BT][8], const uint8_t *const (&slot)[RPT],
+                                          const int8_t *qs, const int32_t *c, const float *d,
+                                          int astride, int lane) {
+    unsigned lo[RPT][4], hi[RPT][4];
+    float dw[RPT];
+#pragma unroll
+    for (int t = 0; t < RPT; t++) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(slot[t] + lane * 16);
+        dw[t] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(slot[t] + 512 + lane * 2)));
+        const unsigned qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            lo[t][k] = qw[k] & 0x0F0F0F0Fu;
+            hi[t][k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < BT; b++) {
+        const int4 a0 = reinterpret_cast<const int4 *>(qs + (size_t)b * astride * 32)[0];
+        const int4 a1 = reinterpret_cast<const int4 *>(qs + (size_t)b * astride * 32)[1];
+        const int4 c0 = reinterpret_cast<const int4 *>(c + (size_t)b * astride * 8)[0];
+        const int4 c1 = reinterpret_cast<const int4 *>(c + (size_t)b * astride * 8)[1];
+        const float da = d[(size_t)b * astride];
+        const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int t = 0; t < RPT; t++) {
+            const float dd = __fmul_rn(dw[t], da);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
+                acc[t][b][k] = __fmaf_rn(dd, f0, acc[t][b][k]);
+                float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
+                acc[t][b][4 + k] = __fmaf_rn(dd, f1, acc[t][b][4 + k]);
+            }
+        }
+    }
 }
 
-constexpr int JC = 64;   // activation blocks per shared-memory chunk (multiple of PF)
+// The reduction of the 8 lane accumulators and the fused epilogues
+// (store / residual / RoPE + KV append / SwiGLU + Q8) for one warp.
+template <int RPT, int BT, int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs &a, const float (&acc)[RPT][BT][8],
+                                              const int (&tile)[RPT], int total_tiles, int b0,
+                                              int lane) {
+    float y[RPT][BT];
+#pragma unroll
+    for (int t = 0; t < RPT; t++)
+#pragma unroll
+        for (int b = 0; b < BT; b++) {
+            float s0 = __fadd_rn(acc[t][b][0], acc[t][b][4]);
+            float s1 = __fadd_rn(acc[t][b][1], acc[t][b][5]);
+            float s2 = __fadd_rn(acc[t][b][2], acc[t][b][6]);
+            float s3 = __fadd_rn(acc[t][b][3], acc[t][b][7]);
+            y[t][b] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+        }
+
+    if constexpr (EPI == EPI_SWIGLU_Q8) {
+        const int hdim = (total_tiles / 2) * TILE_ROWS;
+        const int nb_out = hdim / 32;
+        const int hrow = tile[0] * TILE_ROWS + lane;
+#pragma unroll
+        for (int b = 0; b < BT; b++) {
+            const int bb = b0 + b;
+            if (bb >= a.batch) break;  // warp-uniform
+            float o = swiglu1(y[0][b], y[RPT - 1][b]);
+            if (a.out) a.out[(size_t)bb * a.ld_out + hrow] = o;
+            q8x_store_block(o, a.q8_out, (size_t)bb * nb_out + tile[0], lane);
+        }
+    } else {
+        const int row = tile[0] * TILE_ROWS + lane;
+#pragma unroll
+        for (int b = 0; b < BT; b++) {
+            const int bb = b0 + b;
+            if (bb >= a.batch) break;  // warp-uniform
+            const float v = y[0][b];
+            if constexpr (EPI == EPI_STORE) {
+                if (row < a.rows) a.out[(size_t)bb * a.ld_out + row] = v;
+            } else if constexpr (EPI == EPI_RESIDUAL) {
+                if (row < a.rows)
+                    a.out[(size_t)bb * a.ld_out + row] =
+                        __fadd_rn(a.res[(size_t)bb * a.ld_res + row], v);
+            } else if constexpr (EPI == EPI_QKV) {
+                const QkvArgs &q = a.qkv;
+                // RoPE pairs (2j, 2j+1) sit in lanes (2j, 2j+1) of the same tile
+                const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+                const int p = q.pos[bb];
+                if (p < 0 || p >= q.max_seq) {  // never write outside the cache
+                    if (lane == 0 && q.err) atomicExch(q.err, 2);
+                    continue;
+                }
+                if (row < q.dim + q.kv_dim) {
+                    const int local = row < q.dim ? row : row - q.dim;
+                    const int i = local % q.head_dim;
+                    const int jj = i >> 1;
+                    const int half = q.head_dim >> 1;
+                    const float cc = q.rope_cos[(size_t)p * half + jj];
+                    const float ss = q.rope_sin[(size_t)p * half + jj];
+                    float r;
+                    if ((i & 1) == 0)  // v0*c - v1*s
+                        r = __fsub_rn(__fmul_rn(v, cc), __fmul_rn(partner, ss));
+                    else  // v0*s + v1*c
+                        r = __fadd_rn(__fmul_rn(partner, ss), __fmul_rn(v, cc));
+                    if (row < q.dim) {
+                        q.q[(size_t)bb * q.ldq + row] = r;
+                    } else {
+                        float *kb = q.k_base + (size_t)q.slot[bb] * q.slot_stride + q.layer_off;
+                        kb[(size_t)p * q.kv_dim + local] = r;
+                    }
+                } else if (row < q.dim + 2 * q.kv_dim) {
+                    const int local = row - q.dim - q.kv_dim;
+                    float *vb = q.v_base + (size_t)q.slot[bb] * q.slot_stride + q.layer_off;
+                    vb[(size_t)p * q.kv_dim + local] = v;
+                }
+            }
+        }
+    }
+}
 
 template <int BT, int EPI>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, int units) {
@@ -119,120 +239,199 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a, int total_tiles, 
             fetch(j + PF - 1);
             asm volatile("cp.async.wait_group %0;\n" ::"n"(PF - 1));
             __syncwarp();
-            unsigned lo[RPT][4], hi[RPT][4];
-            float dw[RPT];
+            const uint8_t *slots[RPT];
 #pragma unroll
-            for (int t = 0; t < RPT; t++) {
-                const uint8_t *slot = s_w + (t * PF + j % PF) * TILE_BYTES;
-                const uint4 q = *reinterpret_cast<const uint4 *>(slot + lane * 16);
-                dw[t] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(slot + 512 + lane * 2)));
-                const unsigned qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    lo[t][k] = qw[k] & 0x0F0F0F0Fu;
-                    hi[t][k] = (qw[k] >> 4) & 0x0F0F0F0Fu;
-                }
-            }
+            for (int t = 0; t < RPT; t++) slots[t] = s_w + (t * PF + j % PF) * TILE_BYTES;
+            block_dot<RPT, BT>(acc, slots, s_qs + jl * 32, s_c + jl * 8, s_d + jl, JC, lane);
             __syncwarp();  // the slot may be refilled by the next fetch
-#pragma unroll
-            for (int b = 0; b < BT; b++) {
-                const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[0];
-                const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (b * JC + jl) * 32)[1];
-                const int4 c0 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[0];
-                const int4 c1 = reinterpret_cast<const int4 *>(s_c + (b * JC + jl) * 8)[1];
-                const float da = s_d[b * JC + jl];
-                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                for (int t = 0; t < RPT; t++) {
-                    const float d = __fmul_rn(dw[t], da);
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        float f0 = __fsub_rn(__int_as_float(dp4a_us(lo[t][k], av[k], cv[k])), MAGIC_F);
-                        acc[t][b][k] = __fmaf_rn(d, f0, acc[t][b][k]);
-                        float f1 = __fsub_rn(__int_as_float(dp4a_us(hi[t][k], av[4 + k], cv[4 + k])), MAGIC_F);
-                        acc[t][b][4 + k] = __fmaf_rn(d, f1, acc[t][b][4 + k]);
-                    }
-                }
-            }
         }
     }
     asm volatile("cp.async.wait_group 0;\n" ::);
     if (!live) return;
+    gemv_epilogue<RPT, BT, EPI>(a, acc, tile, total_tiles, b0, lane);
+}
 
-    // ---- epilogue
-    float y[RPT][BT];
+// Staged GEMV: one CTA per (unit = RPT weight tiles, group of NW*BT
+// activation rows), NW warps, warp w owning activation rows w*BT..w*BT+BT-1
+// of the group.  The unit's whole tiles (nb blocks each, contiguous in the
+// repacked layout) go global -> shared as TMA bulk copies and every warp of
+// the CTA reuses them, so the kernel pays one memory latency instead of one
+// per PF blocks and reads each tile once per row group.  The activation rows
+// complete first on their own mbarrier: as Q8X blocks, or with NORM as f32
+// rows that each warp turns into RMSNorm(x)*w (graph.rs:141-155: four lane
+// chains of x*x, (l0+l1)+(l2+l3), 1/sqrt(mean+eps)) quantized to Q8_0 while
+// the weights are still in flight -- which replaces a separate RMSNorm launch
+// and its round trip through global memory.  Both waits are bounded.
+constexpr size_t STAGED_SMEM_MAX = 200 * 1024;
+constexpr int STAGED_MAX_WARPS = 8;
+
+__host__ __device__ inline size_t staged_smem(int rpt, int rows, int nb, bool norm) {
+    size_t s = (size_t)rpt * nb * TILE_BYTES + (size_t)rows * nb * 68;
+    if (norm) s += sizeof(float) * ((size_t)(rows + 1) * nb * 32 + 2 * STAGED_MAX_WARPS * 4 + 4);
+    return s;
+}
+
+template <int BT, int EPI, bool NORM>
+__global__ void __launch_bounds__(32 * STAGED_MAX_WARPS) gemv_staged_kernel(GemvArgs a, int total_tiles) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bar_rows, bar_w;
+    __shared__ int s_abort;
+    const int nb = a.nb, n = nb * 32;
+    const int nw = blockDim.x >> 5;
+    const int grows = nw * BT;  // activation rows of the group
+    const int tile_bytes = nb * TILE_BYTES;
+    uint8_t *s_w = smem;                                            // [RPT][nb*576]
+    int8_t *s_qs = (int8_t *)(smem + (size_t)RPT * tile_bytes);     // [grows][nb][32]
+    int32_t *s_c = (int32_t *)(s_qs + (size_t)grows * nb * 32);     // [grows][nb][8]
+    float *s_d = (float *)(s_c + (size_t)grows * nb * 8);           // [grows][nb]
+    // NORM: [grows][n] rows, [n] weights, [grows] rms; 16-byte aligned for cp.async
+    float *s_x = s_d + ((grows * nb + 3) & ~3);
+    float *s_nw = s_x + (size_t)grows * n;
+    float *s_rms = s_nw + n;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int unit = blockIdx.x;
+    const int g0 = blockIdx.y * grows;     // first activation row of the group
+    const int b0 = g0 + warp * BT;         // this warp's first row
+    int tile[RPT];
+    tile[0] = unit;
+    if (RPT == 2) tile[RPT - 1] = unit + total_tiles / 2;
+
+    // One thread puts every copy on the TMA engine (bulk copies, no LSU
+    // work): the group's activation rows on bar_rows, the unit's weight
+    // tiles on bar_w.  Rows past the batch are padding written by the threads.
+    if (threadIdx.x == 0) {
+        mbar_init(&bar_rows, 1);
+        mbar_init(&bar_w, 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const int valid = a.batch - g0 < grows ? a.batch - g0 : grows;
+    if (threadIdx.x == 0) {
+        if constexpr (NORM) {
+            mbar_arrive_expect_tx(&bar_rows, (unsigned)(valid + 1) * (unsigned)n * 4u);
+            for (int rb = 0; rb < valid; rb++)
+                bulk_copy(s_x + (size_t)rb * n, a.nx + (size_t)(g0 + rb) * a.ld_nx, (unsigned)n * 4u,
+                          &bar_rows);
+            bulk_copy(s_nw, a.nw, (unsigned)n * 4u, &bar_rows);
+        } else {
+            mbar_arrive_expect_tx(&bar_rows, (unsigned)valid * (unsigned)nb * 64u);
+            for (int rb = 0; rb < valid; rb++) {
+                const size_t blk = (size_t)(g0 + rb) * nb;
+                bulk_copy(s_qs + (size_t)rb * nb * 32, a.x.qs + blk * 32, (unsigned)nb * 32u, &bar_rows);
+                bulk_copy(s_c + (size_t)rb * nb * 8, a.x.c + blk * 8, (unsigned)nb * 32u, &bar_rows);
+            }
+        }
+        mbar_arrive_expect_tx(&bar_w, (unsigned)RPT * (unsigned)tile_bytes);
+#pragma unroll
+        for (int t = 0; t < RPT; t++)
+            bulk_copy(s_w + (size_t)t * tile_bytes, a.w + tile_offset((size_t)tile[t], nb, 0),
+                      (unsigned)tile_bytes, &bar_w);
+    }
+    if constexpr (NORM) {
+        for (int i = threadIdx.x; i < (grows - valid) * n; i += blockDim.x) s_x[(size_t)valid * n + i] = 0.0f;
+    } else {
+        for (int i = threadIdx.x; i < (grows - valid) * nb * 8; i += blockDim.x) {
+            reinterpret_cast<int *>(s_qs + (size_t)valid * nb * 32)[i] = 0;
+            s_c[(size_t)valid * nb * 8 + i] = MAGIC_I;
+        }
+        for (int i = threadIdx.x; i < grows * nb; i += blockDim.x) {
+            const int rb = i / nb, j = i - rb * nb;
+            s_d[i] = rb < valid ? a.x.d[(size_t)(g0 + rb) * nb + j] : 0.0f;
+        }
+    }
+
+    if constexpr (NORM) {
+        mbar_wait(&bar_rows, 0, &s_abort, a.err);  // rows and norm weights landed
+        __syncthreads();
+        // each warp normalizes its own BT rows: lanes 4b..4b+3 run the four
+        // chains of row b
+        if (!s_abort) {
+            float acc = 0.0f;
+            const int rb = lane >> 2, l = lane & 3;
+            if (rb < BT) {
+                // n % 32 == 0: groups of 8 steps, the next group's loads in
+                // flight while the current one is added
+                const float *xr = s_x + (size_t)(warp * BT + rb) * n + l;
+                const int ng = n >> 5;
+                float cur[8], nxt[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) cur[u] = xr[4 * u];
+                for (int gi = 0; gi < ng; gi++) {
+                    if (gi + 1 < ng) {
+#pragma unroll
+                        for (int u = 0; u < 8; u++) nxt[u] = xr[32 * (gi + 1) + 4 * u];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, __fmul_rn(cur[u], cur[u]));
+#pragma unroll
+                    for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+                }
+            }
+            const float a1 = __shfl_down_sync(0xffffffffu, acc, 1);
+            const float a2 = __shfl_down_sync(0xffffffffu, acc, 2);
+            const float a3 = __shfl_down_sync(0xffffffffu, acc, 3);
+            if (rb < BT && l == 0) {
+                // n % 4 == 0: no tail
+                const float sum = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+                const float mean = __fmul_rn(sum, a.inv_n);
+                s_rms[warp * BT + rb] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+            }
+        }
+        __syncwarp();
+        // x*rms*w and its Q8_0: lane j quantizes block j of this warp's rows
+        // on its own (all blocks of a row in parallel)
+        Q8X sq;
+        sq.qs = s_qs;
+        sq.c = s_c;
+        sq.d = s_d;
+        for (int qi = lane; qi < (s_abort ? 0 : BT * nb); qi += 32) {
+            const int rb = qi / nb, j = qi - rb * nb;
+            const int row = warp * BT + rb;
+            const float *xr = s_x + (size_t)row * n + j * 32;
+            const float *wr = s_nw + j * 32;
+            const float rms = s_rms[row];
+            q8x_store_block_thread(
+                [&](int i) { return __fmul_rn(__fmul_rn(xr[i], rms), wr[i]); }, sq,
+                (size_t)row * nb + j, lane & 7);
+        }
+    }
+    if constexpr (!NORM) mbar_wait(&bar_rows, 0, &s_abort, a.err);
+    mbar_wait(&bar_w, 0, &s_abort, a.err);
+    __syncthreads();  // the weight tiles and the Q8X rows are visible to every warp
+    if (s_abort) {
+        // a wait gave up: let the copies in flight land (bounded) before the
+        // shared memory is released, and write nothing
+        if (threadIdx.x == 0) {
+            const long long tw = clock64();
+            while ((!mbar_test(&bar_rows, 0) || !mbar_test(&bar_w, 0)) && clock64() - tw < WAIT_LIMIT) {
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    if (b0 >= a.batch) return;  // warp-uniform: padding rows only
+
+    float acc[RPT][BT][8];
 #pragma unroll
     for (int t = 0; t < RPT; t++)
 #pragma unroll
-        for (int b = 0; b < BT; b++) {
-            float s0 = __fadd_rn(acc[t][b][0], acc[t][b][4]);
-            float s1 = __fadd_rn(acc[t][b][1], acc[t][b][5]);
-            float s2 = __fadd_rn(acc[t][b][2], acc[t][b][6]);
-            float s3 = __fadd_rn(acc[t][b][3], acc[t][b][7]);
-            y[t][b] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-        }
-
-    if constexpr (EPI == EPI_SWIGLU_Q8) {
-        const int hdim = (total_tiles / 2) * TILE_ROWS;
-        const int nb_out = hdim / 32;
-        const int hrow = tile[0] * TILE_ROWS + lane;
+        for (int b = 0; b < BT; b++)
 #pragma unroll
-        for (int b = 0; b < BT; b++) {
-            const int bb = b0 + b;
-            if (bb >= a.batch) break;  // warp-uniform
-            float o = swiglu1(y[0][b], y[RPT - 1][b]);
-            if (a.out) a.out[(size_t)bb * a.ld_out + hrow] = o;
-            q8x_store_block(o, a.q8_out, (size_t)bb * nb_out + tile[0], lane);
-        }
-    } else {
-        const int row = tile[0] * TILE_ROWS + lane;
+            for (int k = 0; k < 8; k++) acc[t][b][k] = 0.0f;
+    const int8_t *aq = s_qs + (size_t)warp * BT * nb * 32;
+    const int32_t *ac = s_c + (size_t)warp * BT * nb * 8;
+    const float *ad = s_d + (size_t)warp * BT * nb;
+#pragma unroll 2
+    for (int j = 0; j < nb; j++) {
+        const uint8_t *slots[RPT];
 #pragma unroll
-        for (int b = 0; b < BT; b++) {
-            const int bb = b0 + b;
-            if (bb >= a.batch) break;  // warp-uniform
-            const float v = y[0][b];
-            if constexpr (EPI == EPI_STORE) {
-                if (row < a.rows) a.out[(size_t)bb * a.ld_out + row] = v;
-            } else if constexpr (EPI == EPI_RESIDUAL) {
-                if (row < a.rows)
-                    a.out[(size_t)bb * a.ld_out + row] =
-                        __fadd_rn(a.res[(size_t)bb * a.ld_res + row], v);
-            } else if constexpr (EPI == EPI_QKV) {
-                const QkvArgs &q = a.qkv;
-                // RoPE pairs (2j, 2j+1) sit in lanes (2j, 2j+1) of the same tile
-                const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
-                const int p = q.pos[bb];
-                if (p < 0 || p >= q.max_seq) {  // never write outside the cache
-                    if (lane == 0 && q.err) atomicExch(q.err, 2);
-                    continue;
-                }
-                if (row < q.dim + q.kv_dim) {
-                    const int local = row < q.dim ? row : row - q.dim;
-                    const int i = local % q.head_dim;
-                    const int jj = i >> 1;
-                    const int half = q.head_dim >> 1;
-                    const float c = q.rope_cos[(size_t)p * half + jj];
-                    const float s = q.rope_sin[(size_t)p * half + jj];
-                    float r;
-                    if ((i & 1) == 0)  // v0*c - v1*s
-                        r = __fsub_rn(__fmul_rn(v, c), __fmul_rn(partner, s));
-                    else  // v0*s + v1*c
-                        r = __fadd_rn(__fmul_rn(partner, s), __fmul_rn(v, c));
-                    if (row < q.dim) {
-                        q.q[(size_t)bb * q.ldq + row] = r;
-                    } else {
-                        float *kb = q.k_base + (size_t)q.slot[bb] * q.slot_stride + q.layer_off;
-                        kb[(size_t)p * q.kv_dim + local] = r;
-                    }
-                } else if (row < q.dim + 2 * q.kv_dim) {
-                    const int local = row - q.dim - q.kv_dim;
-                    float *vb = q.v_base + (size_t)q.slot[bb] * q.slot_stride + q.layer_off;
-                    vb[(size_t)p * q.kv_dim + local] = v;
-                }
-            }
-        }
+        for (int t = 0; t < RPT; t++) slots[t] = s_w + (size_t)t * tile_bytes + (size_t)j * TILE_BYTES;
+        block_dot<RPT, BT>(acc, slots, aq + j * 32, ac + j * 8, ad + j, nb, lane);
     }
+    gemv_epilogue<RPT, BT, EPI>(a, acc, tile, total_tiles, b0, lane);
 }
 
 constexpr int TARGET_WARPS = 148 * 4;
@@ -246,15 +445,56 @@ void launch_bt(const GemvArgs &a, int total_tiles, int units, cudaStream_t s) {
     gemv_kernel<BT, EPI><<<grid, 128, smem, s>>>(a, total_tiles, units);
 }
 
+// Warps per staged CTA: the most (up to 8) that still gives every SM a CTA
+// (within 5%), so the weight tiles are shared by as many rows as the grid allows.
+inline int pick_nw(int units, int batch) {
+    for (int nw = STAGED_MAX_WARPS; nw > 1; nw >>= 1)
+        if ((long)units * ((batch + nw - 1) / nw) >= 140) return nw;
+    return 1;
+}
+
+template <int BT, int EPI, bool NORM>
+void launch_staged(const GemvArgs &a, int nw, int total_tiles, int units, cudaStream_t s) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    const int groups = (a.batch + nw * BT - 1) / (nw * BT);
+    dim3 grid((unsigned)units, (unsigned)groups);
+    gemv_staged_kernel<BT, EPI, NORM>
+        <<<grid, 32 * nw, staged_smem(RPT, nw * BT, a.nb, NORM), s>>>(a, total_tiles);
+}
+
+// the widest activation tile (<= 4) that still leaves enough warps
+inline int pick_bt(int units, int batch) {
+    auto warps = [&](int bt) { return (long)units * ((batch + bt - 1) / bt); };
+    if (batch >= 4 && warps(4) >= TARGET_WARPS) return 4;
+    if (batch >= 2 && warps(2) >= TARGET_WARPS) return 2;
+    return 1;
+}
+
+inline int units_of(int rows, int epi) {
+    const int total_tiles = (rows + TILE_ROWS - 1) / TILE_ROWS;
+    return epi == EPI_SWIGLU_Q8 ? total_tiles / 2 : total_tiles;
+}
+
 template <int EPI>
 void launch_epi(const GemvArgs &a, cudaStream_t s) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
-    const int units = EPI == EPI_SWIGLU_Q8 ? total_tiles / 2 : total_tiles;
-    // the widest activation tile (<= 4) that still leaves enough warps
-    auto warps = [&](int bt) { return (long)units * ((a.batch + bt - 1) / bt); };
-    if (a.batch >= 4 && warps(4) >= TARGET_WARPS)
+    const int units = units_of(a.rows, EPI);
+    const bool norm = a.nx != nullptr;
+    const int nw = pick_nw(units, a.batch);
+    if (staged_smem(RPT, nw, a.nb, norm) <= STAGED_SMEM_MAX) {
+        // one activation row per warp
+        if (norm)
+            launch_staged<1, EPI, true>(a, nw, total_tiles, units, s);
+        else
+            launch_staged<1, EPI, false>(a, nw, total_tiles, units, s);
+        return;
+    }
+    // tiles too large to stage whole: the weight-ring kernel (no norm prologue)
+    const int bt = pick_bt(units, a.batch);
+    if (bt == 4)
         launch_bt<4, EPI>(a, total_tiles, units, s);
-    else if (a.batch >= 2 && warps(2) >= TARGET_WARPS)
+    else if (bt == 2)
         launch_bt<2, EPI>(a, total_tiles, units, s);
     else
         launch_bt<1, EPI>(a, total_tiles, units, s);
@@ -265,6 +505,9 @@ void set_limits(int bytes) {
     cudaFuncSetAttribute(gemv_kernel<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(gemv_kernel<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(gemv_kernel<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    const int st = bytes < (int)STAGED_SMEM_MAX ? bytes : (int)STAGED_SMEM_MAX;
+    cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
+    cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
 }
 
 }  // namespace
@@ -274,6 +517,12 @@ void set_gemv_smem_limit(int bytes) {
     set_limits<EPI_RESIDUAL>(bytes);
     set_limits<EPI_QKV>(bytes);
     set_limits<EPI_SWIGLU_Q8>(bytes);
+}
+
+bool gemv_fuses_norm(int rows, int nb, int epi, int batch) {
+    const int rpt = epi == EPI_SWIGLU_Q8 ? 2 : 1;
+    const int units = units_of(rows, epi);
+    return staged_smem(rpt, pick_nw(units, batch), nb, true) <= STAGED_SMEM_MAX;
 }
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s) {

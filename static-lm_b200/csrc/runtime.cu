@@ -515,9 +515,11 @@ SLM_EXPORT int slm_causal_attention(const float *q, const float *k, const float 
     a.rows = 1;
     a.max_len = (int)pos + 1;
     // one [max_seq][kv_dim] plane of V: z = 0 for every row
-    CUtensorMap vmap;
+    CUtensorMap vmap, kmap;
     const bool have_map = encode_v_map(&vmap, v, a.kv_dim, a.max_seq, 1, a.head_dim);
-    launch_attention(a, have_map ? &vmap : nullptr, (cudaStream_t)stream);
+    const bool have_kmap = encode_k_map(&kmap, k, a.kv_dim, a.max_seq, 1, a.head_dim);
+    launch_attention(a, have_map ? &vmap : nullptr, have_kmap ? &kmap : nullptr,
+                     (cudaStream_t)stream);
     return launch_check("attention kernels");
 }
 
@@ -569,10 +571,12 @@ struct slm_model {
     bool use_graphs = true;
     bool use_fused_attention = true;
     bool split_decode = true;
+    bool fuse_norm = true;   // RMSNorm + Q8 inside the QKV and gate/up GEMVs
     cudaStream_t stream2 = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
-    bool have_vmap = false;
+    CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
+    bool have_vmap = false, have_kmap = false;
 };
 
 namespace {
@@ -640,6 +644,19 @@ inline void mark(Profiler *p, int ph) {
 // on stream `st` with the Q8 scratch pair `part` (0 or 1).  Rows of
 // different sequences are independent, so disjoint row ranges can run on
 // different streams at the same time.
+// Whether the QKV / gate-up GEMVs of an n-row step run the RMSNorm prologue
+// themselves (staged weight tiles fit in shared memory); otherwise a separate
+// RMSNorm + Q8 launch precedes them.  Activation rows are 16-byte aligned in
+// the arena (dim is a multiple of 32), as the prologue's cp.async requires.
+bool qkv_norm_fused(const slm_model *m, int n) {
+    return m->fuse_norm && gemv_fuses_norm((int)m->layers[0].wqkv.rows, (int)(m->cfg.dim / QK),
+                                           EPI_QKV, n);
+}
+bool gate_up_norm_fused(const slm_model *m, int n) {
+    return m->fuse_norm &&
+           gemv_fuses_norm(2 * (int)m->cfg.hidden_dim, (int)(m->cfg.dim / QK), EPI_SWIGLU_Q8, n);
+}
+
 void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, cudaStream_t st,
                      int part, Profiler *prof = nullptr) {
     const slm_config &c = m->cfg;
@@ -695,13 +712,25 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         const int kv_mul = (int)(c.num_heads / c.num_kv_heads);
         if ((kv_mul * m->hd) % 32 == 0) aa.q8_out = qb8;
     }
+    const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
+    const bool norm_gu = m->L > 0 && gate_up_norm_fused(m, n);
+    const float inv_d = 1.0f / (float)d;
     for (int l = 0; l < m->L; l++) {
         const LayerDev &ld = m->layers[l];
-        // rmsnorm(x) -> Q8 (transformer.rs:411, kernels.rs:301)
-        launch_rmsnorm_q8(x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
-        mark(prof, SLM_PHASE_RMSNORM);
-        // Wq/Wk/Wv + RoPE + KV append (transformer.rs:413-428)
+        // rmsnorm(x) -> Q8 (transformer.rs:411, kernels.rs:301), in the QKV
+        // GEMV's prologue when it stages whole tiles
         GemvArgs g{};
+        if (norm_qkv) {
+            g.nx = x;
+            g.ld_nx = d;
+            g.nw = ld.rms_att;
+            g.eps = c.rms_eps;
+            g.inv_n = inv_d;
+        } else {
+            launch_rmsnorm_q8(x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
+            mark(prof, SLM_PHASE_RMSNORM);
+        }
+        // Wq/Wk/Wv + RoPE + KV append (transformer.rs:413-428)
         g.w = ld.wqkv.tiles;
         g.rows = ld.wqkv.rows;
         g.nb = d / QK;
@@ -710,6 +739,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.epi = EPI_QKV;
         qa.layer_off = (size_t)l * m->layer_stride;
         g.qkv = qa;
+        g.err = m->d_err;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_QKV);
         // attention (transformer.rs:430-443)
@@ -717,7 +747,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         aa.z_layer = 2LL * l;
         if (fused) {
             // scores, then softmax + PV + the Q8_0 of the output
-            launch_attn_fused(aa, m->vmap, st);
+            launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
             if (!aa.q8_out.qs) {
                 launch_quantize_q8x(xb, d, d, qb8, n, st);
@@ -745,12 +775,21 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.ld_out = d;
         g.res = x;
         g.ld_res = d;
+        g.err = m->d_err;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_WO);
         // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
-        launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
-        mark(prof, SLM_PHASE_RMSNORM);
         g = GemvArgs{};
+        if (norm_gu) {
+            g.nx = x_mid;
+            g.ld_nx = d;
+            g.nw = ld.rms_ffn;
+            g.eps = c.rms_eps;
+            g.inv_n = inv_d;
+        } else {
+            launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
+            mark(prof, SLM_PHASE_RMSNORM);
+        }
         g.w = ld.wgu.tiles;
         g.rows = 2 * h;
         g.nb = d / QK;
@@ -758,6 +797,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.batch = n;
         g.epi = EPI_SWIGLU_Q8;
         g.q8_out = qb8;
+        g.err = m->d_err;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_GATE_UP);
         // down + residual (transformer.rs:477-486)
@@ -772,6 +812,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.ld_out = d;
         g.res = x_mid;
         g.ld_res = d;
+        g.err = m->d_err;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_DOWN);
     }
@@ -790,23 +831,27 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     g.epi = EPI_STORE;
     g.out = logits;
     g.ld_out = m->vocab;
+    g.err = m->d_err;
     launch_gemv(g, st);
     mark(prof, SLM_PHASE_LM_HEAD);
     launch_argmax(logits, m->vocab, m->vocab, next, rows, st);
     mark(prof, SLM_PHASE_ARGMAX);
 }
 
-// kernel launches of one decode step (enqueue_forward + the greedy advance)
-uint32_t decode_launches(const slm_model *m) {
-    // embed; per layer: rmsnorm, qkv, attention (1 fused, +1 quantize unless
-    // fused into it; or 3 + quantize), wo, rmsnorm, gate/up, down; final
-    // rmsnorm, lm_head, argmax; advance
+// kernel launches of one n-row decode part (enqueue_forward): embed; per
+// layer: [rmsnorm], qkv, attention (fused: scores + softmax/PV, + quantize
+// unless fused into it; or scores, softmax, pv, quantize), wo, [rmsnorm],
+// gate/up, down; final rmsnorm, lm_head, argmax
+uint32_t decode_launches(const slm_model *m, int n) {
     uint32_t attn = 4;
-    if (m->use_fused_attention) {
+    if (m->use_fused_attention && m->have_vmap) {
         const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
-        attn = ((kv_mul * m->hd) % 32 == 0) ? 1 : 2;
+        attn = ((kv_mul * m->hd) % 32 == 0) ? 2 : 3;
     }
-    return 1u + (6u + attn) * (uint32_t)m->L + 3u;
+    uint32_t per_layer = 4u + attn;
+    if (m->L > 0 && !qkv_norm_fused(m, n)) per_layer++;
+    if (m->L > 0 && !gate_up_norm_fused(m, n)) per_layer++;
+    return 1u + per_layer * (uint32_t)m->L + 3u;
 }
 
 // Decode rows split into two halves on two streams when the batch is large
@@ -900,7 +945,7 @@ void ensure_kernel_attributes() {
     if (dev < 31 && (done_mask & (1 << dev))) return;
     slm::set_attention_smem_limit(200 * 1024);
     slm::set_rmsnorm_smem_limit(200 * 1024);
-    slm::set_gemv_smem_limit(96 * 1024);
+    slm::set_gemv_smem_limit(200 * 1024);
     if (dev < 31) done_mask |= 1 << dev;
 }
 }  // namespace
@@ -1035,9 +1080,14 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->use_fused_attention = !(env && env[0] == '1');
     env = getenv("SLM_DECODE_ONE_STREAM");
     m->split_decode = !(env && env[0] == '1');
+    env = getenv("SLM_UNFUSED_NORM");
+    m->fuse_norm = !(env && env[0] == '1');
     // every V plane of the cache, addressed from the first one: plane
     // (slot, layer) sits at z = slot*2L + 2*layer, the last at S*2L - 2
     m->have_vmap = encode_v_map(&m->vmap, m->kv + m->v_off, m->kvd, (int)cfg->max_seq_len,
+                                (uint64_t)S * 2 * m->L - 1, m->hd);
+    // K plane (slot, layer) at z = slot*2L + 2*layer from the cache start
+    m->have_kmap = encode_k_map(&m->kmap, m->kv, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd);
     *out = m;
     return SLM_OK;
@@ -1276,7 +1326,10 @@ SLM_EXPORT int slm_model_read_hidden(slm_model *m, uint32_t row, float *host) {
 }
 
 SLM_EXPORT uint32_t slm_model_launches_per_decode_step(const slm_model *m, uint32_t n) {
-    return m ? decode_launches(m) * (uint32_t)decode_parts(m, (int)n) + 1u : 0;
+    if (!m || n == 0) return 0;
+    if (decode_parts(m, (int)n) == 1) return decode_launches(m, (int)n) + 1u;
+    const int h = (int)n / 2;
+    return decode_launches(m, h) + decode_launches(m, (int)n - h) + 1u;  // + advance
 }
 
 SLM_EXPORT int slm_model_kv_write_device(slm_model *m, uint32_t seq, uint32_t layer,

@@ -186,6 +186,30 @@ def test_fused_and_three_pass_attention_agree(cuda):
     assert fused.launches_per_decode_step(2) < three.launches_per_decode_step(2)
 
 
+def test_norm_fused_into_gemv_matches_separate_rmsnorm(cuda):
+    cfg, layers, vocab = synth.config("cfg2")
+    w = synth.synth_model(cfg, layers, vocab, seed=8)
+    os.environ["SLM_UNFUSED_NORM"] = "1"
+    try:
+        sep = S.Model(cfg, w, max_sequences=3, max_rows=32)
+    finally:
+        del os.environ["SLM_UNFUSED_NORM"]
+    fus = S.Model(cfg, w, max_sequences=3, max_rows=32)
+    assert fus.launches_per_decode_step(3) < sep.launches_per_decode_step(3)
+    for m in (sep, fus):
+        m.prefill_tokens(list(range(1, 20)), seq=0)
+        m.prefill_tokens([4, 5, 6], seq=1)
+        m.prefill_tokens([7], seq=2)
+    toks, pos = [11, 12, 13], [19, 3, 1]
+    for _ in range(3):
+        a = sep.decode_batch([0, 1, 2], toks, pos)
+        b = fus.decode_batch([0, 1, 2], toks, pos)
+        assert list(a) == list(b)
+        for r in range(3):
+            assert np.array_equal(sep.logits(r), fus.logits(r))
+        toks, pos = list(a), [p + 1 for p in pos]
+
+
 def test_cfg3_shape_prefilled_kv_decode(cuda):
     """SmolLM2-135M shape, KV rows 0..2047 from seeded N(0,1), two sequences,
     two decode steps at positions 2048 and 2049: logits bit-exact."""
