@@ -1,0 +1,94 @@
+"""Multi-rank host logic of the sequence-sharded decode (bench.py), on CPU
+with `gloo` ranks: the shards partition the batch, the job time is the max
+over ranks, and decoding each rank's shard on its own gives exactly the
+tokens of decoding the whole batch in one process (sequences are
+independent, so the sharded path needs no data-path collective)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import bench
+import oracle as O
+from static_lm import synth
+
+GLOBAL = 6
+STEPS = 3
+
+
+def _decode(cfg, w, vocab, gseqs):
+    """Greedy decode of the given global sequences, one oracle model each."""
+    out = {}
+    for g in gseqs:
+        m = O.Model(cfg, w, threads=1)
+        prompt = [int((g * 31 + i * 7 + 1) % vocab) for i in range(3 + g % 3)]
+        tok = m.prefill_tokens(prompt)
+        toks = [tok]
+        pos = len(prompt)
+        for _ in range(STEPS - 1):
+            tok = m.forward_token(tok, pos)
+            pos += 1
+            toks.append(tok)
+        out[g] = toks
+        m.close()
+    return out
+
+
+def _rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg, layers, vocab = synth.config("cfg1")
+        w = synth.synth_model(cfg, layers, vocab, seed=3)
+        mine = bench.shard_sequences(GLOBAL, world, rank)
+        toks = _decode(cfg, w, vocab, mine)
+        slowest = bench.max_over_ranks(torch, float(rank + 1), world)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, {"seqs": mine, "toks": toks, "max": slowest})
+        if rank == 0:
+            q.put(gathered)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shards_partition_the_batch():
+    for world in (1, 2, 3, 6):
+        shards = [bench.shard_sequences(GLOBAL, world, r) for r in range(world)]
+        flat = [g for sh in shards for g in sh]
+        assert sorted(flat) == list(range(GLOBAL)) and len(set(flat)) == GLOBAL
+        assert len({len(sh) for sh in shards}) == 1
+    with pytest.raises(SystemExit):
+        bench.shard_sequences(GLOBAL, 4, 0)
+
+
+def test_two_gloo_ranks_decode_their_shards_like_one_process():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    gathered = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(g["max"] == float(world) for g in gathered)
+    sharded = {}
+    for g in gathered:
+        sharded.update(g["toks"])
+    cfg, layers, vocab = synth.config("cfg1")
+    w = synth.synth_model(cfg, layers, vocab, seed=3)
+    whole = _decode(cfg, w, vocab, list(range(GLOBAL)))
+    assert sharded == whole
