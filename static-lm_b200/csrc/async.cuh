@@ -52,6 +52,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
 constexpr long long WAIT_LIMIT = 2000000000LL;
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
                                           int32_t *err) {
+    if (mbar_test(bar, parity)) return true;  // fast path: the phase is already complete
     const long long t0 = clock64();
     while (!mbar_test(bar, parity)) {
         if (*abort) return false;
@@ -82,6 +83,20 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------
+// A kernel launched with the programmatic-serialization attribute may start
+// while its predecessor in the stream is still running.  It runs only work
+// that does not depend on the predecessor (constant weights, shared-memory
+// set-up, data written two or more kernels back), then pdl_wait() (returns
+// once the predecessor has completed and its writes are visible; a no-op for
+// a normal launch), then pdl_release() so that its own successor may start.
+// Releasing only after the wait keeps "two kernels back" complete whenever a
+// successor starts.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
 }  // namespace slm

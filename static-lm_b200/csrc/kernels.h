@@ -6,9 +6,30 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace slm {
+
+// Launch `kernel` on `s`, with the programmatic-serialization attribute when
+// `pdl` (the kernel must then call pdl_wait() before reading its
+// predecessor's outputs).
+template <typename... KArgs, typename... Args>
+inline void launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t s, bool pdl, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- vector ops / quantization (kernels_vec.cu)
 // RMSNorm of `rows` rows (graph.rs:141-155) fused with Q8_0 quantization of the
@@ -93,6 +114,7 @@ struct GemvArgs {
     const float *nw;
     float eps, inv_n;
     int32_t *err;            // set to 3 when a bounded copy wait gave up (may be null)
+    bool pdl;                // launch with programmatic dependent launch (staged path)
 };
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
 // Whether launch_gemv stages whole weight tiles for this shape (and can then
@@ -122,6 +144,7 @@ struct AttnArgs {
     int32_t *err;            // set to 3 when a bounded wait gave up (may be null)
     // fused path: V plane of row r in the tensor map = slot*z_slot + z_layer
     long long z_slot, z_layer;
+    bool pdl;                // fused path: programmatic dependent launch
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)

@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(TILE_KEYS)
         mbar_fence_init();
     }
     __syncthreads();
+    pdl_wait();  // q and the K row at pos come from the QKV kernel
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, (unsigned)nbox * TILE_KEYS * 128u);
         for (int b = 0; b < nbox; b++)
@@ -345,6 +346,7 @@ __global__ void __launch_bounds__(TILE_KEYS)
         __syncthreads();
         return;
     }
+    pdl_release();
     const int t = threadIdx.x;
     if (t >= nrows) return;
     const unsigned sw = (unsigned)(t & 7);
@@ -374,6 +376,149 @@ __global__ void __launch_bounds__(TILE_KEYS)
 #pragma unroll
         for (int u = 0; u < 4; u++)
             if (u < nh) att[(size_t)(h0 + u) * a.att_ld] = __fmul_rn(dot[u], a.scale);
+    }
+}
+
+// (A'') scores, pipelined: a fixed grid of a few CTAs per SM walks the
+// (row, KV head, 128-key tile) items.  One producer warp loads each item's
+// row position and slot, then puts its K tile (head_dim/32 swizzled TMA boxes
+// as in (A')) and its query vectors (one bulk copy) into one of two stages;
+// four consumer warps compute the previous item meanwhile (thread t = key t,
+// kv_mul chains), so copy latency and the per-item set-up overlap compute
+// instead of being paid once per CTA.  FULL/EMPTY mbarriers per stage, all
+// waits bounded; an item with info.r < 0 ends the consumers' loop.
+constexpr int SCORE_STAGES = 2;
+constexpr int SCORE_CONS_WARPS = TILE_KEYS / 32;
+
+struct ScoreItem {
+    int r, g, t0, nrows;
+};
+
+__host__ __device__ inline size_t score_stage_bytes(int kv_mul, int hd) {
+    // K boxes, then the query vectors, 1 KB aligned
+    return ((size_t)(hd / 32) * TILE_KEYS * 128 + sizeof(float) * kv_mul * hd + 1023) / 1024 * 1024;
+}
+
+__global__ void __launch_bounds__(TILE_KEYS + 32)
+    attn_scores_pipe_kernel(AttnArgs a, int ntile_max, const __grid_constant__ CUtensorMap kmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar_full[SCORE_STAGES], bar_empty[SCORE_STAGES];
+    __shared__ ScoreItem s_item[SCORE_STAGES];
+    __shared__ int s_abort, s_issued;
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int kv_mul = a.num_heads / a.num_kv_heads;
+    const int hd = a.head_dim, nbox = hd >> 5;
+    const size_t stage_bytes = score_stage_bytes(kv_mul, hd);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const long long n_items = (long long)a.rows * a.num_kv_heads * ntile_max;
+    if (tid == 0) {
+        for (int st = 0; st < SCORE_STAGES; st++) {
+            mbar_init(&bar_full[st], 1);
+            mbar_init(&bar_empty[st], SCORE_CONS_WARPS);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_wait();  // q and the K row at pos come from the QKV kernel
+    pdl_release();
+
+    if (warp == SCORE_CONS_WARPS) {
+        // ---- producer
+        int n = 0;  // items handed to the consumers
+        for (long long it = blockIdx.x; ; it += gridDim.x) {
+            ScoreItem item{-1, 0, 0, 0};
+            if (it < n_items) {
+                const int k = (int)(it % ntile_max);
+                const long long rg = it / ntile_max;
+                item.g = (int)(rg % a.num_kv_heads);
+                item.r = (int)(rg / a.num_kv_heads);
+                const int L = row_len(a, item.r);
+                item.t0 = k * TILE_KEYS;
+                if (item.t0 >= L) continue;  // past this row's keys
+                item.nrows = L - item.t0 < TILE_KEYS ? L - item.t0 : TILE_KEYS;
+            }
+            const int st = n % SCORE_STAGES;
+            if (n >= SCORE_STAGES &&
+                !mbar_wait(&bar_empty[st], (unsigned)((n / SCORE_STAGES) - 1) & 1u, &s_abort, a.err))
+                break;
+            if (lane == 0) {
+                s_item[st] = item;
+                if (item.r < 0) {
+                    mbar_arrive(&bar_full[st]);  // end marker, no bytes
+                } else {
+                    unsigned char *dst = base + (size_t)st * stage_bytes;
+                    float *q_dst = reinterpret_cast<float *>(dst + (size_t)nbox * TILE_KEYS * 128);
+                    const int kz = (int)((long long)row_slot(a, item.r) * a.z_slot + a.z_layer);
+                    mbar_arrive_expect_tx(&bar_full[st],
+                                          (unsigned)nbox * TILE_KEYS * 128u + (unsigned)(kv_mul * hd) * 4u);
+                    for (int b = 0; b < nbox; b++)
+                        tma_load_3d(dst + (size_t)b * TILE_KEYS * 128, &kmap, item.g * hd + 32 * b,
+                                    item.t0, kz, &bar_full[st]);
+                    bulk_copy(q_dst, a.q + (size_t)item.r * a.ldq + (size_t)item.g * kv_mul * hd,
+                              (unsigned)(kv_mul * hd) * 4u, &bar_full[st]);
+                }
+                s_issued = n + 1;
+            }
+            __syncwarp();
+            n++;
+            if (item.r < 0) break;
+        }
+    } else {
+        // ---- consumers: thread t = key t0 + t of the current item
+        const unsigned sw = (unsigned)(tid & 7);
+        for (int n = 0; ; n++) {
+            const int st = n % SCORE_STAGES;
+            if (!mbar_wait(&bar_full[st], (unsigned)(n / SCORE_STAGES) & 1u, &s_abort, a.err)) break;
+            const ScoreItem item = s_item[st];
+            if (item.r < 0) break;
+            const unsigned char *s_k = base + (size_t)st * stage_bytes;
+            const float *s_q = reinterpret_cast<const float *>(s_k + (size_t)nbox * TILE_KEYS * 128);
+            if (tid < item.nrows) {
+                float *att = a.att + ((size_t)item.r * a.num_heads + (size_t)item.g * kv_mul) * a.att_ld +
+                             item.t0 + tid;
+                for (int h0 = 0; h0 < kv_mul; h0 += 4) {
+                    const int nh = kv_mul - h0 < 4 ? kv_mul - h0 : 4;
+                    float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    const float4 *q4 = reinterpret_cast<const float4 *>(s_q + h0 * hd);
+                    for (int b = 0; b < nbox; b++) {
+                        const unsigned char *row = s_k + (size_t)b * TILE_KEYS * 128 + (size_t)tid * 128;
+#pragma unroll
+                        for (int c = 0; c < 8; c++) {
+                            const float4 kk = *reinterpret_cast<const float4 *>(row + ((c ^ sw) << 4));
+                            const int v = b * 8 + c;  // float4 index within the head
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                if (u < nh) {
+                                    const float4 qq = q4[u * (hd >> 2) + v];
+                                    dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.x, kk.x));
+                                    dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.y, kk.y));
+                                    dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.z, kk.z));
+                                    dot[u] = __fadd_rn(dot[u], __fmul_rn(qq.w, kk.w));
+                                }
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+                        if (u < nh) att[(size_t)(h0 + u) * a.att_ld] = __fmul_rn(dot[u], a.scale);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[st]);
+        }
+    }
+    __syncthreads();
+    if (s_abort && tid == 0) {
+        // a wait gave up: let the copies already issued land (bounded)
+        const int n_iss = s_issued;
+        for (int k = n_iss - SCORE_STAGES < 0 ? 0 : n_iss - SCORE_STAGES; k < n_iss; k++) {
+            const long long t0 = clock64();
+            while (!mbar_test(&bar_full[k % SCORE_STAGES], (unsigned)(k / SCORE_STAGES) & 1u) &&
+                   clock64() - t0 < WAIT_LIMIT) {
+            }
+        }
     }
 }
 
@@ -434,6 +579,8 @@ __global__ void __launch_bounds__(1024)
         }
         s_issued = k;
     }
+    // V rows were written two kernels back (QKV), the scores by the previous one
+    pdl_wait();
 
     // scores of the KVM heads of this group (cp.async, awaited before the softmax)
     const float *att = a.att + ((size_t)r * a.num_heads + (size_t)g * KVM) * a.att_ld;
@@ -473,51 +620,48 @@ __global__ void __launch_bounds__(1024)
         }
         __syncthreads();
     }
-    // exp(s - max), four independent elements per iteration
-    for (int h = 0; h < KVM; h++) {
-        const float mx = s_red[32 + h];
-        float *row = s_sc + h * lp;
-        int t = tid;
-        for (; t + 3 * nth < L; t += 4 * nth) {
-            const float x0 = row[t], x1 = row[t + nth], x2 = row[t + 2 * nth], x3 = row[t + 3 * nth];
-            const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
-            const float e2 = exp_poly(__fsub_rn(x2, mx)), e3 = exp_poly(__fsub_rn(x3, mx));
-            row[t] = e0;
-            row[t + nth] = e1;
-            row[t + 2 * nth] = e2;
-            row[t + 3 * nth] = e3;
-        }
-        for (; t < L; t += nth) row[t] = exp_poly(__fsub_rn(row[t], mx));
-    }
-    __syncthreads();
-    // four lane chains per head over [0, L & ~3): the next 8 values are
-    // loaded before the current 8 are added
+    // exp(s - max) and the four lane sums of each head (graph.rs:168-179
+    // order), pipelined by segments of SEG positions: warp 0's lanes 4h..4h+3
+    // add segment k-1 while the other warps exponentiate segment k.  The lane
+    // chains cover [0, L & ~3) in order; the tail [L & ~3, L) is added after.
     const int vl = L & ~3;
-    if (tid < 4 * KVM) {
-        const int h = tid >> 2, l = tid & 3;
-        const float *e = s_sc + h * lp;
-        float acc = 0.0f;
-        int i = l;
-        float cur[8], nxt[8];
-        const int nfull = (vl - l + 3) / 4 / 8;  // full groups of 8 steps
-        if (nfull > 0) {
-#pragma unroll
-            for (int u = 0; u < 8; u++) cur[u] = e[i + 4 * u];
-            for (int gi = 0; gi < nfull; gi++) {
-                if (gi + 1 < nfull) {
-#pragma unroll
-                    for (int u = 0; u < 8; u++) nxt[u] = e[i + 32 + 4 * u];
+    constexpr int SEG = 256;
+    const int nseg = (L + SEG - 1) / SEG;
+    float chain = 0.0f;
+    for (int k = 0; k <= nseg; k++) {
+        if (warp > 0 && k < nseg) {
+            const int t0 = k * SEG, t1 = L - t0 < SEG ? L : t0 + SEG;
+            const int nwk = nth - 32;
+            for (int h = 0; h < KVM; h++) {
+                const float mx = s_red[32 + h];
+                float *row = s_sc + h * lp;
+                int t = t0 + tid - 32;
+                for (; t + nwk < t1; t += 2 * nwk) {
+                    const float x0 = row[t], x1 = row[t + nwk];
+                    const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
+                    row[t] = e0;
+                    row[t + nwk] = e1;
                 }
-#pragma unroll
-                for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, cur[u]);
-#pragma unroll
-                for (int u = 0; u < 8; u++) cur[u] = nxt[u];
-                i += 32;
+                for (; t < t1; t += nwk) row[t] = exp_poly(__fsub_rn(row[t], mx));
             }
         }
-        for (; i < vl; i += 4) acc = __fadd_rn(acc, e[i]);
-        s_red[tid] = acc;  // [0, 4*KVM) with KVM <= 8 stays below 32
+        if (warp == 0 && k > 0 && tid < 4 * KVM) {
+            const int h = tid >> 2, l = tid & 3;
+            const float *e = s_sc + h * lp;
+            const int t1 = (k * SEG < vl) ? k * SEG : vl;
+            int i = (k - 1) * SEG + l;
+            for (; i + 28 < t1; i += 32) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = e[i + 4 * u];
+#pragma unroll
+                for (int u = 0; u < 8; u++) chain = __fadd_rn(chain, v[u]);
+            }
+            for (; i < t1; i += 4) chain = __fadd_rn(chain, e[i]);
+        }
+        __syncthreads();
     }
+    if (tid < 4 * KVM) s_red[tid] = chain;  // [0, 4*KVM) with KVM <= 8 stays below 32
     __syncthreads();
     if (tid < KVM) {
         const float *e = s_sc + tid * lp;
@@ -527,12 +671,13 @@ __global__ void __launch_bounds__(1024)
         s_red[48 + tid] = __fdiv_rn(1.0f, sum);
     }
     __syncthreads();
-    for (int h = 0; h < KVM; h++) {
+    // p = e * (1/sum): stored (and written out) here only when the caller
+    // wants the probabilities; otherwise the PV loop multiplies on the fly
+    // (the same rounding) and this pass is skipped
+    for (int h = 0; h < (a.write_probs ? KVM : 0); h++) {
         const float inv = s_red[48 + h];
         float *row = s_sc + h * lp;
-        float *prow = a.write_probs
-                          ? a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld
-                          : nullptr;
+        float *prow = a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld;
         int t = tid;
         for (; t + 3 * nth < L; t += 4 * nth) {
             const float p0 = __fmul_rn(row[t], inv), p1 = __fmul_rn(row[t + nth], inv);
@@ -541,17 +686,15 @@ __global__ void __launch_bounds__(1024)
             row[t + nth] = p1;
             row[t + 2 * nth] = p2;
             row[t + 3 * nth] = p3;
-            if (prow) {
-                prow[t] = p0;
-                prow[t + nth] = p1;
-                prow[t + 2 * nth] = p2;
-                prow[t + 3 * nth] = p3;
-            }
+            prow[t] = p0;
+            prow[t + nth] = p1;
+            prow[t + 2 * nth] = p2;
+            prow[t + 3 * nth] = p3;
         }
         for (; t < L; t += nth) {
             const float pr = __fmul_rn(row[t], inv);
             row[t] = pr;
-            if (prow) prow[t] = pr;
+            prow[t] = pr;
         }
     }
 
@@ -576,6 +719,8 @@ __global__ void __launch_bounds__(1024)
         const bool active = tid < n_pairs;
         const int hl = tid / (hd >> 1), j2 = 2 * (tid - hl * (hd >> 1));
         float acc0 = 0.0f, acc1 = 0.0f;  // out[hl][j2], out[hl][j2 + 1]
+        // s_sc holds e (p = e * inv) unless the normalize pass ran (x 1.0 is exact)
+        const float inv = a.write_probs ? 1.0f : s_red[48 + (hl < KVM ? hl : 0)];
 #pragma unroll 1
         for (int k = 0; k < ntiles; k++) {
             if (!mbar_wait(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u, &s_abort,
@@ -591,6 +736,8 @@ __global__ void __launch_bounds__(1024)
                     // full tile: the loads of positions 4j+4..4j+7 are in
                     // flight while positions 4j..4j+3 are added
                     float4 pc = *reinterpret_cast<const float4 *>(pp);
+                    pc = make_float4(__fmul_rn(pc.x, inv), __fmul_rn(pc.y, inv), __fmul_rn(pc.z, inv),
+                                     __fmul_rn(pc.w, inv));
                     float2 vc[4];
 #pragma unroll
                     for (int u = 0; u < 4; u++) vc[u] = vt[u * hs];
@@ -600,6 +747,8 @@ __global__ void __launch_bounds__(1024)
                         float2 vn[4];
                         if (j + 1 < tt / 4) {
                             pn = *reinterpret_cast<const float4 *>(pp + 4 * j + 4);
+                            pn = make_float4(__fmul_rn(pn.x, inv), __fmul_rn(pn.y, inv),
+                                             __fmul_rn(pn.z, inv), __fmul_rn(pn.w, inv));
 #pragma unroll
                             for (int u = 0; u < 4; u++) vn[u] = vt[(4 * j + 4 + u) * hs];
                         }
@@ -619,7 +768,7 @@ __global__ void __launch_bounds__(1024)
                     }
                 } else {
                     for (int tl = 0; tl < nrows; tl++) {
-                        const float pr = pp[tl];
+                        const float pr = __fmul_rn(pp[tl], inv);
                         const float2 vv = vt[tl * hs];
                         acc0 = __fadd_rn(acc0, __fmul_rn(pr, vv.x));
                         acc1 = __fadd_rn(acc1, __fmul_rn(pr, vv.y));
@@ -651,6 +800,7 @@ __global__ void __launch_bounds__(1024)
         __syncthreads();
         return;
     }
+    pdl_release();  // the successor may start while the outputs are written
     float *orow = a.out + (size_t)r * a.ldo + (size_t)g * KVM * hd;
     for (int k = tid; k < KVM * hd; k += nth) orow[k] = s_out[k];
     // Q8_0 of the attention output for the Wo GEMV: this CTA owns the
@@ -671,7 +821,7 @@ void launch_softmax_pv(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t 
     // consumer warps (one thread per head and dim pair) plus the producer warp
     int nth = (KVM * (a.head_dim / 2) + 31) / 32 * 32 + 32;
     nth = nth < PV_THREADS ? PV_THREADS : nth;
-    attn_softmax_pv_kernel<KVM><<<grid, nth, f.smem, s>>>(a, f.lp, vmap);
+    launch_kernel(attn_softmax_pv_kernel<KVM>, grid, dim3(nth), f.smem, s, a.pdl, a, f.lp, vmap);
 }
 
 template <int KVM>
@@ -746,10 +896,21 @@ void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtenso
     if (a.rows <= 0) return;
     const int kv_mul = a.num_heads / a.num_kv_heads;
     dim3 g1((a.max_len + TILE_KEYS - 1) / TILE_KEYS, a.num_kv_heads, a.rows);
-    if (kmap && a.head_dim % 32 == 0) {
-        const size_t sk = (size_t)(a.head_dim / 32) * TILE_KEYS * 128 +
-                          sizeof(float) * (size_t)kv_mul * a.head_dim + 1024;
-        attn_scores_tma_kernel<<<g1, TILE_KEYS, sk, s>>>(a, *kmap);
+    // the pipelined kernel bulk-copies the query vectors: 16-byte aligned rows
+    const bool q_bulk = ((uintptr_t)a.q & 15) == 0 && (a.ldq & 3) == 0;
+    if (kmap && a.head_dim % 32 == 0 && q_bulk) {
+        // pipelined: a few CTAs per SM walk all (row, KV head, tile) items
+        const int ntile_max = (a.max_len + TILE_KEYS - 1) / TILE_KEYS;
+        const long long items = (long long)a.rows * a.num_kv_heads * ntile_max;
+        const size_t sk = SCORE_STAGES * score_stage_bytes(kv_mul, a.head_dim) + 1024;
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int per_sm = (int)((200 * 1024) / sk) < 3 ? (int)((200 * 1024) / sk) : 3;
+        long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
+        if (grid > items) grid = items;
+        launch_kernel(attn_scores_pipe_kernel, dim3((unsigned)grid), dim3(TILE_KEYS + 32), sk, s, a.pdl,
+                      a, ntile_max, *kmap);
     } else {
         const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
         attn_scores_tiled_kernel<<<g1, TILE_KEYS, sk, s>>>(a);
@@ -777,6 +938,7 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<8>(bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 

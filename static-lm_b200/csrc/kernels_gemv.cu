@@ -309,6 +309,15 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS) gemv_staged_kernel(Gemv
     }
     __syncthreads();
     const int valid = a.batch - g0 < grows ? a.batch - g0 : grows;
+    // constant data first: it may be fetched while the previous kernel runs
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar_w, (unsigned)RPT * (unsigned)tile_bytes);
+#pragma unroll
+        for (int t = 0; t < RPT; t++)
+            bulk_copy(s_w + (size_t)t * tile_bytes, a.w + tile_offset((size_t)tile[t], nb, 0),
+                      (unsigned)tile_bytes, &bar_w);
+    }
+    pdl_wait();  // the activation rows are the previous kernel's output
     if (threadIdx.x == 0) {
         if constexpr (NORM) {
             mbar_arrive_expect_tx(&bar_rows, (unsigned)(valid + 1) * (unsigned)n * 4u);
@@ -324,11 +333,6 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS) gemv_staged_kernel(Gemv
                 bulk_copy(s_c + (size_t)rb * nb * 8, a.x.c + blk * 8, (unsigned)nb * 32u, &bar_rows);
             }
         }
-        mbar_arrive_expect_tx(&bar_w, (unsigned)RPT * (unsigned)tile_bytes);
-#pragma unroll
-        for (int t = 0; t < RPT; t++)
-            bulk_copy(s_w + (size_t)t * tile_bytes, a.w + tile_offset((size_t)tile[t], nb, 0),
-                      (unsigned)tile_bytes, &bar_w);
     }
     if constexpr (NORM) {
         for (int i = threadIdx.x; i < (grows - valid) * n; i += blockDim.x) s_x[(size_t)valid * n + i] = 0.0f;
@@ -431,6 +435,7 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS) gemv_staged_kernel(Gemv
         for (int t = 0; t < RPT; t++) slots[t] = s_w + (size_t)t * tile_bytes + (size_t)j * TILE_BYTES;
         block_dot<RPT, BT>(acc, slots, aq + j * 32, ac + j * 8, ad + j, nb, lane);
     }
+    pdl_release();  // the successor may start while this epilogue runs
     gemv_epilogue<RPT, BT, EPI>(a, acc, tile, total_tiles, b0, lane);
 }
 
@@ -458,8 +463,8 @@ void launch_staged(const GemvArgs &a, int nw, int total_tiles, int units, cudaSt
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     const int groups = (a.batch + nw * BT - 1) / (nw * BT);
     dim3 grid((unsigned)units, (unsigned)groups);
-    gemv_staged_kernel<BT, EPI, NORM>
-        <<<grid, 32 * nw, staged_smem(RPT, nw * BT, a.nb, NORM), s>>>(a, total_tiles);
+    launch_kernel(gemv_staged_kernel<BT, EPI, NORM>, grid, dim3(32 * nw),
+                  staged_smem(RPT, nw * BT, a.nb, NORM), s, a.pdl, a, total_tiles);
 }
 
 // the widest activation tile (<= 4) that still leaves enough warps

@@ -562,7 +562,8 @@ struct slm_model {
     slm_arena *arena = nullptr;
     // arena views
     float *rope_cos, *rope_sin, *x, *x_mid, *xb, *q, *logits, *att, *kv, *ybuf, *emb;
-    void *q8a[2], *q8b[2];  // Q8X scratch pairs of the two decode parts
+    static constexpr int MAX_PARTS = 4;
+    void *q8a[MAX_PARTS], *q8b[MAX_PARTS];  // Q8X scratch pairs of the decode parts
     uint64_t q8_blocks = 0;
     int32_t *d_tok, *d_pos, *d_slot, *d_next, *d_err;
     uint64_t slot_stride = 0, layer_stride = 0, v_off = 0;
@@ -572,8 +573,10 @@ struct slm_model {
     bool use_fused_attention = true;
     bool split_decode = true;
     bool fuse_norm = true;   // RMSNorm + Q8 inside the QKV and gate/up GEMVs
-    cudaStream_t stream2 = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool use_pdl = true;     // programmatic dependent launch between decode kernels
+    int parts = 4;           // decode parts (streams) for batches of 16+ rows
+    cudaStream_t side[MAX_PARTS - 1] = {};  // streams of parts 1..
+    cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
     CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
     bool have_vmap = false, have_kmap = false;
@@ -704,6 +707,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     aa.max_len = max_len;
     aa.err = m->d_err;
     aa.z_slot = 2LL * m->L;  // planes [slot][layer][K|V] from the first V plane
+    aa.pdl = m->use_pdl;
 
     Q8X qa8 = q8view(m->q8a[part], m->q8_blocks), qb8 = q8view(m->q8b[part], m->q8_blocks);
     const bool fused = m->use_fused_attention && m->have_vmap && attention_fused_ok(aa);
@@ -740,6 +744,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         qa.layer_off = (size_t)l * m->layer_stride;
         g.qkv = qa;
         g.err = m->d_err;
+        g.pdl = m->use_pdl;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_QKV);
         // attention (transformer.rs:430-443)
@@ -776,6 +781,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.res = x;
         g.ld_res = d;
         g.err = m->d_err;
+        g.pdl = m->use_pdl;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_WO);
         // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
@@ -798,6 +804,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.epi = EPI_SWIGLU_Q8;
         g.q8_out = qb8;
         g.err = m->d_err;
+        g.pdl = m->use_pdl;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_GATE_UP);
         // down + residual (transformer.rs:477-486)
@@ -813,6 +820,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.res = x_mid;
         g.ld_res = d;
         g.err = m->d_err;
+        g.pdl = m->use_pdl;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_DOWN);
     }
@@ -854,31 +862,37 @@ uint32_t decode_launches(const slm_model *m, int n) {
     return 1u + per_layer * (uint32_t)m->L + 3u;
 }
 
-// Decode rows split into two halves on two streams when the batch is large
-// enough for both halves to fill the GPU's latency gaps.
-int decode_parts(const slm_model *m, int n) { return (m->split_decode && n >= 16) ? 2 : 1; }
+// Decode rows split into parts on parallel streams when the batch is large
+// enough (8+ rows per part) for the parts to fill each other's latency gaps.
+int decode_parts(const slm_model *m, int n) {
+    if (!m->split_decode || n < 16) return 1;
+    return std::max(1, std::min(m->parts, n / 8));
+}
 
 int len_bucket(const slm_model *m, int max_len) {
     int b = (max_len + 255) / 256 * 256;
     return std::min<int>(b, (int)m->cfg.max_seq_len);
 }
 
-// Enqueue a decode step of rows [0, n) (and the greedy advance): with two
-// parts, rows [0, n/2) run on the model stream and [n/2, n) on the second
-// stream, forked and joined with events so that a graph capture records two
+// Enqueue a decode step of rows [0, n) (and the greedy advance): with P
+// parts, rows [p*n/P, (p+1)*n/P) run on part p's stream (part 0 on the model
+// stream), forked and joined with events so that a graph capture records P
 // parallel branches.
 void enqueue_decode(slm_model *m, int n, int bucket, bool advance) {
     const int parts = decode_parts(m, n);
     if (parts == 1) {
         enqueue_forward(m, 0, n, bucket, STEP_DECODE, m->stream, 0);
     } else {
-        const int na = n / 2;
         cudaEventRecord(m->ev_fork, m->stream);
-        cudaStreamWaitEvent(m->stream2, m->ev_fork, 0);
-        enqueue_forward(m, 0, na, bucket, STEP_DECODE, m->stream, 0);
-        enqueue_forward(m, na, n - na, bucket, STEP_DECODE, m->stream2, 1);
-        cudaEventRecord(m->ev_join, m->stream2);
-        cudaStreamWaitEvent(m->stream, m->ev_join, 0);
+        for (int p = 1; p < parts; p++) cudaStreamWaitEvent(m->side[p - 1], m->ev_fork, 0);
+        for (int p = 0; p < parts; p++) {
+            const int r0 = p * n / parts, r1 = (p + 1) * n / parts;
+            enqueue_forward(m, r0, r1 - r0, bucket, STEP_DECODE, p ? m->side[p - 1] : m->stream, p);
+        }
+        for (int p = 1; p < parts; p++) {
+            cudaEventRecord(m->ev_join[p - 1], m->side[p - 1]);
+            cudaStreamWaitEvent(m->stream, m->ev_join[p - 1], 0);
+        }
     }
     if (advance) launch_advance(m->d_tok, m->d_pos, m->d_next, n, m->stream);
 }
@@ -983,9 +997,11 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         return rc;
     };
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream2, cudaStreamNonBlocking);
+    for (int p = 0; p + 1 < slm_model::MAX_PARTS && e == cudaSuccess; p++) {
+        e = cudaStreamCreateWithFlags(&m->side[p], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_join[p], cudaEventDisableTiming);
+    }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming);
     if (e != cudaSuccess) return cleanup(fail(SLM_ERR_CUDA, cudaGetErrorString(e)));
 
     // ---- weights: one device buffer
@@ -1043,7 +1059,7 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     add_f(d);                                  // embedding accumulator
     add_f(S * V);                              // logits
     add_f(R * cfg->num_heads * T);             // att
-    for (int i = 0; i < 4; i++) add_f(q8f);
+    for (int i = 0; i < 2 * slm_model::MAX_PARTS; i++) add_f(q8f);  // Q8X pair per decode part
     for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
     add_f(S * m->slot_stride);                 // KV
     rc = slm_arena_create(device, cap + a16, &m->arena);
@@ -1058,7 +1074,7 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         (rc = alloc_view(m, d, &m->emb)) || (rc = alloc_view(m, S * V, &m->logits)) ||
         (rc = alloc_view(m, R * cfg->num_heads * T, &m->att)))
         return cleanup(rc);
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < slm_model::MAX_PARTS; i++) {
         if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
         m->q8a[i] = p;
         if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
@@ -1080,6 +1096,10 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->use_fused_attention = !(env && env[0] == '1');
     env = getenv("SLM_DECODE_ONE_STREAM");
     m->split_decode = !(env && env[0] == '1');
+    env = getenv("SLM_DECODE_PARTS");
+    if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
+    env = getenv("SLM_NO_PDL");
+    m->use_pdl = !(env && env[0] == '1');
     env = getenv("SLM_UNFUSED_NORM");
     m->fuse_norm = !(env && env[0] == '1');
     // every V plane of the cache, addressed from the first one: plane
@@ -1097,11 +1117,14 @@ SLM_EXPORT void slm_model_destroy(slm_model *m) {
     if (!m) return;
     DeviceScope ds(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
-    if (m->stream2) cudaStreamSynchronize(m->stream2);
+    for (auto st : m->side)
+        if (st) cudaStreamSynchronize(st);
     for (auto &kv : m->graphs) cudaGraphExecDestroy(kv.second);
     if (m->ev_fork) cudaEventDestroy(m->ev_fork);
-    if (m->ev_join) cudaEventDestroy(m->ev_join);
-    if (m->stream2) cudaStreamDestroy(m->stream2);
+    for (auto ev : m->ev_join)
+        if (ev) cudaEventDestroy(ev);
+    for (auto st : m->side)
+        if (st) cudaStreamDestroy(st);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->arena) slm_arena_destroy(m->arena);
     if (m->wbuf) cudaFree(m->wbuf);
@@ -1327,9 +1350,11 @@ SLM_EXPORT int slm_model_read_hidden(slm_model *m, uint32_t row, float *host) {
 
 SLM_EXPORT uint32_t slm_model_launches_per_decode_step(const slm_model *m, uint32_t n) {
     if (!m || n == 0) return 0;
-    if (decode_parts(m, (int)n) == 1) return decode_launches(m, (int)n) + 1u;
-    const int h = (int)n / 2;
-    return decode_launches(m, h) + decode_launches(m, (int)n - h) + 1u;  // + advance
+    const int parts = decode_parts(m, (int)n);
+    uint32_t total = 1u;  // the greedy advance
+    for (int p = 0; p < parts; p++)
+        total += decode_launches(m, (int)((p + 1) * n / parts - p * n / parts));
+    return total;
 }
 
 SLM_EXPORT int slm_model_kv_write_device(slm_model *m, uint32_t seq, uint32_t layer,
