@@ -628,14 +628,18 @@ __global__ void __launch_bounds__(1024)
     constexpr int SEG = 256;
     const int nseg = (L + SEG - 1) / SEG;
     float chain = 0.0f;
+    // exp workers: warps w >= 1 with w % 4 != 0, so that no exp work shares
+    // warp 0's scheduler with the dependent chains
+    const bool worker = warp > 0 && (warp & 3) != 0;
+    const int wid = (warp - 1 - (warp >> 2)) * 32 + lane;
+    const int nwk = ((nw - 1) - (nw - 1) / 4) * 32;
     for (int k = 0; k <= nseg; k++) {
-        if (warp > 0 && k < nseg) {
+        if (worker && k < nseg) {
             const int t0 = k * SEG, t1 = L - t0 < SEG ? L : t0 + SEG;
-            const int nwk = nth - 32;
             for (int h = 0; h < KVM; h++) {
                 const float mx = s_red[32 + h];
                 float *row = s_sc + h * lp;
-                int t = t0 + tid - 32;
+                int t = t0 + wid;
                 for (; t + nwk < t1; t += 2 * nwk) {
                     const float x0 = row[t], x1 = row[t + nwk];
                     const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
@@ -671,13 +675,12 @@ __global__ void __launch_bounds__(1024)
         s_red[48 + tid] = __fdiv_rn(1.0f, sum);
     }
     __syncthreads();
-    // p = e * (1/sum): stored (and written out) here only when the caller
-    // wants the probabilities; otherwise the PV loop multiplies on the fly
-    // (the same rounding) and this pass is skipped
-    for (int h = 0; h < (a.write_probs ? KVM : 0); h++) {
+    // p = e * (1/sum), in place (and into att when the caller wants the
+    // probabilities)
+    for (int h = 0; h < KVM; h++) {
         const float inv = s_red[48 + h];
         float *row = s_sc + h * lp;
-        float *prow = a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld;
+        float *prow = a.write_probs ? a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld : nullptr;
         int t = tid;
         for (; t + 3 * nth < L; t += 4 * nth) {
             const float p0 = __fmul_rn(row[t], inv), p1 = __fmul_rn(row[t + nth], inv);
@@ -686,15 +689,17 @@ __global__ void __launch_bounds__(1024)
             row[t + nth] = p1;
             row[t + 2 * nth] = p2;
             row[t + 3 * nth] = p3;
-            prow[t] = p0;
-            prow[t + nth] = p1;
-            prow[t + 2 * nth] = p2;
-            prow[t + 3 * nth] = p3;
+            if (prow) {
+                prow[t] = p0;
+                prow[t + nth] = p1;
+                prow[t + 2 * nth] = p2;
+                prow[t + 3 * nth] = p3;
+            }
         }
         for (; t < L; t += nth) {
             const float pr = __fmul_rn(row[t], inv);
             row[t] = pr;
-            prow[t] = pr;
+            if (prow) prow[t] = pr;
         }
     }
 
@@ -719,8 +724,6 @@ __global__ void __launch_bounds__(1024)
         const bool active = tid < n_pairs;
         const int hl = tid / (hd >> 1), j2 = 2 * (tid - hl * (hd >> 1));
         float acc0 = 0.0f, acc1 = 0.0f;  // out[hl][j2], out[hl][j2 + 1]
-        // s_sc holds e (p = e * inv) unless the normalize pass ran (x 1.0 is exact)
-        const float inv = a.write_probs ? 1.0f : s_red[48 + (hl < KVM ? hl : 0)];
 #pragma unroll 1
         for (int k = 0; k < ntiles; k++) {
             if (!mbar_wait(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u, &s_abort,
@@ -736,8 +739,6 @@ __global__ void __launch_bounds__(1024)
                     // full tile: the loads of positions 4j+4..4j+7 are in
                     // flight while positions 4j..4j+3 are added
                     float4 pc = *reinterpret_cast<const float4 *>(pp);
-                    pc = make_float4(__fmul_rn(pc.x, inv), __fmul_rn(pc.y, inv), __fmul_rn(pc.z, inv),
-                                     __fmul_rn(pc.w, inv));
                     float2 vc[4];
 #pragma unroll
                     for (int u = 0; u < 4; u++) vc[u] = vt[u * hs];
@@ -747,8 +748,6 @@ __global__ void __launch_bounds__(1024)
                         float2 vn[4];
                         if (j + 1 < tt / 4) {
                             pn = *reinterpret_cast<const float4 *>(pp + 4 * j + 4);
-                            pn = make_float4(__fmul_rn(pn.x, inv), __fmul_rn(pn.y, inv),
-                                             __fmul_rn(pn.z, inv), __fmul_rn(pn.w, inv));
 #pragma unroll
                             for (int u = 0; u < 4; u++) vn[u] = vt[(4 * j + 4 + u) * hs];
                         }
@@ -768,7 +767,7 @@ __global__ void __launch_bounds__(1024)
                     }
                 } else {
                     for (int tl = 0; tl < nrows; tl++) {
-                        const float pr = __fmul_rn(pp[tl], inv);
+                        const float pr = pp[tl];
                         const float2 vv = vt[tl * hs];
                         acc0 = __fadd_rn(acc0, __fmul_rn(pr, vv.x));
                         acc1 = __fadd_rn(acc1, __fmul_rn(pr, vv.y));
@@ -891,14 +890,16 @@ bool attention_fused_ok(const AttnArgs &a) {
     return fused_shape(kv_mul, a.head_dim, a.max_len).smem <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
 }
 
-void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
+void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,
                        cudaStream_t s) {
-    if (a.rows <= 0) return;
+    if (args.rows <= 0) return;
+    AttnArgs a = args;
     const int kv_mul = a.num_heads / a.num_kv_heads;
     dim3 g1((a.max_len + TILE_KEYS - 1) / TILE_KEYS, a.num_kv_heads, a.rows);
     // the pipelined kernel bulk-copies the query vectors: 16-byte aligned rows
     const bool q_bulk = ((uintptr_t)a.q & 15) == 0 && (a.ldq & 3) == 0;
-    if (kmap && a.head_dim % 32 == 0 && q_bulk) {
+    const bool pipe = kmap && a.head_dim % 32 == 0 && q_bulk;
+    if (pipe) {
         // pipelined: a few CTAs per SM walk all (row, KV head, tile) items
         const int ntile_max = (a.max_len + TILE_KEYS - 1) / TILE_KEYS;
         const long long items = (long long)a.rows * a.num_kv_heads * ntile_max;
