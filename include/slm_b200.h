@@ -214,6 +214,29 @@ int slm_model_forward_token(slm_model *m, uint32_t seq, int32_t token, uint32_t 
 /* TransformerModel::prefill_tokens (transformer.rs:799-854). */
 int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_t *tokens, uint32_t n,
                              uint32_t start_pos, int32_t *next_token);
+/* Batched prefill of nseq independent prompts of n tokens each at positions
+ * 0..n-1 (tokens [nseq][n], sequence slots seqs[nseq]): one forward over the
+ * nseq*n rows, the same per-token results as prefill_tokens on each prompt
+ * (forward_batch_with_kv, transformer.rs:491-651).  next[i] = greedy next
+ * token of prompt i; logits row i = its logits.  After
+ * slm_model_attach_shard with nranks > 1, each rank computes the attention
+ * of its (sequence, KV head) units only (slm_shard_units) and one NCCL
+ * all-gather per layer assembles the outputs before Wo; every rank then holds
+ * the full results.  Requires nseq*num_kv_heads to divide by nranks. */
+int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
+                            const int32_t *tokens, uint32_t n, int32_t *next);
+/* NCCL unique id (bytes = 128) for slm_model_attach_shard; made on one rank
+ * and sent to the others by the host. */
+int slm_nccl_unique_id(void *id_out, uint64_t bytes);
+/* Join a group of nranks models (one per GPU, collective: every rank calls it
+ * with the same id) for KV-head-sharded batched prefill.  NCCL is loaded at
+ * run time (libnccl.so.2).  nranks = 1 detaches nothing and needs no id. */
+int slm_model_attach_shard(slm_model *m, const void *id, uint64_t bytes, int nranks, int rank);
+/* Units (sequence*num_kv_heads + KV head) that `rank` computes in a sharded
+ * batched prefill, in all-gather order (unit i*nranks + rank); returns their
+ * count (0 when nseq*num_kv_heads does not divide by nranks). */
+uint32_t slm_shard_units(uint32_t nseq, uint32_t num_kv_heads, uint32_t nranks, uint32_t rank,
+                         uint32_t *units_out, uint32_t capacity);
 /* TransformerModel::generate (transformer.rs:858-892); eos < 0 = none. */
 int slm_model_generate(slm_model *m, uint32_t seq, const int32_t *prompt, uint32_t n_prompt,
                        int32_t *out_tokens, uint32_t n_out, int32_t eos, uint32_t *generated);

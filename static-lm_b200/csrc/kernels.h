@@ -145,6 +145,11 @@ struct AttnArgs {
     // fused path: V plane of row r in the tensor map = slot*z_slot + z_layer
     long long z_slot, z_layer;
     bool pdl;                // fused path: programmatic dependent launch
+    // KV-head sharding of a batched prefill (fused path): rows come in runs of
+    // rows_per_seq per sequence; (row r, KV head g) is computed here only when
+    // unit (r / rows_per_seq) * num_kv_heads + g is congruent to shard_r
+    // modulo shard_n.  shard_n <= 1: every unit.
+    int shard_n, shard_r, rows_per_seq;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)
@@ -174,5 +179,14 @@ bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
                   uint64_t planes, int head_dim);
 // Opt the attention kernels into `bytes` of dynamic shared memory (current device).
 void set_attention_smem_limit(int bytes);
+
+// KV-head-sharded prefill: the attention outputs of this rank's units into a
+// contiguous send buffer [unit i][row][kd] (unit u = i*nranks + rank, rows
+// u/kvh*n .. +n, dims (u%kvh)*kd .. +kd of x), and the all-gathered buffer
+// [rank q][unit i][row][kd] back into x.  kd = kv_mul*head_dim.
+void launch_shard_pack(const float *x, size_t ldx, float *send, int units_per_rank, int nranks,
+                       int rank, int kvh, int kd, int n, cudaStream_t s);
+void launch_shard_unpack(const float *recv, float *x, size_t ldx, int units_per_rank, int nranks,
+                         int kvh, int kd, int n, cudaStream_t s);
 
 }  // namespace slm

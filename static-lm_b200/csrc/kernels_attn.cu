@@ -50,6 +50,11 @@ __device__ __forceinline__ int row_len(const AttnArgs &a, int r) {
 __device__ __forceinline__ size_t row_slot(const AttnArgs &a, int r) {
     return a.slot ? (size_t)a.slot[r] : 0;
 }
+// whether this rank computes (row r, KV head g) of a sharded batched prefill
+__device__ __forceinline__ bool unit_owned(const AttnArgs &a, int r, int g) {
+    return a.shard_n <= 1 ||
+           ((r / a.rows_per_seq) * a.num_kv_heads + g) % a.shard_n == a.shard_r;
+}
 
 __global__ void __launch_bounds__(SCORE_T) attn_scores_kernel(AttnArgs a) {
     extern __shared__ float s_q[];  // [kv_mul][head_dim]
@@ -234,6 +239,7 @@ __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a
     __shared__ __align__(8) uint64_t bar;
     __shared__ int s_abort;
     const int r = blockIdx.z, g = blockIdx.y;
+    if (!unit_owned(a, r, g)) return;  // CTA-uniform
     const int kv_mul = a.num_heads / a.num_kv_heads;
     const int hd = a.head_dim, rs = hd + 4;
     const int L = row_len(a, r);
@@ -434,6 +440,7 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
                 const long long rg = it / ntile_max;
                 item.g = (int)(rg % a.num_kv_heads);
                 item.r = (int)(rg / a.num_kv_heads);
+                if (!unit_owned(a, item.r, item.g)) continue;  // another rank's unit
                 const int L = row_len(a, item.r);
                 item.t0 = k * TILE_KEYS;
                 if (item.t0 >= L) continue;  // past this row's keys
@@ -544,6 +551,7 @@ __global__ void __launch_bounds__(1024)
     constexpr int tt = TT_V;
     const int nth = blockDim.x;
     const int g = blockIdx.x, r = blockIdx.y;
+    if (!unit_owned(a, r, g)) return;  // CTA-uniform: another rank's unit
     const int hd = a.head_dim;
     const int tid = threadIdx.x;
     float *s_ring = smem;                                   // [STAGES][tt][hd]
@@ -972,6 +980,44 @@ void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensor
     launch_attn_scores(a, s);
     launch_attn_softmax(a, s);
     launch_attn_pv(a, s);
+}
+
+// ---- KV-head-sharded prefill: exchange layout ------------------------------
+
+namespace {
+
+__global__ void shard_pack_kernel(const float *x, size_t ldx, float *send, int nranks, int rank,
+                                  int kvh, int kd, int n) {
+    const int row = blockIdx.x, i = blockIdx.y;
+    const int u = i * nranks + rank, s = u / kvh, g = u - s * kvh;
+    const float *src = x + (size_t)(s * n + row) * ldx + (size_t)g * kd;
+    float *dst = send + ((size_t)i * n + row) * kd;
+    for (int c = threadIdx.x; c < kd; c += blockDim.x) dst[c] = src[c];
+}
+
+__global__ void shard_unpack_kernel(const float *recv, float *x, size_t ldx, int upr, int nranks,
+                                    int kvh, int kd, int n) {
+    const int row = blockIdx.x, i = blockIdx.y, q = blockIdx.z;
+    const int u = i * nranks + q, s = u / kvh, g = u - s * kvh;
+    const float *src = recv + (((size_t)q * upr + i) * n + row) * kd;
+    float *dst = x + (size_t)(s * n + row) * ldx + (size_t)g * kd;
+    for (int c = threadIdx.x; c < kd; c += blockDim.x) dst[c] = src[c];
+}
+
+}  // namespace
+
+void launch_shard_pack(const float *x, size_t ldx, float *send, int units_per_rank, int nranks,
+                       int rank, int kvh, int kd, int n, cudaStream_t s) {
+    if (units_per_rank <= 0 || n <= 0) return;
+    shard_pack_kernel<<<dim3((unsigned)n, (unsigned)units_per_rank), 128, 0, s>>>(x, ldx, send, nranks,
+                                                                                 rank, kvh, kd, n);
+}
+
+void launch_shard_unpack(const float *recv, float *x, size_t ldx, int units_per_rank, int nranks,
+                         int kvh, int kd, int n, cudaStream_t s) {
+    if (units_per_rank <= 0 || n <= 0) return;
+    shard_unpack_kernel<<<dim3((unsigned)n, (unsigned)units_per_rank, (unsigned)nranks), 128, 0, s>>>(
+        recv, x, ldx, units_per_rank, nranks, kvh, kd, n);
 }
 
 }  // namespace slm

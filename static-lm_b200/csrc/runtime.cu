@@ -2,6 +2,8 @@
 // weights, the operator entry points and the model driver (prefill, batched
 // decode, greedy generation, embeddings) with CUDA-graph replay of decode.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types and prototypes only: the library is resolved at run time
 
 #include <algorithm>
 #include <cmath>
@@ -545,7 +547,34 @@ struct LayerDev {
     float *rms_att = nullptr, *rms_ffn = nullptr;
 };
 
-enum StepKind { STEP_DECODE = 0, STEP_PREFILL = 1, STEP_EMBED = 2 };
+enum StepKind { STEP_DECODE = 0, STEP_PREFILL = 1, STEP_EMBED = 2, STEP_PREFILL_BATCH = 3 };
+
+// NCCL entry points, looked up in whichever libnccl the process has (torch's,
+// or the system's) so that the library itself has no link-time dependency.
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_id = nullptr;
+    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+    bool ok() const { return get_id && init_rank && all_gather && destroy && error_string; }
+};
+
+const NcclApi &nccl_api() {
+    static const NcclApi api = [] {
+        NcclApi a;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return a;
+        a.get_id = reinterpret_cast<decltype(a.get_id)>(dlsym(h, "ncclGetUniqueId"));
+        a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+        a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+        a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+        a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+        return a;
+    }();
+    return api;
+}
 
 }  // namespace
 
@@ -580,6 +609,10 @@ struct slm_model {
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
     CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
     bool have_vmap = false, have_kmap = false;
+    // KV-head-sharded batched prefill (slm_model_attach_shard)
+    int shard_n = 1, shard_r = 0;
+    ncclComm_t comm = nullptr;
+    float *shard_send = nullptr, *shard_recv = nullptr;  // R*dim floats each
 };
 
 namespace {
@@ -661,7 +694,7 @@ bool gate_up_norm_fused(const slm_model *m, int n) {
 }
 
 void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, cudaStream_t st,
-                     int part, Profiler *prof = nullptr) {
+                     int part, Profiler *prof = nullptr, int seq_rows = 0) {
     const slm_config &c = m->cfg;
     const int d = (int)c.dim, h = (int)c.hidden_dim;
     const size_t r0 = (size_t)row0;
@@ -711,11 +744,20 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
 
     Q8X qa8 = q8view(m->q8a[part], m->q8_blocks), qb8 = q8view(m->q8b[part], m->q8_blocks);
     const bool fused = m->use_fused_attention && m->have_vmap && attention_fused_ok(aa);
+    const int kv_mul = (int)(c.num_heads / c.num_kv_heads);
+    // a batched prefill on a sharded model computes only this rank's
+    // (sequence, KV head) units, then all-gathers the outputs before Wo
+    const bool sharded = kind == STEP_PREFILL_BATCH && m->shard_n > 1 && fused;
+    if (kind == STEP_PREFILL_BATCH) {
+        aa.rows_per_seq = seq_rows;
+        aa.shard_n = sharded ? m->shard_n : 1;
+        aa.shard_r = sharded ? m->shard_r : 0;
+    }
     if (fused) {
         aa.write_probs = false;  // probabilities stay in shared memory
-        const int kv_mul = (int)(c.num_heads / c.num_kv_heads);
-        if ((kv_mul * m->hd) % 32 == 0) aa.q8_out = qb8;
+        if ((kv_mul * m->hd) % 32 == 0 && !sharded) aa.q8_out = qb8;
     }
+    const int n_units = kind == STEP_PREFILL_BATCH && seq_rows > 0 ? (n / seq_rows) * (int)c.num_kv_heads : 0;
     const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
     const bool norm_gu = m->L > 0 && gate_up_norm_fused(m, n);
     const float inv_d = 1.0f / (float)d;
@@ -754,6 +796,16 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             // scores, then softmax + PV + the Q8_0 of the output
             launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
+            if (sharded) {
+                // this rank's units -> all ranks: one all-gather before Wo
+                const int upr = n_units / m->shard_n, kd = kv_mul * m->hd;
+                launch_shard_pack(xb, d, m->shard_send, upr, m->shard_n, m->shard_r,
+                                  (int)c.num_kv_heads, kd, seq_rows, st);
+                nccl_api().all_gather(m->shard_send, m->shard_recv, (size_t)upr * seq_rows * kd,
+                                      ncclFloat32, m->comm, st);
+                launch_shard_unpack(m->shard_recv, xb, d, upr, m->shard_n, (int)c.num_kv_heads, kd,
+                                    seq_rows, st);
+            }
             if (!aa.q8_out.qs) {
                 launch_quantize_q8x(xb, d, d, qb8, n, st);
                 mark(prof, SLM_PHASE_QUANTIZE);
@@ -826,9 +878,13 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     }
     if (kind == STEP_EMBED) return;
     // final RMSNorm + lm_head + argmax (transformer.rs:776-794 / 835-853)
-    const float *xs = kind == STEP_PREFILL ? x + (size_t)(n - 1) * d : x;
-    int rows = kind == STEP_PREFILL ? 1 : n;
-    launch_rmsnorm_q8(xs, d, m->out_norm, d, c.rms_eps, nullptr, 0, qa8, rows, st);
+    // prefill: the last row (of each sequence, for a batched prefill)
+    const float *xs = kind == STEP_PREFILL ? x + (size_t)(n - 1) * d
+                      : kind == STEP_PREFILL_BATCH ? x + (size_t)(seq_rows - 1) * d
+                                                    : x;
+    const size_t ldxs = kind == STEP_PREFILL_BATCH ? (size_t)seq_rows * d : (size_t)d;
+    int rows = kind == STEP_PREFILL ? 1 : kind == STEP_PREFILL_BATCH ? n / seq_rows : n;
+    launch_rmsnorm_q8(xs, ldxs, m->out_norm, d, c.rms_eps, nullptr, 0, qa8, rows, st);
     mark(prof, SLM_PHASE_RMSNORM);
     GemvArgs g{};
     g.w = m->lm_head.tiles;
@@ -1125,6 +1181,9 @@ SLM_EXPORT void slm_model_destroy(slm_model *m) {
         if (ev) cudaEventDestroy(ev);
     for (auto st : m->side)
         if (st) cudaStreamDestroy(st);
+    if (m->comm) nccl_api().destroy(m->comm);
+    if (m->shard_send) cudaFree(m->shard_send);
+    if (m->shard_recv) cudaFree(m->shard_recv);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->arena) slm_arena_destroy(m->arena);
     if (m->wbuf) cudaFree(m->wbuf);
@@ -1214,6 +1273,90 @@ SLM_EXPORT int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_
     enqueue_forward(m, 0, (int)n, (int)(start_pos + n), STEP_PREFILL, m->stream, 0);
     TRY(launch_check("prefill"));
     return fetch_next(m, 1, next);
+}
+
+SLM_EXPORT int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
+                                       const int32_t *tokens, uint32_t n, int32_t *next) {
+    if (!m || !seqs || !tokens || !next) return fail(SLM_ERR_INVALID_ARG, "null argument");
+    if (nseq == 0 || n == 0) return fail(SLM_ERR_INVALID_ARG, "empty batch or prompt");
+    if ((uint64_t)nseq * n > (uint64_t)m->R || nseq > (uint32_t)m->S)
+        return fail(SLM_ERR_CAPACITY, "nseq * n above max_rows or nseq above max_sequences");
+    if (n > m->cfg.max_seq_len) return fail(SLM_ERR_OUT_OF_BOUNDS, "prompt longer than max_seq_len");
+    for (uint32_t i = 0; i < nseq; i++)
+        if (seqs[i] >= (uint32_t)m->S) return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence out of range");
+    const int rows = (int)(nseq * n);
+    TRY(check_tokens(m, rows, tokens));
+    if (m->shard_n > 1) {
+        if ((nseq * m->cfg.num_kv_heads) % (uint32_t)m->shard_n)
+            return fail(SLM_ERR_SHAPE, "nseq * num_kv_heads must divide by the number of ranks");
+        AttnArgs probe = attn_args_for(&m->cfg);
+        probe.k_base = m->kv;
+        probe.v_base = m->kv + m->v_off;
+        probe.att = m->att;
+        probe.slot_stride = m->slot_stride;
+        probe.max_len = (int)n;
+        if (!(m->use_fused_attention && m->have_vmap && attention_fused_ok(probe)))
+            return fail(SLM_ERR_SHAPE, "sharded prefill needs the fused attention path");
+    }
+    DeviceScope ds(m->device);
+    std::vector<uint32_t> slot(rows), pos(rows);
+    for (int r = 0; r < rows; r++) {
+        slot[r] = seqs[r / n];
+        pos[r] = (uint32_t)(r % n);
+    }
+    TRY(stage_rows(m, rows, tokens, slot.data(), 0, pos.data(), 0));
+    enqueue_forward(m, 0, rows, (int)n, STEP_PREFILL_BATCH, m->stream, 0, nullptr, (int)n);
+    TRY(launch_check("batched prefill"));
+    return fetch_next(m, (int)nseq, next);
+}
+
+SLM_EXPORT int slm_nccl_unique_id(void *id_out, uint64_t bytes) {
+    if (!id_out || bytes != sizeof(ncclUniqueId))
+        return fail(SLM_ERR_INVALID_ARG, "id buffer must hold " + std::to_string(sizeof(ncclUniqueId)) + " bytes");
+    const NcclApi &api = nccl_api();
+    if (!api.ok()) return fail(SLM_ERR_CUDA, "no NCCL library (libnccl.so.2) could be loaded");
+    ncclUniqueId id;
+    const ncclResult_t r = api.get_id(&id);
+    if (r != ncclSuccess) return fail(SLM_ERR_CUDA, std::string("ncclGetUniqueId: ") + api.error_string(r));
+    std::memcpy(id_out, &id, sizeof(id));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_attach_shard(slm_model *m, const void *id, uint64_t bytes, int nranks,
+                                      int rank) {
+    if (!m) return fail(SLM_ERR_INVALID_ARG, "model is null");
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(SLM_ERR_INVALID_ARG, "bad rank / nranks");
+    if (m->comm) return fail(SLM_ERR_INVALID_ARG, "model already attached to a shard group");
+    if (nranks == 1) {
+        m->shard_n = 1;
+        m->shard_r = 0;
+        return SLM_OK;
+    }
+    if (!id || bytes != sizeof(ncclUniqueId)) return fail(SLM_ERR_INVALID_ARG, "bad NCCL unique id");
+    const NcclApi &api = nccl_api();
+    if (!api.ok()) return fail(SLM_ERR_CUDA, "no NCCL library (libnccl.so.2) could be loaded");
+    DeviceScope ds(m->device);
+    const size_t bytes_buf = (size_t)m->R * m->cfg.dim * sizeof(float);
+    CUDA_TRY(cudaMalloc(&m->shard_send, bytes_buf));
+    CUDA_TRY(cudaMalloc(&m->shard_recv, bytes_buf));
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = api.init_rank(&comm, nranks, uid, rank);
+    if (r != ncclSuccess) return fail(SLM_ERR_CUDA, std::string("ncclCommInitRank: ") + api.error_string(r));
+    m->comm = comm;
+    m->shard_n = nranks;
+    m->shard_r = rank;
+    return SLM_OK;
+}
+
+SLM_EXPORT uint32_t slm_shard_units(uint32_t nseq, uint32_t num_kv_heads, uint32_t nranks,
+                                    uint32_t rank, uint32_t *units_out, uint32_t capacity) {
+    if (nranks == 0 || rank >= nranks || (nseq * num_kv_heads) % nranks) return 0;
+    const uint32_t upr = nseq * num_kv_heads / nranks;
+    for (uint32_t i = 0; i < upr && i < capacity; i++)
+        if (units_out) units_out[i] = i * nranks + rank;
+    return upr;
 }
 
 SLM_EXPORT int slm_model_generate(slm_model *m, uint32_t seq, const int32_t *prompt,

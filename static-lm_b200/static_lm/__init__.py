@@ -202,6 +202,23 @@ class Model:
                                        start_pos, C.byref(nxt))
         return int(nxt.value)
 
+    def prefill_batch(self, prompts, seqs=None):
+        """Batched prefill of equal-length prompts (2-D array [nseq][n]); returns
+        the greedy next token of each (slm_model_prefill_batch)."""
+        t = np.ascontiguousarray(prompts, dtype=np.int32)
+        nseq, n = t.shape
+        s = np.ascontiguousarray(range(nseq) if seqs is None else seqs, dtype=np.uint32)
+        nxt = np.zeros(nseq, dtype=np.int32)
+        lib().slm_model_prefill_batch(self.h, nseq, s.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                      t.ctypes.data_as(C.POINTER(C.c_int32)), n,
+                                      nxt.ctypes.data_as(C.POINTER(C.c_int32)))
+        return nxt
+
+    def attach_shard(self, nccl_id: bytes, nranks: int, rank: int):
+        """Join the KV-head sharding group (collective over the ranks)."""
+        buf = C.create_string_buffer(bytes(nccl_id), 128) if nranks > 1 else None
+        lib().slm_model_attach_shard(self.h, buf, 128 if buf is not None else 0, nranks, rank)
+
     def generate(self, prompt, n_out: int, eos: int = -1, seq: int = 0):
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.zeros(max(n_out, 1), dtype=np.int32)
@@ -267,3 +284,20 @@ class Model:
         out = np.zeros(self.cfg.dim, dtype=np.float32)
         lib().slm_model_read_hidden(self.h, row, _np_ptr(out))
         return out
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Model.attach_shard."""
+    buf = C.create_string_buffer(128)
+    lib().slm_nccl_unique_id(buf, 128)
+    return buf.raw
+
+
+def shard_units(nseq: int, num_kv_heads: int, nranks: int, rank: int):
+    """The (sequence*num_kv_heads + KV head) units `rank` computes in a sharded
+    batched prefill, in all-gather order."""
+    cap = max(1, nseq * num_kv_heads)
+    out = np.zeros(cap, dtype=np.uint32)
+    k = lib().slm_shard_units(nseq, num_kv_heads, nranks, rank,
+                              out.ctypes.data_as(C.POINTER(C.c_uint32)), cap)
+    return [int(u) for u in out[:k]]

@@ -99,6 +99,10 @@ SIGNATURES = {
     "slm_model_device_bytes": (_U64, [_V], False),
     "slm_model_forward_token": (C.c_int, [_V, _U32, C.c_int32, _U32, _I32P], True),
     "slm_model_prefill_tokens": (C.c_int, [_V, _U32, _I32P, _U32, _U32, _I32P], True),
+    "slm_model_prefill_batch": (C.c_int, [_V, _U32, _U32P, _I32P, _U32, _I32P], True),
+    "slm_nccl_unique_id": (C.c_int, [_V, _U64], True),
+    "slm_model_attach_shard": (C.c_int, [_V, _V, _U64, C.c_int, C.c_int], True),
+    "slm_shard_units": (_U32, [_U32, _U32, _U32, _U32, _U32P, _U32], False),
     "slm_model_generate": (C.c_int, [_V, _U32, _I32P, _U32, _I32P, _U32, C.c_int32, _U32P], True),
     "slm_model_embed_tokens": (C.c_int, [_V, _U32, _I32P, _U32, C.POINTER(C.c_float)], True),
     "slm_model_decode_batch": (C.c_int, [_V, _U32, _U32P, _I32P, _U32P, _I32P], True),

@@ -1,0 +1,95 @@
+"""Batched prefill (slm_model_prefill_batch) against per-sequence prefill, and
+its KV-head-sharded form on two GPUs against one GPU.  Bit-exact: the batched
+and sharded forms run the same per-(row, head) chains; the all-gather only
+moves bytes."""
+import os
+
+import numpy as np
+import pytest
+
+import static_lm as S
+from static_lm import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _prompts(vocab, nseq, n, seed):
+    return np.random.default_rng(seed).integers(0, vocab, (nseq, n)).astype(np.int32)
+
+
+@pytest.mark.parametrize("name,layers,nseq,n", [("cfg1", None, 3, 20), ("cfg2", 2, 2, 24),
+                                                ("cfg3", 2, 2, 40)])
+def test_prefill_batch_matches_per_sequence_prefill(cuda, name, layers, nseq, n):
+    cfg, nl, vocab = synth.config(name)
+    w = synth.synth_model(cfg, layers or nl, vocab, seed=21)
+    prompts = _prompts(vocab, nseq, n, 3)
+    batch = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n)
+    got = batch.prefill_batch(prompts)
+    one = S.Model(cfg, w, max_sequences=nseq, max_rows=n)
+    for s in range(nseq):
+        assert one.prefill_tokens(prompts[s], seq=s) == got[s]
+        want = one.logits(0)
+        assert np.array_equal(batch.logits(s), want), s
+    # decode continues from the batched prefill's KV exactly as from the sequential one
+    nxt_b = batch.decode_batch(list(range(nseq)), list(got), [n] * nseq)
+    for s in range(nseq):
+        one.prefill_tokens(prompts[s], seq=s)
+    nxt_o = one.decode_batch(list(range(nseq)), list(got), [n] * nseq)
+    assert list(nxt_b) == list(nxt_o)
+
+
+SH = ("cfg3", 2, 4, 48)  # name, layers, sequences, tokens: 12 (sequence, KV head) units
+
+
+def _sharded_rank(rank, world, q_in, q_out):
+    import torch
+    try:
+        torch.cuda.set_device(rank)
+        name, layers, nseq, n = SH
+        cfg, _, vocab = synth.config(name)
+        w = synth.synth_model(cfg, layers, vocab, seed=22)
+        m = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n, device=rank)
+        if rank == 0:
+            uid = S.nccl_unique_id()
+            for _ in range(world - 1):
+                q_in.put(uid)
+        else:
+            uid = q_in.get(timeout=120)
+        m.attach_shard(uid, world, rank)
+        nxt = m.prefill_batch(_prompts(vocab, nseq, n, 4))
+        q_out.put((rank, list(nxt), [m.logits(s) for s in range(nseq)]))
+        m.close()
+    except Exception as e:
+        q_out.put((rank, repr(e), None))
+        raise
+
+
+def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q_in, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_sharded_rank, args=(r, world, q_in, q_out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q_out.get(timeout=300) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, nxt, logits in res:
+        assert logits is not None, (rank, nxt)
+    name, layers, nseq, n = SH
+    cfg, _, vocab = synth.config(name)
+    w = synth.synth_model(cfg, layers, vocab, seed=22)
+    ref = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n)
+    want = list(ref.prefill_batch(_prompts(vocab, nseq, n, 4)))
+    for rank, nxt, logits in res:
+        assert nxt == want, rank
+        for s in range(nseq):
+            assert np.array_equal(logits[s], ref.logits(s)), (rank, s)

@@ -92,3 +92,86 @@ def test_two_gloo_ranks_decode_their_shards_like_one_process():
     w = synth.synth_model(cfg, layers, vocab, seed=3)
     whole = _decode(cfg, w, vocab, list(range(GLOBAL)))
     assert sharded == whole
+
+
+# ---- KV-head-sharded batched prefill: the exchange layout -----------------
+
+NSEQ, NTOK = 4, 6
+SH_CFG = (128, 256, 4, 2, 16, 1e-5)  # dim, hidden, heads, kv heads, max_seq, eps
+
+
+def _full_attention():
+    """Attention outputs [NSEQ*NTOK][dim] of seeded q/K/V, every (row, head)."""
+    cfg = O.Config(*SH_CFG)
+    dim, heads, kvh = SH_CFG[0], SH_CFG[2], SH_CFG[3]
+    kvd = dim // heads * kvh
+    rng = np.random.default_rng(9)
+    out = np.zeros((NSEQ * NTOK, dim), np.float32)
+    for s in range(NSEQ):
+        k = rng.standard_normal(SH_CFG[4] * kvd).astype(np.float32)
+        v = rng.standard_normal(SH_CFG[4] * kvd).astype(np.float32)
+        for t in range(NTOK):
+            q = rng.standard_normal(dim).astype(np.float32)
+            out[s * NTOK + t] = O.attention(q, k, v, cfg, t)[0]
+    return out
+
+
+def _unit_block(out, u):
+    """Rows and dims of unit u = sequence * kv_heads + KV head."""
+    dim, heads, kvh = SH_CFG[0], SH_CFG[2], SH_CFG[3]
+    kd = dim // heads * (heads // kvh)
+    s, g = divmod(u, kvh)
+    return out[s * NTOK:(s + 1) * NTOK, g * kd:(g + 1) * kd]
+
+
+def _shard_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    import static_lm as S
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = _full_attention()
+        units = S.shard_units(NSEQ, SH_CFG[3], world, rank)
+        # this rank's attention outputs, packed [unit][row][kd] as the library sends them
+        send = torch.from_numpy(np.stack([_unit_block(full, u) for u in units]).copy())
+        recv = torch.empty((world * send.shape[0],) + tuple(send.shape[1:]), dtype=send.dtype)
+        dist.all_gather_into_tensor(recv, send)
+        # unpack with the all-gather order: rank r's i-th unit is i*world + r
+        got = np.zeros_like(full)
+        for r in range(world):
+            for i, u in enumerate(S.shard_units(NSEQ, SH_CFG[3], world, r)):
+                _unit_block(got, u)[:] = recv[r * len(units) + i].numpy()
+        q.put((rank, bool(np.array_equal(got, full)), units))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, False, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_units_partition_the_units():
+    import static_lm as S
+    for world in (1, 2, 4, 8):
+        parts = [S.shard_units(NSEQ, SH_CFG[3], world, r) for r in range(world)]
+        flat = sorted(u for p in parts for u in p)
+        assert flat == list(range(NSEQ * SH_CFG[3]))
+        assert len({len(p) for p in parts}) == 1
+    assert S.shard_units(3, 3, 2, 0) == []  # 9 units do not divide over 2 ranks
+
+
+def test_two_gloo_ranks_assemble_the_sharded_attention():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in res), res
+    assert sorted(u for _, _, units in res for u in units) == list(range(NSEQ * SH_CFG[3]))
