@@ -31,6 +31,7 @@ import numpy as np  # noqa: E402
 
 GLOBAL_BATCH = 64
 CTX = 2048
+PREFILL_SEQS, PREFILL_LEN = 8, 4096  # config 5: 8 prompts of 4096 tokens
 DECODE_ROOM = 128  # max_seq_len = 2048 + 128: the steps after the prefilled context
 METRIC = "decode tok/s (SmolLM2-135M shape, batch 64, 2048-token context)"
 
@@ -45,6 +46,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU work of the cpu_baseline / reference sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-prefill", action="store_true", help="skip the prefill measurement")
     p.add_argument("--layers", type=int, default=None,
                    help="profiling case only: fewer layers (same per-kernel shapes); the "
                         "line is then marked as not a bench value")
@@ -419,6 +421,42 @@ def run_ours(args):
         # free parity check: the GPU's first tokens of the sampled sequences
         parity = all(list(tokens_dev[:len(o), s]) == o for s, o in zip(sample_seqs, outs))
 
+    # ---- prefill (config 5): 8 prompts x 4096 tokens in one batched forward;
+    # with N ranks each computes its (sequence, KV head) units of attention
+    # and one NCCL all-gather per layer assembles them before Wo
+    gpu_launches = model.launches_per_decode_step(B) * K
+    prefill = None
+    if not args.no_prefill:
+        model.close()
+        model = None
+        pcfg, _, _ = __import__("static_lm.synth", fromlist=["config"]).config(
+            "cfg3", max_seq_len=PREFILL_LEN + 128)
+        pm = S.Model(pcfg, w, max_sequences=PREFILL_SEQS, max_rows=PREFILL_SEQS * PREFILL_LEN,
+                     device=local)
+        if ws > 1:
+            obj = [S.nccl_unique_id() if rank == 0 else None]
+            torch.distributed.broadcast_object_list(obj, src=0)
+            pm.attach_shard(obj[0], ws, rank)
+        prompts = np.random.default_rng(args.seed).integers(
+            0, vocab, (PREFILL_SEQS, PREFILL_LEN)).astype(np.int32)
+        pm.prefill_batch(prompts)  # warm-up
+        barrier()
+        pev0, pev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pstream = torch.cuda.ExternalStream(pm.stream)
+        pev0.record(pstream)
+        first = pm.prefill_batch(prompts)
+        pev1.record(pstream)
+        pstream.synchronize()
+        pms = max_ranks(pev0.elapsed_time(pev1))
+        prefill = {"value": PREFILL_SEQS * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
+                   "ms": pms, "workload": f"{PREFILL_SEQS} prompts x {PREFILL_LEN} tokens, "
+                   "SmolLM2-135M shape, batched causal prefill to the first greedy token",
+                   "sharding": (f"(sequence, KV head) units over {ws} ranks, one NCCL "
+                                "all-gather of attention outputs per layer before Wo")
+                   if ws > 1 else "one GPU",
+                   "first_tokens": [int(t) for t in first[:4]]}
+        pm.close()
+
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
         "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -438,9 +476,10 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * GLOBAL_BATCH,
                 "d2h_bytes_per_step": 4 * GLOBAL_BATCH,
                 "api": "slm_model_decode_batch (host token/position arrays in, next tokens out)"},
-        "gpu_launches": model.launches_per_decode_step(B) * K,
+        "gpu_launches": gpu_launches,
         "clocks": clk,
         "setup_s": round(setup_s, 1),
+        "prefill": prefill,
     }
     if cpu:
         line["cpu_baseline"] = cpu
@@ -450,7 +489,8 @@ def run_ours(args):
         line["note"] = "profiling case with fewer layers: not a bench value"
     if rank == 0:
         print(json.dumps(line), flush=True)
-    model.close()
+    if model is not None:
+        model.close()
     if ws > 1:
         torch.distributed.destroy_process_group()
     return 0
