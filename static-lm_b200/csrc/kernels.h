@@ -150,6 +150,9 @@ struct AttnArgs {
     // unit (r / rows_per_seq) * num_kv_heads + g is congruent to shard_r
     // modulo shard_n.  shard_n <= 1: every unit.
     int shard_n, shard_r, rows_per_seq;
+    // prefill (fused path): rows come in runs of prefill_run rows holding
+    // consecutive positions of one sequence (0 = no such structure)
+    int prefill_run;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)

@@ -529,6 +529,166 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
     }
 }
 
+// (P1) prefill scores, query-tiled: rows come in runs of consecutive
+// positions (the tokens of one prompt); an item is (run, PQT query rows,
+// KV head, 128-key tile) of the causal triangle.  A producer warp fetches the
+// K tile (swizzled boxes as in (A')) and the tile's query vectors (one bulk
+// copy per row) into one of two stages; consumer thread t loads key t's K row
+// into registers once and runs every (row, head) dot of the tile against it,
+// sequential in i as in (A), so each K tile crosses the memory system once
+// per PQT query rows instead of once per row.
+constexpr int PQT = 16;
+
+struct PrefillItem {
+    int r0, nr, p0, g, t0;
+};
+
+__host__ __device__ inline size_t prefill_stage_bytes(int kv_mul, int hd) {
+    return ((size_t)(hd / 32) * TILE_KEYS * 128 + sizeof(float) * PQT * kv_mul * hd + 1023) / 1024 * 1024;
+}
+
+template <int KVM, int HD>
+__global__ void __launch_bounds__(TILE_KEYS + 32)
+    attn_prefill_scores_kernel(AttnArgs a, int run, int nqt, int nkt,
+                               const __grid_constant__ CUtensorMap kmap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar_full[SCORE_STAGES], bar_empty[SCORE_STAGES];
+    __shared__ PrefillItem s_item[SCORE_STAGES];
+    __shared__ int s_abort, s_issued;
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    constexpr int nbox = HD / 32, QW = KVM * HD;  // floats of one row's query vectors
+    const size_t stage_bytes = prefill_stage_bytes(KVM, HD);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const long long n_items = (long long)(a.rows / run) * nqt * a.num_kv_heads * nkt;
+    if (tid == 0) {
+        for (int st = 0; st < SCORE_STAGES; st++) {
+            mbar_init(&bar_full[st], 1);
+            mbar_init(&bar_empty[st], SCORE_CONS_WARPS);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_wait();  // q and the K rows of this prompt come from the QKV kernel
+    pdl_release();
+
+    if (warp == SCORE_CONS_WARPS) {
+        // ---- producer
+        int n = 0;
+        for (long long it = blockIdx.x; ; it += gridDim.x) {
+            PrefillItem item{-1, 0, 0, 0, 0};
+            if (it < n_items) {
+                const int kt = (int)(it % nkt);
+                long long rest = it / nkt;
+                item.g = (int)(rest % a.num_kv_heads);
+                rest /= a.num_kv_heads;
+                const int qt = (int)(rest % nqt);
+                const int run_i = (int)(rest / nqt);
+                item.r0 = run_i * run + qt * PQT;
+                item.nr = run - qt * PQT < PQT ? run - qt * PQT : PQT;
+                if (!unit_owned(a, item.r0, item.g)) continue;  // another rank's unit
+                item.p0 = a.pos ? a.pos[item.r0] : a.pos_const;
+                int lmax = item.p0 + item.nr;  // keys of the tile's last row
+                lmax = lmax < a.max_seq ? lmax : a.max_seq;
+                lmax = lmax < a.max_len ? lmax : a.max_len;
+                item.t0 = kt * TILE_KEYS;
+                if (item.t0 >= lmax) continue;  // above the causal triangle
+            }
+            const int st = n % SCORE_STAGES;
+            if (n >= SCORE_STAGES &&
+                !mbar_wait(&bar_empty[st], (unsigned)((n / SCORE_STAGES) - 1) & 1u, &s_abort, a.err))
+                break;
+            unsigned char *dst = base + (size_t)st * stage_bytes;
+            if (lane == 0) {
+                s_item[st] = item;
+                if (item.r0 < 0) {
+                    mbar_arrive(&bar_full[st]);  // end marker, no bytes
+                } else {
+                    const int kz = (int)((long long)row_slot(a, item.r0) * a.z_slot + a.z_layer);
+                    mbar_arrive_expect_tx(&bar_full[st],
+                                          (unsigned)nbox * TILE_KEYS * 128u + (unsigned)(item.nr * QW) * 4u);
+                    for (int b = 0; b < nbox; b++)
+                        tma_load_3d(dst + (size_t)b * TILE_KEYS * 128, &kmap, item.g * HD + 32 * b,
+                                    item.t0, kz, &bar_full[st]);
+                }
+                s_issued = n + 1;
+            }
+            __syncwarp();
+            if (item.r0 >= 0 && lane < item.nr) {
+                float *q_dst = reinterpret_cast<float *>(dst + (size_t)nbox * TILE_KEYS * 128) + lane * QW;
+                bulk_copy(q_dst, a.q + (size_t)(item.r0 + lane) * a.ldq + (size_t)item.g * QW,
+                          (unsigned)QW * 4u, &bar_full[st]);
+            }
+            __syncwarp();
+            n++;
+            if (item.r0 < 0) break;
+        }
+    } else {
+        // ---- consumers: thread t = key t0 + t
+        const unsigned sw = (unsigned)(tid & 7);
+        for (int n = 0; ; n++) {
+            const int st = n % SCORE_STAGES;
+            if (!mbar_wait(&bar_full[st], (unsigned)(n / SCORE_STAGES) & 1u, &s_abort, a.err)) break;
+            const PrefillItem item = s_item[st];
+            if (item.r0 < 0) break;
+            const unsigned char *s_k = base + (size_t)st * stage_bytes;
+            const float *s_q = reinterpret_cast<const float *>(s_k + (size_t)nbox * TILE_KEYS * 128);
+            float kr[HD];
+#pragma unroll
+            for (int b = 0; b < nbox; b++) {
+                const unsigned char *row = s_k + (size_t)b * TILE_KEYS * 128 + (size_t)tid * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const float4 kk = *reinterpret_cast<const float4 *>(row + ((c ^ sw) << 4));
+                    kr[b * 32 + c * 4 + 0] = kk.x;
+                    kr[b * 32 + c * 4 + 1] = kk.y;
+                    kr[b * 32 + c * 4 + 2] = kk.z;
+                    kr[b * 32 + c * 4 + 3] = kk.w;
+                }
+            }
+            const int key = item.t0 + tid;
+            for (int i = 0; i < item.nr; i++) {
+                int L = item.p0 + i + 1;  // keys of row r0+i
+                L = L < a.max_seq ? L : a.max_seq;
+                L = L < a.max_len ? L : a.max_len;
+                if (key >= L) continue;  // the causal mask (later rows see more keys)
+                float dot[KVM];
+#pragma unroll
+                for (int h = 0; h < KVM; h++) dot[h] = 0.0f;
+                const float4 *q4 = reinterpret_cast<const float4 *>(s_q + i * QW);
+#pragma unroll
+                for (int v = 0; v < HD / 4; v++) {
+#pragma unroll
+                    for (int h = 0; h < KVM; h++) {
+                        const float4 qq = q4[h * (HD / 4) + v];
+                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.x, kr[4 * v + 0]));
+                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.y, kr[4 * v + 1]));
+                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.z, kr[4 * v + 2]));
+                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.w, kr[4 * v + 3]));
+                    }
+                }
+                float *att = a.att + ((size_t)(item.r0 + i) * a.num_heads + (size_t)item.g * KVM) * a.att_ld + key;
+#pragma unroll
+                for (int h = 0; h < KVM; h++) att[(size_t)h * a.att_ld] = __fmul_rn(dot[h], a.scale);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[st]);
+        }
+    }
+    __syncthreads();
+    if (s_abort && tid == 0) {
+        // a wait gave up: let the copies already issued land (bounded)
+        const int n_iss = s_issued;
+        for (int k = n_iss - SCORE_STAGES < 0 ? 0 : n_iss - SCORE_STAGES; k < n_iss; k++) {
+            const long long t0 = clock64();
+            while (!mbar_test(&bar_full[k % SCORE_STAGES], (unsigned)(k / SCORE_STAGES) & 1u) &&
+                   clock64() - t0 < WAIT_LIMIT) {
+            }
+        }
+    }
+}
+
 // (B) softmax + PV: one CTA per (row, KV head), warp-specialized.  One
 // producer thread owns every copy of V: each stage is one TMA box (TT_V
 // positions x head_dim floats of this KV head) of a 3-D tensor map over the
@@ -907,7 +1067,40 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
     // the pipelined kernel bulk-copies the query vectors: 16-byte aligned rows
     const bool q_bulk = ((uintptr_t)a.q & 15) == 0 && (a.ldq & 3) == 0;
     const bool pipe = kmap && a.head_dim % 32 == 0 && q_bulk;
-    if (pipe) {
+    const bool prefill_tiles = pipe && a.prefill_run > 0 && a.rows % a.prefill_run == 0 &&
+                               (a.head_dim == 32 || a.head_dim == 64) && kv_mul <= 4;
+    if (prefill_tiles) {
+        // query-tiled: one K tile per PQT rows of a prompt
+        const int run = a.prefill_run, nqt = (run + PQT - 1) / PQT;
+        const int nkt = (a.max_len + TILE_KEYS - 1) / TILE_KEYS;
+        const long long items = (long long)(a.rows / run) * nqt * a.num_kv_heads * nkt;
+        const size_t sk = SCORE_STAGES * prefill_stage_bytes(kv_mul, a.head_dim) + 1024;
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int per_sm = (int)((200 * 1024) / sk) < 2 ? (int)((200 * 1024) / sk) : 2;
+        long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
+        if (grid > items) grid = items;
+        auto go = [&](auto kern) {
+            launch_kernel(kern, dim3((unsigned)grid), dim3(TILE_KEYS + 32), sk, s, a.pdl, a, run, nqt,
+                          nkt, *kmap);
+        };
+        if (a.head_dim == 32) {
+            switch (kv_mul) {
+                case 1: go(attn_prefill_scores_kernel<1, 32>); break;
+                case 2: go(attn_prefill_scores_kernel<2, 32>); break;
+                case 3: go(attn_prefill_scores_kernel<3, 32>); break;
+                default: go(attn_prefill_scores_kernel<4, 32>); break;
+            }
+        } else {
+            switch (kv_mul) {
+                case 1: go(attn_prefill_scores_kernel<1, 64>); break;
+                case 2: go(attn_prefill_scores_kernel<2, 64>); break;
+                case 3: go(attn_prefill_scores_kernel<3, 64>); break;
+                default: go(attn_prefill_scores_kernel<4, 64>); break;
+            }
+        }
+    } else if (pipe) {
         // pipelined: a few CTAs per SM walk all (row, KV head, tile) items
         const int ntile_max = (a.max_len + TILE_KEYS - 1) / TILE_KEYS;
         const long long items = (long long)a.rows * a.num_kv_heads * ntile_max;
@@ -948,6 +1141,14 @@ void set_attention_smem_limit(int bytes) {
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<1, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<3, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<4, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<1, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<2, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<3, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_scores_kernel<4, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 

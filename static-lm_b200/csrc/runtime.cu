@@ -603,6 +603,7 @@ struct slm_model {
     bool split_decode = true;
     bool fuse_norm = true;   // RMSNorm + Q8 inside the QKV and gate/up GEMVs
     bool use_pdl = true;     // programmatic dependent launch between decode kernels
+    bool no_prefill_tiles = false;  // SLM_PREFILL_ROWWISE=1: prefill through the per-row kernels
     int parts = 4;           // decode parts (streams) for batches of 16+ rows
     cudaStream_t side[MAX_PARTS - 1] = {};  // streams of parts 1..
     cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
@@ -748,6 +749,9 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     // a batched prefill on a sharded model computes only this rank's
     // (sequence, KV head) units, then all-gathers the outputs before Wo
     const bool sharded = kind == STEP_PREFILL_BATCH && m->shard_n > 1 && fused;
+    // prefill rows are runs of consecutive positions of one sequence
+    aa.prefill_run = kind == STEP_PREFILL ? n : kind == STEP_PREFILL_BATCH ? seq_rows : 0;
+    if (m->no_prefill_tiles) aa.prefill_run = 0;
     if (kind == STEP_PREFILL_BATCH) {
         aa.rows_per_seq = seq_rows;
         aa.shard_n = sharded ? m->shard_n : 1;
@@ -1154,6 +1158,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->split_decode = !(env && env[0] == '1');
     env = getenv("SLM_DECODE_PARTS");
     if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
+    env = getenv("SLM_PREFILL_ROWWISE");
+    m->no_prefill_tiles = env && env[0] == '1';
     env = getenv("SLM_NO_PDL");
     m->use_pdl = !(env && env[0] == '1');
     env = getenv("SLM_UNFUSED_NORM");
