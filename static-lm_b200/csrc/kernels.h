@@ -168,8 +168,14 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
 // (head_dim % 4 and <= 224, kv_mul <= 8, 16-byte bases, scores fit in
 // shared memory).
 bool attention_fused_ok(const AttnArgs &a);
+// amap: the tensor map of encode_att_map over the att scratch (null = no
+// query-tiled prefill softmax/PV)
 void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       cudaStream_t s);
+                       const CUtensorMap *amap, cudaStream_t s);
+// 3-D tensor map over att [rows][heads][att_ld] f32, box = 64 positions x
+// kv_mul heads x 16 rows (the prefill probability tiles).
+bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, uint64_t rows,
+                    int kv_mul);
 // 3-D tensor map over `planes` consecutive [max_seq][kv_dim] f32 planes from
 // `base`, box = head_dim floats x 64 positions x 1 plane.  False when the
 // driver entry point is missing or the shape is not expressible (the caller

@@ -689,6 +689,234 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
     }
 }
 
+// (P2) prefill softmax + PV, query-tiled: one CTA per (run, PQT query rows,
+// KV head).  The softmax of the tile's PQT x kv_mul (row, head) score rows
+// runs over att (L2-resident) in the reference's order -- max, exp, four lane
+// chains + tail, 1/sum, p = e * inv written back -- then a producer warp
+// streams, per 64-key stage, the V tile (tensor map over the V planes) and
+// the probability tile [PQT rows][kv_mul heads][64 keys] (tensor map over
+// att) into a ring; consumer thread (dim pair, row group) runs the PV chains
+// of its rows and heads, sequential in t, masking each row's keys past its
+// own position.  The probabilities are written with ordinary stores and read
+// by TMA (the async proxy): every thread fences before the barrier that
+// precedes the first TMA issue.
+constexpr int PPV_TT = 64;
+static_assert(PPV_TT == TT_V, "the V tensor map's box holds PPV_TT positions");
+constexpr int PPV_STAGES = 3;
+constexpr int PPV_CONS = 256;  // consumer threads
+
+__host__ __device__ inline size_t ppv_stage_bytes(int kv_mul, int hd) {
+    return ((size_t)PPV_TT * hd * 4 + (size_t)PQT * kv_mul * PPV_TT * 4 + 127) / 128 * 128;
+}
+
+template <int KVM, int HD>
+__global__ void __launch_bounds__(PPV_CONS + 32)
+    attn_prefill_softmax_pv_kernel(AttnArgs a, int run, const __grid_constant__ CUtensorMap vmap,
+                                   const __grid_constant__ CUtensorMap amap) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar_full[PPV_STAGES], bar_empty[PPV_STAGES];
+    __shared__ int s_abort, s_issued;
+    __shared__ float s_max[PQT * KVM], s_inv[PQT * KVM], s_chain[4 * PQT * KVM];
+    unsigned char *base = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+    constexpr int DP = HD / 2;               // dim pairs
+    constexpr int RG = PPV_CONS / DP;        // row groups
+    constexpr int RPG = PQT / RG;            // rows per group
+    static_assert(RPG * RG == PQT && RPG >= 1, "tile shape");
+    const int qt = blockIdx.x, g = blockIdx.y, run_i = blockIdx.z;
+    const int r0 = run_i * run + qt * PQT;
+    const int nr = run - qt * PQT < PQT ? run - qt * PQT : PQT;
+    if (!unit_owned(a, r0, g)) return;  // CTA-uniform: another rank's unit
+    const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31;
+    const int nw = nth >> 5;
+    const int p0 = a.pos ? a.pos[r0] : a.pos_const;
+    auto row_L = [&](int i) {
+        int L = p0 + i + 1;
+        L = L < a.max_seq ? L : a.max_seq;
+        return L < a.max_len ? L : a.max_len;
+    };
+    const int npairs = nr * KVM;
+    auto prow = [&](int pr) {  // score / probability row of pair pr = i*KVM + h
+        return a.att + ((size_t)(r0 + pr / KVM) * a.num_heads + (size_t)g * KVM + pr % KVM) * a.att_ld;
+    };
+    const size_t stage_bytes = ppv_stage_bytes(KVM, HD);
+    if (tid == 0) {
+        for (int st = 0; st < PPV_STAGES; st++) {
+            mbar_init(&bar_full[st], 1);
+            mbar_init(&bar_empty[st], PPV_CONS / 32);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        mbar_fence_init();
+    }
+    pdl_wait();  // the score rows come from the scores kernel
+    __syncthreads();
+
+    // ---- softmax of every pair (graph.rs:168-179 order)
+    for (int pr = warp; pr < npairs; pr += nw) {
+        const float *row = prow(pr);
+        const int L = row_L(pr / KVM);
+        float m = -INFINITY;
+        for (int t = lane; t < L; t += 32) m = cl_fmax(m, row[t]);
+        for (int o = 16; o > 0; o >>= 1) m = cl_fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_max[pr] = m;
+    }
+    __syncthreads();
+    for (int pr = 0; pr < npairs; pr++) {
+        float *row = prow(pr);
+        const float mx = s_max[pr];
+        const int L = row_L(pr / KVM);
+        for (int t = tid; t < L; t += nth) row[t] = exp_poly(__fsub_rn(row[t], mx));
+    }
+    __syncthreads();
+    if (tid < 4 * npairs) {
+        // lane chain l of pair pr over [0, L & ~3), loads eight steps ahead
+        const int pr = tid >> 2, l = tid & 3;
+        const float *e = prow(pr);
+        const int vl = row_L(pr / KVM) & ~3;
+        float acc = 0.0f;
+        int i = l;
+        for (; i + 28 < vl; i += 32) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = e[i + 4 * u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; i < vl; i += 4) acc = __fadd_rn(acc, e[i]);
+        s_chain[tid] = acc;
+    }
+    __syncthreads();
+    if (tid < npairs) {
+        const float *e = prow(tid);
+        const int L = row_L(tid / KVM), vl = L & ~3;
+        float sum = __fadd_rn(__fadd_rn(s_chain[4 * tid], s_chain[4 * tid + 1]),
+                              __fadd_rn(s_chain[4 * tid + 2], s_chain[4 * tid + 3]));
+        for (int i = vl; i < L; i++) sum = __fadd_rn(sum, e[i]);
+        s_inv[tid] = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    for (int pr = 0; pr < npairs; pr++) {
+        float *row = prow(pr);
+        const float inv = s_inv[pr];
+        const int L = row_L(pr / KVM);
+        for (int t = tid; t < L; t += nth) row[t] = __fmul_rn(row[t], inv);
+    }
+    // the probabilities are read next by TMA (async proxy)
+    __threadfence();
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");
+    __syncthreads();
+
+    // ---- out = sum_t p_t * v_t per (row, head, dim), sequential in t
+    const int Lmax = row_L(nr - 1);
+    const int ntiles = (Lmax + PPV_TT - 1) / PPV_TT;
+    const unsigned tile_tx = (unsigned)(PPV_TT * HD * 4 + PQT * KVM * PPV_TT * 4);
+    if (warp == PPV_CONS / 32) {
+        // ---- producer
+        const int vz = (int)((long long)row_slot(a, r0) * a.z_slot + a.z_layer);
+        for (int k = 0; k < ntiles; k++) {
+            const int st = k % PPV_STAGES;
+            if (k >= PPV_STAGES &&
+                !mbar_wait(&bar_empty[st], (unsigned)((k / PPV_STAGES) - 1) & 1u, &s_abort, a.err))
+                break;
+            if (lane == 0) {
+                unsigned char *dst = base + (size_t)st * stage_bytes;
+                mbar_arrive_expect_tx(&bar_full[st], tile_tx);
+                tma_load_3d(dst, &vmap, g * HD, k * PPV_TT, vz, &bar_full[st]);
+                tma_load_3d(dst + (size_t)PPV_TT * HD * 4, &amap, k * PPV_TT, g * KVM, r0, &bar_full[st]);
+                s_issued = k + 1;
+            }
+            __syncwarp();
+        }
+    } else {
+        // ---- consumers: dims 2*dp, 2*dp+1 of rows rg*RPG .. rg*RPG+RPG-1, all heads
+        const int dp = tid % DP, rg = tid / DP;
+        int Lr[RPG];
+#pragma unroll
+        for (int ii = 0; ii < RPG; ii++) Lr[ii] = rg * RPG + ii < nr ? row_L(rg * RPG + ii) : 0;
+        float acc[RPG][KVM][2];
+#pragma unroll
+        for (int ii = 0; ii < RPG; ii++)
+#pragma unroll
+            for (int h = 0; h < KVM; h++) acc[ii][h][0] = acc[ii][h][1] = 0.0f;
+        for (int k = 0; k < ntiles; k++) {
+            const int st = k % PPV_STAGES;
+            if (!mbar_wait(&bar_full[st], (unsigned)(k / PPV_STAGES) & 1u, &s_abort, a.err)) break;
+            const unsigned char *stg = base + (size_t)st * stage_bytes;
+            const float2 *vt = reinterpret_cast<const float2 *>(stg) + dp;  // row stride DP pairs
+            const float *pt = reinterpret_cast<const float *>(stg + (size_t)PPV_TT * HD * 4);
+            const int t0 = k * PPV_TT;
+            bool full = true;
+#pragma unroll
+            for (int ii = 0; ii < RPG; ii++) full = full && (Lr[ii] >= t0 + PPV_TT || Lr[ii] == 0);
+            if (full) {
+#pragma unroll 4
+                for (int u0 = 0; u0 < PPV_TT; u0 += 4) {
+                    float2 vv[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) vv[u] = vt[(u0 + u) * DP];
+#pragma unroll
+                    for (int ii = 0; ii < RPG; ii++) {
+#pragma unroll
+                        for (int h = 0; h < KVM; h++) {
+                            const float4 p4 = *reinterpret_cast<const float4 *>(
+                                pt + ((rg * RPG + ii) * KVM + h) * PPV_TT + u0);
+                            acc[ii][h][0] = __fadd_rn(acc[ii][h][0], __fmul_rn(p4.x, vv[0].x));
+                            acc[ii][h][1] = __fadd_rn(acc[ii][h][1], __fmul_rn(p4.x, vv[0].y));
+                            acc[ii][h][0] = __fadd_rn(acc[ii][h][0], __fmul_rn(p4.y, vv[1].x));
+                            acc[ii][h][1] = __fadd_rn(acc[ii][h][1], __fmul_rn(p4.y, vv[1].y));
+                            acc[ii][h][0] = __fadd_rn(acc[ii][h][0], __fmul_rn(p4.z, vv[2].x));
+                            acc[ii][h][1] = __fadd_rn(acc[ii][h][1], __fmul_rn(p4.z, vv[2].y));
+                            acc[ii][h][0] = __fadd_rn(acc[ii][h][0], __fmul_rn(p4.w, vv[3].x));
+                            acc[ii][h][1] = __fadd_rn(acc[ii][h][1], __fmul_rn(p4.w, vv[3].y));
+                        }
+                    }
+                }
+            } else {
+                for (int u = 0; u < PPV_TT; u++) {
+                    const float2 v = vt[u * DP];
+#pragma unroll
+                    for (int ii = 0; ii < RPG; ii++) {
+                        if (t0 + u < Lr[ii]) {
+#pragma unroll
+                            for (int h = 0; h < KVM; h++) {
+                                const float pv = pt[((rg * RPG + ii) * KVM + h) * PPV_TT + u];
+                                acc[ii][h][0] = __fadd_rn(acc[ii][h][0], __fmul_rn(pv, v.x));
+                                acc[ii][h][1] = __fadd_rn(acc[ii][h][1], __fmul_rn(pv, v.y));
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[st]);
+        }
+        if (!s_abort) {
+#pragma unroll
+            for (int ii = 0; ii < RPG; ii++) {
+                const int i = rg * RPG + ii;
+                if (i < nr) {
+#pragma unroll
+                    for (int h = 0; h < KVM; h++)
+                        *reinterpret_cast<float2 *>(a.out + (size_t)(r0 + i) * a.ldo + (size_t)(g * KVM + h) * HD +
+                                                    2 * dp) = make_float2(acc[ii][h][0], acc[ii][h][1]);
+                }
+            }
+        }
+    }
+    pdl_release();
+    __syncthreads();
+    if (s_abort && tid == 0) {
+        // a wait gave up: let the copies already issued land (bounded)
+        const int n_iss = s_issued;
+        for (int k = n_iss - PPV_STAGES < 0 ? 0 : n_iss - PPV_STAGES; k < n_iss; k++) {
+            const long long t0 = clock64();
+            while (!mbar_test(&bar_full[k % PPV_STAGES], (unsigned)(k / PPV_STAGES) & 1u) &&
+                   clock64() - t0 < WAIT_LIMIT) {
+            }
+        }
+    }
+}
+
 // (B) softmax + PV: one CTA per (row, KV head), warp-specialized.  One
 // producer thread owns every copy of V: each stage is one TMA box (TT_V
 // positions x head_dim floats of this KV head) of a 3-D tensor map over the
@@ -1048,6 +1276,21 @@ bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, uint64_t rows,
+                    int kv_mul) {
+    const EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || !att || ((uintptr_t)att & 15) || (att_ld & 3) || att_ld < PPV_TT || kv_mul < 1 ||
+        kv_mul > heads || heads > 256 || rows == 0 || rows > 0x7fffffffULL)
+        return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)att_ld, (cuuint64_t)heads, (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)att_ld * 4, (cuuint64_t)att_ld * 4 * (cuuint64_t)heads};
+    const cuuint32_t box[3] = {(cuuint32_t)PPV_TT, (cuuint32_t)kv_mul, (cuuint32_t)PQT};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(att), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool attention_fused_ok(const AttnArgs &a) {
     const int kv_mul = a.num_heads / a.num_kv_heads;
     if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 992) return false;
@@ -1059,7 +1302,7 @@ bool attention_fused_ok(const AttnArgs &a) {
 }
 
 void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       cudaStream_t s) {
+                       const CUtensorMap *amap, cudaStream_t s) {
     if (args.rows <= 0) return;
     AttnArgs a = args;
     const int kv_mul = a.num_heads / a.num_kv_heads;
@@ -1117,6 +1360,32 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
         attn_scores_tiled_kernel<<<g1, TILE_KEYS, sk, s>>>(a);
     }
+    if (prefill_tiles && amap) {
+        // query-tiled softmax + PV, then the Q8_0 of the output if asked for
+        const int run = a.prefill_run, nqt = (run + PQT - 1) / PQT;
+        const size_t sp = PPV_STAGES * ppv_stage_bytes(kv_mul, a.head_dim) + 128;
+        const dim3 grid((unsigned)nqt, (unsigned)a.num_kv_heads, (unsigned)(a.rows / run));
+        auto go = [&](auto kern) {
+            launch_kernel(kern, grid, dim3(PPV_CONS + 32), sp, s, a.pdl, a, run, vmap, *amap);
+        };
+        if (a.head_dim == 32) {
+            switch (kv_mul) {
+                case 1: go(attn_prefill_softmax_pv_kernel<1, 32>); break;
+                case 2: go(attn_prefill_softmax_pv_kernel<2, 32>); break;
+                case 3: go(attn_prefill_softmax_pv_kernel<3, 32>); break;
+                default: go(attn_prefill_softmax_pv_kernel<4, 32>); break;
+            }
+        } else {
+            switch (kv_mul) {
+                case 1: go(attn_prefill_softmax_pv_kernel<1, 64>); break;
+                case 2: go(attn_prefill_softmax_pv_kernel<2, 64>); break;
+                case 3: go(attn_prefill_softmax_pv_kernel<3, 64>); break;
+                default: go(attn_prefill_softmax_pv_kernel<4, 64>); break;
+            }
+        }
+        if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
+        return;
+    }
     switch (kv_mul) {
         case 1: launch_softmax_pv<1>(a, vmap, s); break;
         case 2: launch_softmax_pv<2>(a, vmap, s); break;
@@ -1141,6 +1410,14 @@ void set_attention_smem_limit(int bytes) {
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<1, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<3, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<4, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<1, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<2, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<3, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_prefill_softmax_pv_kernel<4, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_prefill_scores_kernel<1, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_prefill_scores_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_prefill_scores_kernel<3, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -1175,7 +1452,7 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s) {
 void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
                       cudaStream_t s) {
     if (vmap && attention_fused_ok(a)) {
-        launch_attn_fused(a, *vmap, kmap, s);
+        launch_attn_fused(a, *vmap, kmap, nullptr, s);
         return;
     }
     launch_attn_scores(a, s);

@@ -609,7 +609,8 @@ struct slm_model {
     cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
     CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
-    bool have_vmap = false, have_kmap = false;
+    CUtensorMap amap;        // att scratch, probability tiles of the prefill softmax/PV
+    bool have_vmap = false, have_kmap = false, have_amap = false;
     // KV-head-sharded batched prefill (slm_model_attach_shard)
     int shard_n = 1, shard_r = 0;
     ncclComm_t comm = nullptr;
@@ -798,7 +799,8 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         aa.z_layer = 2LL * l;
         if (fused) {
             // scores, then softmax + PV + the Q8_0 of the output
-            launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr, st);
+            launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr,
+                              m->have_amap && row0 == 0 ? &m->amap : nullptr, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
             if (sharded) {
                 // this rank's units -> all ranks: one all-gather before Wo
@@ -1171,6 +1173,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     // K plane (slot, layer) at z = slot*2L + 2*layer from the cache start
     m->have_kmap = encode_k_map(&m->kmap, m->kv, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd);
+    m->have_amap = encode_att_map(&m->amap, m->att, (int)cfg->max_seq_len, (int)cfg->num_heads,
+                                  (uint64_t)R, (int)(cfg->num_heads / cfg->num_kv_heads));
     *out = m;
     return SLM_OK;
 }

@@ -93,3 +93,25 @@ def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda):
         assert nxt == want, rank
         for s in range(nseq):
             assert np.array_equal(logits[s], ref.logits(s)), (rank, s)
+
+
+def test_tiled_prefill_matches_oracle_and_rowwise_kernels(cuda):
+    """GQA (kv_mul 3, head_dim 64): a 150-token prompt (several 128-key and
+    64-key tiles, a partial 16-row query tile), then 37 more tokens from
+    start_pos 150; logits equal the oracle's and the per-row kernels'."""
+    import oracle as O
+    cfg, _, vocab = synth.config("cfg3", max_seq_len=256)
+    w = synth.synth_model(cfg, 2, vocab, seed=23)
+    toks = _prompts(vocab, 1, 187, 6)[0]
+    tiled = S.Model(cfg, w, max_sequences=1, max_rows=160)
+    os.environ["SLM_PREFILL_ROWWISE"] = "1"
+    try:
+        rowwise = S.Model(cfg, w, max_sequences=1, max_rows=160)
+    finally:
+        del os.environ["SLM_PREFILL_ROWWISE"]
+    o = O.Model(cfg, w, threads=4)
+    for lo, hi in ((0, 150), (150, 187)):
+        want = o.prefill_tokens(list(toks[lo:hi]), lo)
+        for m in (tiled, rowwise):
+            assert m.prefill_tokens(toks[lo:hi], start_pos=lo) == want
+            assert np.array_equal(m.logits(0), o.logits())
