@@ -99,4 +99,17 @@ __device__ __forceinline__ void pdl_release() {
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// Named barrier `id` over `count` threads (whole warps) that also returns the
+// OR of `pred` over them, so every participant takes the same branch after it.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+    int r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n"
+        " bar.red.or.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((int)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 }  // namespace slm

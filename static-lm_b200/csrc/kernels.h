@@ -153,6 +153,10 @@ struct AttnArgs {
     // prefill (fused path): rows come in runs of prefill_run rows holding
     // consecutive positions of one sequence (0 = no such structure)
     int prefill_run;
+    // prefill (optional): maxima of every 32 scores of each (row, head),
+    // [rows][num_heads][tmax_ld], tmax_ld >= ceil(max_len/32)
+    float *tmax;
+    int tmax_ld;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)

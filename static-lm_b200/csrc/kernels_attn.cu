@@ -647,12 +647,12 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
                     kr[b * 32 + c * 4 + 3] = kk.w;
                 }
             }
-            const int key = item.t0 + tid;
+            const int key = item.t0 + tid, wkey = item.t0 + warp * 32;
             for (int i = 0; i < item.nr; i++) {
                 int L = item.p0 + i + 1;  // keys of row r0+i
                 L = L < a.max_seq ? L : a.max_seq;
                 L = L < a.max_len ? L : a.max_len;
-                if (key >= L) continue;  // the causal mask (later rows see more keys)
+                if (wkey >= L) continue;  // the causal mask, whole warp (later rows see more keys)
                 float dot[KVM];
 #pragma unroll
                 for (int h = 0; h < KVM; h++) dot[h] = 0.0f;
@@ -668,9 +668,21 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
                         dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.w, kr[4 * v + 3]));
                     }
                 }
-                float *att = a.att + ((size_t)(item.r0 + i) * a.num_heads + (size_t)item.g * KVM) * a.att_ld + key;
+                const size_t prow = (size_t)(item.r0 + i) * a.num_heads + (size_t)item.g * KVM;
+                float *att = a.att + prow * a.att_ld + key;
+                const bool live = key < L;  // lanes past the mask computed on whatever the tile held
 #pragma unroll
-                for (int h = 0; h < KVM; h++) att[(size_t)h * a.att_ld] = __fmul_rn(dot[h], a.scale);
+                for (int h = 0; h < KVM; h++) {
+                    const float sc = __fmul_rn(dot[h], a.scale);
+                    if (live) att[(size_t)h * a.att_ld] = sc;
+                    if (a.tmax) {
+                        // maximum of this warp's 32 scores (the softmax's fmax
+                        // semantics; masked keys do not take part)
+                        float m = live ? sc : -INFINITY;
+                        for (int o = 16; o > 0; o >>= 1) m = cl_fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+                        if (lane == 0) a.tmax[(prow + h) * a.tmax_ld + wkey / 32] = m;
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_empty[st]);
@@ -753,26 +765,28 @@ __global__ void __launch_bounds__(PPV_CONS + 32)
 
     // ---- softmax of every pair (graph.rs:168-179 order)
     for (int pr = warp; pr < npairs; pr += nw) {
-        const float *row = prow(pr);
         const int L = row_L(pr / KVM);
         float m = -INFINITY;
-        for (int t = lane; t < L; t += 32) m = cl_fmax(m, row[t]);
+        if (a.tmax) {  // from the scores kernel's per-32-key maxima
+            const float *tm = a.tmax + ((size_t)(r0 + pr / KVM) * a.num_heads + (size_t)g * KVM + pr % KVM) *
+                                           a.tmax_ld;
+            for (int j = lane; j < (L + 31) / 32; j += 32) m = cl_fmax(m, tm[j]);
+        } else {
+            const float *row = prow(pr);
+            for (int t = lane; t < L; t += 32) m = cl_fmax(m, row[t]);
+        }
         for (int o = 16; o > 0; o >>= 1) m = cl_fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) s_max[pr] = m;
     }
     __syncthreads();
-    for (int pr = 0; pr < npairs; pr++) {
-        float *row = prow(pr);
-        const float mx = s_max[pr];
-        const int L = row_L(pr / KVM);
-        for (int t = tid; t < L; t += nth) row[t] = exp_poly(__fsub_rn(row[t], mx));
-    }
-    __syncthreads();
     if (tid < 4 * npairs) {
-        // lane chain l of pair pr over [0, L & ~3), loads eight steps ahead
+        // lane chain l of pair pr over [0, L & ~3): this thread also forms the
+        // exps of its lane (off the dependent chain) and stores them; the
+        // scores are loaded eight steps ahead
         const int pr = tid >> 2, l = tid & 3;
-        const float *e = prow(pr);
-        const int vl = row_L(pr / KVM) & ~3;
+        float *e = prow(pr);
+        const float mx = s_max[pr];
+        const int L = row_L(pr / KVM), vl = L & ~3;
         float acc = 0.0f;
         int i = l;
         for (; i + 28 < vl; i += 32) {
@@ -780,10 +794,21 @@ __global__ void __launch_bounds__(PPV_CONS + 32)
 #pragma unroll
             for (int u = 0; u < 8; u++) v[u] = e[i + 4 * u];
 #pragma unroll
+            for (int u = 0; u < 8; u++) {
+                v[u] = exp_poly(__fsub_rn(v[u], mx));
+                e[i + 4 * u] = v[u];
+            }
+#pragma unroll
             for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
         }
-        for (; i < vl; i += 4) acc = __fadd_rn(acc, e[i]);
+        for (; i < vl; i += 4) {
+            const float ev = exp_poly(__fsub_rn(e[i], mx));
+            e[i] = ev;
+            acc = __fadd_rn(acc, ev);
+        }
         s_chain[tid] = acc;
+        if (l == 0)
+            for (int t = vl; t < L; t++) e[t] = exp_poly(__fsub_rn(e[t], mx));  // the tail
     }
     __syncthreads();
     if (tid < npairs) {
@@ -794,14 +819,8 @@ __global__ void __launch_bounds__(PPV_CONS + 32)
         for (int i = vl; i < L; i++) sum = __fadd_rn(sum, e[i]);
         s_inv[tid] = __fdiv_rn(1.0f, sum);
     }
-    __syncthreads();
-    for (int pr = 0; pr < npairs; pr++) {
-        float *row = prow(pr);
-        const float inv = s_inv[pr];
-        const int L = row_L(pr / KVM);
-        for (int t = tid; t < L; t += nth) row[t] = __fmul_rn(row[t], inv);
-    }
-    // the probabilities are read next by TMA (async proxy)
+    // the exps are read next by TMA (async proxy); p = e * inv is formed in
+    // shared memory when each tile lands
     __threadfence();
     asm volatile("fence.proxy.async.global;\n" ::: "memory");
     __syncthreads();
@@ -840,10 +859,20 @@ __global__ void __launch_bounds__(PPV_CONS + 32)
             for (int h = 0; h < KVM; h++) acc[ii][h][0] = acc[ii][h][1] = 0.0f;
         for (int k = 0; k < ntiles; k++) {
             const int st = k % PPV_STAGES;
-            if (!mbar_wait(&bar_full[st], (unsigned)(k / PPV_STAGES) & 1u, &s_abort, a.err)) break;
-            const unsigned char *stg = base + (size_t)st * stage_bytes;
+            const bool ok = mbar_wait(&bar_full[st], (unsigned)(k / PPV_STAGES) & 1u, &s_abort, a.err);
+            unsigned char *stg = base + (size_t)st * stage_bytes;
             const float2 *vt = reinterpret_cast<const float2 *>(stg) + dp;  // row stride DP pairs
-            const float *pt = reinterpret_cast<const float *>(stg + (size_t)PPV_TT * HD * 4);
+            float *ptw = reinterpret_cast<float *>(stg + (size_t)PPV_TT * HD * 4);
+            // p = e * (1/sum) of the tile's [PQT][KVM][64] entries, once, by
+            // all consumers; the barrier over the consumer warps also makes the
+            // give-up decision the same for all of them
+            if (ok)
+                for (int j = tid; j < PQT * KVM * PPV_TT; j += PPV_CONS) {
+                    const int pr = j / PPV_TT;
+                    if (pr < npairs) ptw[j] = __fmul_rn(ptw[j], s_inv[pr]);
+                }
+            if (named_bar_or(1, PPV_CONS, !ok)) break;
+            const float *pt = ptw;
             const int t0 = k * PPV_TT;
             bool full = true;
 #pragma unroll
@@ -1312,6 +1341,8 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
     const bool pipe = kmap && a.head_dim % 32 == 0 && q_bulk;
     const bool prefill_tiles = pipe && a.prefill_run > 0 && a.rows % a.prefill_run == 0 &&
                                (a.head_dim == 32 || a.head_dim == 64) && kv_mul <= 4;
+    // the per-32-key maxima are made and used only by the two prefill kernels
+    if (!(prefill_tiles && amap) || a.tmax_ld < (a.max_len + 31) / 32) a.tmax = nullptr;
     if (prefill_tiles) {
         // query-tiled: one K tile per PQT rows of a prompt
         const int run = a.prefill_run, nqt = (run + PQT - 1) / PQT;
@@ -1362,6 +1393,7 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
     }
     if (prefill_tiles && amap) {
         // query-tiled softmax + PV, then the Q8_0 of the output if asked for
+        // (the scores kernel above wrote the per-32-key maxima when a.tmax)
         const int run = a.prefill_run, nqt = (run + PQT - 1) / PQT;
         const size_t sp = PPV_STAGES * ppv_stage_bytes(kv_mul, a.head_dim) + 128;
         const dim3 grid((unsigned)nqt, (unsigned)a.num_kv_heads, (unsigned)(a.rows / run));

@@ -591,6 +591,8 @@ struct slm_model {
     slm_arena *arena = nullptr;
     // arena views
     float *rope_cos, *rope_sin, *x, *x_mid, *xb, *q, *logits, *att, *kv, *ybuf, *emb;
+    float *tmax = nullptr;   // [R][heads][tmax_ld] per-32-key score maxima (prefill)
+    int tmax_ld = 0;
     static constexpr int MAX_PARTS = 4;
     void *q8a[MAX_PARTS], *q8b[MAX_PARTS];  // Q8X scratch pairs of the decode parts
     uint64_t q8_blocks = 0;
@@ -743,6 +745,8 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     aa.err = m->d_err;
     aa.z_slot = 2LL * m->L;  // planes [slot][layer][K|V] from the first V plane
     aa.pdl = m->use_pdl;
+    aa.tmax = row0 == 0 ? m->tmax : nullptr;
+    aa.tmax_ld = m->tmax_ld;
 
     Q8X qa8 = q8view(m->q8a[part], m->q8_blocks), qb8 = q8view(m->q8b[part], m->q8_blocks);
     const bool fused = m->use_fused_attention && m->have_vmap && attention_fused_ok(aa);
@@ -1121,6 +1125,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     add_f(d);                                  // embedding accumulator
     add_f(S * V);                              // logits
     add_f(R * cfg->num_heads * T);             // att
+    m->tmax_ld = (int)((T + 31) / 32);
+    add_f(R * cfg->num_heads * (uint64_t)m->tmax_ld);  // score maxima
     for (int i = 0; i < 2 * slm_model::MAX_PARTS; i++) add_f(q8f);  // Q8X pair per decode part
     for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
     add_f(S * m->slot_stride);                 // KV
@@ -1134,7 +1140,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         (rc = alloc_view(m, R * d, &m->x_mid)) || (rc = alloc_view(m, R * d, &m->xb)) ||
         (rc = alloc_view(m, R * d, &m->q)) || (rc = alloc_view(m, R * d, &m->ybuf)) ||
         (rc = alloc_view(m, d, &m->emb)) || (rc = alloc_view(m, S * V, &m->logits)) ||
-        (rc = alloc_view(m, R * cfg->num_heads * T, &m->att)))
+        (rc = alloc_view(m, R * cfg->num_heads * T, &m->att)) ||
+        (rc = alloc_view(m, R * cfg->num_heads * (uint64_t)m->tmax_ld, &m->tmax)))
         return cleanup(rc);
     for (int i = 0; i < slm_model::MAX_PARTS; i++) {
         if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
