@@ -88,6 +88,14 @@ __device__ __forceinline__ float cl_fmin(float a, float b) {
     return (a != a || b != b) ? nan : r;
 }
 
+// Maximum over the warp of a float, NaN if any lane holds NaN (sm_100a
+// redux.sync on f32).  Zeros of either sign compare equal.
+__device__ __forceinline__ float warp_max_nan(float v) {
+    float r;
+    asm volatile("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;\n" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // The reference's polynomial exp (src/jit/lower.rs:22-65): clamp to
 // [-87.3, 88.3], n = nearest(x*log2 e), Cody-Waite split of n*ln2,
 // degree-5 Horner polynomial with separately rounded mul/add, times 2^n built

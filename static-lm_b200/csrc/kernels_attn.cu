@@ -648,39 +648,54 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
                 }
             }
             const int key = item.t0 + tid, wkey = item.t0 + warp * 32;
-            for (int i = 0; i < item.nr; i++) {
-                int L = item.p0 + i + 1;  // keys of row r0+i
+            auto row_keys = [&](int i) {  // keys of row r0+i (0 past the tile)
+                int L = item.p0 + i + 1;
                 L = L < a.max_seq ? L : a.max_seq;
                 L = L < a.max_len ? L : a.max_len;
-                if (wkey >= L) continue;  // the causal mask, whole warp (later rows see more keys)
-                float dot[KVM];
+                return i < item.nr ? L : 0;
+            };
+            // two query rows at a time: 2*KVM independent sequential chains
+            for (int i = 0; i < item.nr; i += 2) {
+                const int L0 = row_keys(i), L1 = row_keys(i + 1);
+                if (wkey >= (L0 > L1 ? L0 : L1)) continue;  // the causal mask, whole warp
+                float dot[2][KVM];
 #pragma unroll
-                for (int h = 0; h < KVM; h++) dot[h] = 0.0f;
+                for (int h = 0; h < KVM; h++) dot[0][h] = dot[1][h] = 0.0f;
+                // row i+1 past the tile reads stale q; its results are dropped
                 const float4 *q4 = reinterpret_cast<const float4 *>(s_q + i * QW);
 #pragma unroll
                 for (int v = 0; v < HD / 4; v++) {
 #pragma unroll
-                    for (int h = 0; h < KVM; h++) {
-                        const float4 qq = q4[h * (HD / 4) + v];
-                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.x, kr[4 * v + 0]));
-                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.y, kr[4 * v + 1]));
-                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.z, kr[4 * v + 2]));
-                        dot[h] = __fadd_rn(dot[h], __fmul_rn(qq.w, kr[4 * v + 3]));
+                    for (int j = 0; j < 2; j++) {
+#pragma unroll
+                        for (int h = 0; h < KVM; h++) {
+                            const float4 qq = q4[j * (QW / 4) + h * (HD / 4) + v];
+                            dot[j][h] = __fadd_rn(dot[j][h], __fmul_rn(qq.x, kr[4 * v + 0]));
+                            dot[j][h] = __fadd_rn(dot[j][h], __fmul_rn(qq.y, kr[4 * v + 1]));
+                            dot[j][h] = __fadd_rn(dot[j][h], __fmul_rn(qq.z, kr[4 * v + 2]));
+                            dot[j][h] = __fadd_rn(dot[j][h], __fmul_rn(qq.w, kr[4 * v + 3]));
+                        }
                     }
                 }
-                const size_t prow = (size_t)(item.r0 + i) * a.num_heads + (size_t)item.g * KVM;
-                float *att = a.att + prow * a.att_ld + key;
-                const bool live = key < L;  // lanes past the mask computed on whatever the tile held
 #pragma unroll
-                for (int h = 0; h < KVM; h++) {
-                    const float sc = __fmul_rn(dot[h], a.scale);
-                    if (live) att[(size_t)h * a.att_ld] = sc;
-                    if (a.tmax) {
-                        // maximum of this warp's 32 scores (the softmax's fmax
-                        // semantics; masked keys do not take part)
-                        float m = live ? sc : -INFINITY;
-                        for (int o = 16; o > 0; o >>= 1) m = cl_fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
-                        if (lane == 0) a.tmax[(prow + h) * a.tmax_ld + wkey / 32] = m;
+                for (int j = 0; j < 2; j++) {
+                    const int L = j ? L1 : L0;
+                    if (wkey >= L) continue;  // warp-uniform
+                    const size_t prow = (size_t)(item.r0 + i + j) * a.num_heads + (size_t)item.g * KVM;
+                    float *att = a.att + prow * a.att_ld + key;
+                    const bool live = key < L;  // lanes past the mask computed on whatever the tile held
+#pragma unroll
+                    for (int h = 0; h < KVM; h++) {
+                        const float sc = __fmul_rn(dot[j][h], a.scale);
+                        if (live) att[(size_t)h * a.att_ld] = sc;
+                        if (a.tmax) {
+                            // maximum of this warp's 32 scores, masked keys left
+                            // out; NaN propagates.  The sign of a zero maximum
+                            // does not matter to the softmax: exp(x - (+0)) and
+                            // exp(x - (-0)) are equal for every x.
+                            const float m = warp_max_nan(live ? sc : -INFINITY);
+                            if (lane == 0) a.tmax[(prow + h) * a.tmax_ld + wkey / 32] = m;
+                        }
                     }
                 }
             }
