@@ -85,6 +85,15 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Hint: bring one tile (box) of a 3-D tensor map from global memory into L2,
+// without a destination or a completion (no shared memory, nothing to wait on).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------
 // A kernel launched with the programmatic-serialization attribute may start
 // while its predecessor in the stream is still running.  It runs only work

@@ -972,8 +972,27 @@ __global__ void __launch_bounds__(PPV_CONS + 32)
 // load covering four positions.  When q8_out is
 // given, the output block this CTA owns is quantized for the Wo GEMV in the
 // same kernel.  Every mbarrier wait is bounded (mbar_wait).
-template <int KVM>
-__global__ void __launch_bounds__(1024)
+// PV consumer thread shape: NH query heads x ND consecutive dims of chains
+// per thread.  The launch uses (1, 2), a thread per (head, dim pair); (KVM, 1)
+// and (1, 1) were measured slower on B200.
+template <int ND>
+struct PvVec {
+    float v[ND];
+    __device__ __forceinline__ static PvVec load(const float *p) {
+        PvVec r;
+        if constexpr (ND == 2) {
+            const float2 t = *reinterpret_cast<const float2 *>(p);
+            r.v[0] = t.x;
+            r.v[1] = t.y;
+        } else {
+            r.v[0] = *p;
+        }
+        return r;
+    }
+};
+
+template <int KVM, int NH, int ND>
+__global__ void __launch_bounds__(512)
     attn_softmax_pv_kernel(AttnArgs a, int lp, const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t bar_full[FUSED_STAGES], bar_empty[FUSED_STAGES];
@@ -994,8 +1013,8 @@ __global__ void __launch_bounds__(1024)
     const int ntiles = (L + tt - 1) / tt;
     const int vx = g * hd;
     const int vz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
-    const int n_pairs = KVM * (hd >> 1);     // consumer threads: (head, dim pair)
-    const int n_cons = (n_pairs + 31) >> 5;  // consumer warps
+    const int n_thr = KVM * hd / (NH * ND);  // consumer threads: (NH heads, ND dims)
+    const int n_cons = (n_thr + 31) >> 5;  // consumer warps
     const int warp = tid >> 5, lane = tid & 31;
     const int nw = nth >> 5;
     const bool producer = warp == n_cons;  // the launch has n_cons + 1 warps or more
@@ -1161,66 +1180,93 @@ __global__ void __launch_bounds__(1024)
             __syncwarp();
         }
     } else if (warp < n_cons) {
-        const bool active = tid < n_pairs;
-        const int hl = tid / (hd >> 1), j2 = 2 * (tid - hl * (hd >> 1));
-        float acc0 = 0.0f, acc1 = 0.0f;  // out[hl][j2], out[hl][j2 + 1]
+        const bool active = tid < n_thr;
+        const int dgrp = hd / ND;  // threads per head group
+        const int h0 = (tid / dgrp) * NH, jc = ND * (tid % dgrp);
+        float acc[NH][ND];  // out[h0 + h][jc + c]
+#pragma unroll
+        for (int h = 0; h < NH; h++)
+#pragma unroll
+            for (int c = 0; c < ND; c++) acc[h][c] = 0.0f;
 #pragma unroll 1
         for (int k = 0; k < ntiles; k++) {
             if (!mbar_wait(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u, &s_abort,
                            a.err))
                 break;
             if (active) {
-                const float2 *vt = reinterpret_cast<const float2 *>(
-                    s_ring + (size_t)(k % FUSED_STAGES) * tt * hd + j2);
-                const int hs = hd >> 1;  // row stride in float pairs
-                const float *pp = s_sc + hl * lp + k * tt;
+                const float *vt = s_ring + (size_t)(k % FUSED_STAGES) * tt * hd + jc;  // row stride hd
+                const float *pp = s_sc + h0 * lp + k * tt;                               // head stride lp
                 const int nrows = L - k * tt < tt ? L - k * tt : tt;
                 if (nrows == tt) {
-                    // full tile: the loads of positions 4j+4..4j+7 are in
-                    // flight while positions 4j..4j+3 are added
-                    float4 pc = *reinterpret_cast<const float4 *>(pp);
-                    float2 vc[4];
+                    // full tile in chunks of PV_CH positions: the shared-memory
+                    // loads of chunk c+1 are in flight while chunk c is added
+                    constexpr int PV_CH = NH > 1 ? 8 : 16, NCH = TT_V / PV_CH;
+                    float4 pc[NH][PV_CH / 4], pn[NH][PV_CH / 4];
+                    PvVec<ND> vc[PV_CH], vn[PV_CH];
 #pragma unroll
-                    for (int u = 0; u < 4; u++) vc[u] = vt[u * hs];
+                    for (int h = 0; h < NH; h++)
 #pragma unroll
-                    for (int j = 0; j < tt / 4; j++) {
-                        float4 pn;
-                        float2 vn[4];
-                        if (j + 1 < tt / 4) {
-                            pn = *reinterpret_cast<const float4 *>(pp + 4 * j + 4);
+                        for (int u = 0; u < PV_CH / 4; u++)
+                            pc[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp)[u];
 #pragma unroll
-                            for (int u = 0; u < 4; u++) vn[u] = vt[(4 * j + 4 + u) * hs];
+                    for (int u = 0; u < PV_CH; u++) vc[u] = PvVec<ND>::load(vt + (size_t)u * hd);
+#pragma unroll
+                    for (int ch = 0; ch < NCH; ch++) {
+                        if (ch + 1 < NCH) {
+#pragma unroll
+                            for (int h = 0; h < NH; h++)
+#pragma unroll
+                                for (int u = 0; u < PV_CH / 4; u++)
+                                    pn[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp +
+                                                                                (ch + 1) * PV_CH)[u];
+#pragma unroll
+                            for (int u = 0; u < PV_CH; u++)
+                                vn[u] = PvVec<ND>::load(vt + (size_t)((ch + 1) * PV_CH + u) * hd);
                         }
-                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.x, vc[0].x));
-                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.x, vc[0].y));
-                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.y, vc[1].x));
-                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.y, vc[1].y));
-                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.z, vc[2].x));
-                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.z, vc[2].y));
-                        acc0 = __fadd_rn(acc0, __fmul_rn(pc.w, vc[3].x));
-                        acc1 = __fadd_rn(acc1, __fmul_rn(pc.w, vc[3].y));
-                        if (j + 1 < tt / 4) {
-                            pc = pn;
 #pragma unroll
-                            for (int u = 0; u < 4; u++) vc[u] = vn[u];
+                        for (int u = 0; u < PV_CH / 4; u++) {
+#pragma unroll
+                            for (int e = 0; e < 4; e++)
+#pragma unroll
+                                for (int h = 0; h < NH; h++) {
+                                    const float pr = e == 0 ? pc[h][u].x
+                                                   : e == 1 ? pc[h][u].y
+                                                   : e == 2 ? pc[h][u].z
+                                                            : pc[h][u].w;
+#pragma unroll
+                                    for (int c = 0; c < ND; c++)
+                                        acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vc[4 * u + e].v[c]));
+                                }
+                        }
+                        if (ch + 1 < NCH) {
+#pragma unroll
+                            for (int h = 0; h < NH; h++)
+#pragma unroll
+                                for (int u = 0; u < PV_CH / 4; u++) pc[h][u] = pn[h][u];
+#pragma unroll
+                            for (int u = 0; u < PV_CH; u++) vc[u] = vn[u];
                         }
                     }
                 } else {
                     for (int tl = 0; tl < nrows; tl++) {
-                        const float pr = pp[tl];
-                        const float2 vv = vt[tl * hs];
-                        acc0 = __fadd_rn(acc0, __fmul_rn(pr, vv.x));
-                        acc1 = __fadd_rn(acc1, __fmul_rn(pr, vv.y));
+                        const PvVec<ND> vv = PvVec<ND>::load(vt + (size_t)tl * hd);
+#pragma unroll
+                        for (int h = 0; h < NH; h++) {
+                            const float pr = pp[(size_t)h * lp + tl];
+#pragma unroll
+                            for (int c = 0; c < ND; c++) acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vv.v[c]));
+                        }
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_empty[k % FUSED_STAGES]);
         }
-        if (active) {
-            s_out[hl * hd + j2] = acc0;
-            s_out[hl * hd + j2 + 1] = acc1;
-        }
+        if (active)
+#pragma unroll
+            for (int h = 0; h < NH; h++)
+#pragma unroll
+                for (int c = 0; c < ND; c++) s_out[(h0 + h) * hd + jc + c] = acc[h][c];
     }
     __syncthreads();
     if (s_abort) {
@@ -1257,15 +1303,20 @@ template <int KVM>
 void launch_softmax_pv(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s) {
     const FusedShape f = fused_shape(KVM, a.head_dim, a.max_len);
     dim3 grid(a.num_kv_heads, a.rows);
-    // consumer warps (one thread per head and dim pair) plus the producer warp
-    int nth = (KVM * (a.head_dim / 2) + 31) / 32 * 32 + 32;
-    nth = nth < PV_THREADS ? PV_THREADS : nth;
-    launch_kernel(attn_softmax_pv_kernel<KVM>, grid, dim3(nth), f.smem, s, a.pdl, a, f.lp, vmap);
+    // consumer warps plus the producer warp, at least PV_THREADS
+    auto threads = [&](int cons) {
+        const int n = (cons + 31) / 32 * 32 + 32;
+        return n < PV_THREADS ? PV_THREADS : n;
+    };
+    // a thread per (head, dim pair): measured faster than a thread per dim
+    // running every head (fewer warps) or per (head, dim) (more warps)
+    launch_kernel(attn_softmax_pv_kernel<KVM, 1, 2>, grid, dim3(threads(KVM * a.head_dim / 2)), f.smem, s,
+                  a.pdl, a, f.lp, vmap);
 }
 
 template <int KVM>
 void set_softmax_pv_smem(int bytes) {
-    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          bytes);
 }
 
@@ -1337,7 +1388,8 @@ bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, u
 
 bool attention_fused_ok(const AttnArgs &a) {
     const int kv_mul = a.num_heads / a.num_kv_heads;
-    if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 992) return false;
+    // the softmax+PV CTA: kv_mul*head_dim/2 consumer threads plus a producer warp, <= 512
+    if (a.head_dim % 4 || kv_mul > 8 || kv_mul * a.head_dim > 960) return false;
     if (((uintptr_t)a.k_base | (uintptr_t)a.v_base) & 15) return false;
     if (!a.att) return false;  // the scores go through att
     if ((a.slot_stride | a.layer_off) & 3) return false;
