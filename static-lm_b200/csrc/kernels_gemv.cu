@@ -480,12 +480,28 @@ inline int units_of(int rows, int epi) {
     return epi == EPI_SWIGLU_Q8 ? total_tiles / 2 : total_tiles;
 }
 
+// Prefill-sized batches (GEMM): every warp keeps GEMM_BT activation rows, so
+// each unpacked weight block serves GEMM_BT rows and the CTA's weight tiles
+// serve 8*GEMM_BT rows; the RMSNorm runs as its own launch (a fused prologue
+// would repeat it in every weight unit's CTA).
+constexpr int GEMM_BT = 4;
+constexpr int GEMM_MIN_BATCH = 1024;
+
+inline bool gemm_shape(int rpt, int nb, int batch) {
+    return batch >= GEMM_MIN_BATCH &&
+           staged_smem(rpt, STAGED_MAX_WARPS * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
+}
+
 template <int EPI>
 void launch_epi(const GemvArgs &a, cudaStream_t s) {
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
+    if (!norm && gemm_shape(RPT, a.nb, a.batch)) {
+        launch_staged<GEMM_BT, EPI, false>(a, STAGED_MAX_WARPS, total_tiles, units, s);
+        return;
+    }
     const int nw = pick_nw(units, a.batch);
     if (staged_smem(RPT, nw, a.nb, norm) <= STAGED_SMEM_MAX) {
         // one activation row per warp
@@ -513,6 +529,7 @@ void set_limits(int bytes) {
     const int st = bytes < (int)STAGED_SMEM_MAX ? bytes : (int)STAGED_SMEM_MAX;
     cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
     cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
+    cudaFuncSetAttribute(gemv_staged_kernel<GEMM_BT, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
 }
 
 }  // namespace
@@ -526,6 +543,7 @@ void set_gemv_smem_limit(int bytes) {
 
 bool gemv_fuses_norm(int rows, int nb, int epi, int batch) {
     const int rpt = epi == EPI_SWIGLU_Q8 ? 2 : 1;
+    if (gemm_shape(rpt, nb, batch)) return false;  // the GEMM shape takes normalized Q8X rows
     const int units = units_of(rows, epi);
     return staged_smem(rpt, pick_nw(units, batch), nb, true) <= STAGED_SMEM_MAX;
 }
