@@ -272,7 +272,8 @@ __host__ __device__ inline size_t staged_smem(int rpt, int rows, int nb, bool no
 }
 
 template <int BT, int EPI, bool NORM>
-__global__ void __launch_bounds__(32 * STAGED_MAX_WARPS) gemv_staged_kernel(GemvArgs a, int total_tiles) {
+__global__ void __launch_bounds__(32 * STAGED_MAX_WARPS, BT > 1 ? 2 : 1)
+    gemv_staged_kernel(GemvArgs a, int total_tiles) {
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ __align__(8) uint64_t bar_rows, bar_w;
@@ -487,9 +488,15 @@ inline int units_of(int rows, int epi) {
 constexpr int GEMM_BT = 4;
 constexpr int GEMM_MIN_BATCH = 1024;
 
+// warps per GEMM CTA: 8, or 4 when 8 would keep two CTAs off an SM's shared memory
+inline int gemm_nw(int rpt, int nb) {
+    return staged_smem(rpt, STAGED_MAX_WARPS * GEMM_BT, nb, false) <= 100 * 1024 ? STAGED_MAX_WARPS
+                                                                               : STAGED_MAX_WARPS / 2;
+}
+
 inline bool gemm_shape(int rpt, int nb, int batch) {
     return batch >= GEMM_MIN_BATCH &&
-           staged_smem(rpt, STAGED_MAX_WARPS * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
+           staged_smem(rpt, gemm_nw(rpt, nb) * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
 }
 
 template <int EPI>
@@ -499,7 +506,7 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
     if (!norm && gemm_shape(RPT, a.nb, a.batch)) {
-        launch_staged<GEMM_BT, EPI, false>(a, STAGED_MAX_WARPS, total_tiles, units, s);
+        launch_staged<GEMM_BT, EPI, false>(a, gemm_nw(RPT, a.nb), total_tiles, units, s);
         return;
     }
     const int nw = pick_nw(units, a.batch);
