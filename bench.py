@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--layers", type=int, default=None,
                    help="profiling case only: fewer layers (same per-kernel shapes); the "
                         "line is then marked as not a bench value")
+    p.add_argument("--prefill-seqs", type=int, default=PREFILL_SEQS,
+                   help="profiling case only: prompts of the prefill leg (default 8)")
     return p.parse_args()
 
 
@@ -431,14 +433,15 @@ def run_ours(args):
         model = None
         pcfg, _, _ = __import__("static_lm.synth", fromlist=["config"]).config(
             "cfg3", max_seq_len=PREFILL_LEN + 128)
-        pm = S.Model(pcfg, w, max_sequences=PREFILL_SEQS, max_rows=PREFILL_SEQS * PREFILL_LEN,
+        nps = args.prefill_seqs
+        pm = S.Model(pcfg, w, max_sequences=nps, max_rows=nps * PREFILL_LEN,
                      device=local)
         if ws > 1:
             obj = [S.nccl_unique_id() if rank == 0 else None]
             torch.distributed.broadcast_object_list(obj, src=0)
             pm.attach_shard(obj[0], ws, rank)
         prompts = np.random.default_rng(args.seed).integers(
-            0, vocab, (PREFILL_SEQS, PREFILL_LEN)).astype(np.int32)
+            0, vocab, (nps, PREFILL_LEN)).astype(np.int32)
         pm.prefill_batch(prompts)  # warm-up
         barrier()
         pev0, pev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -448,8 +451,8 @@ def run_ours(args):
         pev1.record(pstream)
         pstream.synchronize()
         pms = max_ranks(pev0.elapsed_time(pev1))
-        prefill = {"value": PREFILL_SEQS * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
-                   "ms": pms, "workload": f"{PREFILL_SEQS} prompts x {PREFILL_LEN} tokens, "
+        prefill = {"value": nps * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
+                   "ms": pms, "workload": f"{nps} prompts x {PREFILL_LEN} tokens, "
                    "SmolLM2-135M shape, batched causal prefill to the first greedy token",
                    "sharding": (f"(sequence, KV head) units over {ws} ranks, one NCCL "
                                 "all-gather of attention outputs per layer before Wo")
@@ -462,7 +465,8 @@ def run_ours(args):
         "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload(ws),
         "roofline": {"bound": "hbm",
-                     "kernel": "attn_fused_kernel (scores+softmax+PV+Q8, one layer launch)"
+                     "kernel": "attention of one layer: attn_scores_pipe_kernel + "
+                               "attn_softmax_pv_kernel (+Q8 of the output) over all parts"
                      if per_step["attn_fused"] > 0 else "attention (scores+softmax+pv, one layer)",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_source": peak_note,
@@ -484,9 +488,10 @@ def run_ours(args):
     if cpu:
         line["cpu_baseline"] = cpu
         line["cpu_parity_tokens_equal"] = parity
-    if args.layers:
+    if args.layers or args.prefill_seqs != PREFILL_SEQS:
         line["config"]["layers"] = layers
-        line["note"] = "profiling case with fewer layers: not a bench value"
+        line["config"]["prefill_seqs"] = args.prefill_seqs
+        line["note"] = "profiling case (fewer layers or prompts): not a bench value"
     if rank == 0:
         print(json.dumps(line), flush=True)
     if model is not None:
