@@ -42,6 +42,12 @@ enum {
     SLM_ERR_DEVICE_INPUT = 7  /* a device-side input check failed (e.g. token id) */
 };
 
+/* Attention arithmetic of prefill (slm_model_set_prefill_mode,
+ * slm_causal_attention_rows): bit-exact CUDA-core chains, or tcgen05 tensor
+ * cores with a 3xTF32 split. */
+#define SLM_PREFILL_EXACT 0
+#define SLM_PREFILL_TENSOR_CORES 1
+
 /* Message of the calling thread's last failed call ("" if none). */
 const char *slm_last_error(void);
 /* Library version string. */
@@ -171,6 +177,17 @@ int slm_apply_rope_cached(float *vec_dev, uint64_t len, const float *cos_row_dev
 int slm_causal_attention(const float *q_dev, const float *k_cache_dev, const float *v_cache_dev,
                          float *att_dev, float *out_dev, const slm_config *cfg, uint32_t pos,
                          void *stream);
+/* The attention of n consecutive rows at positions start_pos..start_pos+n-1
+ * of one sequence: the per-token loop of forward_batch_with_kv
+ * (transformer.rs:563-593) over causal_multi_head_attention_jit.  q [n][dim],
+ * k/v caches [max_seq_len][kv_dim] holding positions < start_pos+n,
+ * att [n][num_heads][max_seq_len] scratch, out [n][dim].  mode is
+ * SLM_PREFILL_EXACT (bit-exact) or SLM_PREFILL_TENSOR_CORES (3xTF32 tensor
+ * cores, head_dim 32 or 64; other shapes run exact).  Synchronizes `stream`. */
+int slm_causal_attention_rows(const float *q_dev, const float *k_cache_dev,
+                              const float *v_cache_dev, float *att_dev, float *out_dev,
+                              const slm_config *cfg, uint32_t n, uint32_t start_pos, int mode,
+                              void *stream);
 /* sample_argmax (transformer.rs:654-667): first maximum wins. */
 int slm_sample_argmax(const float *logits_dev, uint64_t n, int32_t *out_dev, void *stream);
 
@@ -225,6 +242,14 @@ int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_t *tokens, 
  * the full results.  Requires nseq*num_kv_heads to divide by nranks. */
 int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
                             const int32_t *tokens, uint32_t n, int32_t *next);
+/* Attention arithmetic of prefill forwards (prefill_tokens, prefill_batch):
+ * SLM_PREFILL_EXACT (default) reproduces causal_multi_head_attention_jit
+ * (transformer.rs:273-321) bit for bit on the CUDA cores;
+ * SLM_PREFILL_TENSOR_CORES runs QK^T and PV on the tcgen05 tensor cores with
+ * a 3xTF32 split (about 1e-6 relative to the exact path, not bit-exact), for
+ * callers that accept the tolerance.  Decode is always exact.  No reference
+ * counterpart (the reference has one CPU path). */
+int slm_model_set_prefill_mode(slm_model *m, int mode);
 /* NCCL unique id (bytes = 128) for slm_model_attach_shard; made on one rank
  * and sent to the others by the host. */
 int slm_nccl_unique_id(void *id_out, uint64_t bytes);

@@ -157,11 +157,19 @@ struct AttnArgs {
     // [rows][num_heads][tmax_ld], tmax_ld >= ceil(max_len/32)
     float *tmax;
     int tmax_ld;
+    // prefill (fused path): 1 = attention on the tensor cores (tcgen05, 3xTF32;
+    // ~1e-6 relative to the exact path instead of bit-exact)
+    int prefill_tc;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)
 void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
                       cudaStream_t s);
+// Tensor-core causal prefill (kernels_attn_tc.cu): one launch per layer over
+// (128 query rows, query head) tiles, then the Q8_0 of the output when asked.
+bool attn_prefill_tc_ok(const AttnArgs &a);
+void launch_attn_prefill_tc(const AttnArgs &a, cudaStream_t s);
+void set_attn_prefill_tc_smem();
 // the three phases of launch_attention, for callers that time them apart
 void launch_attn_scores(const AttnArgs &a, cudaStream_t s);
 void launch_attn_softmax(const AttnArgs &a, cudaStream_t s);

@@ -29,6 +29,7 @@
 // p = start_pos + i, which reproduces the reference's per-token loop
 // (transformer.rs:563-593) exactly.
 #include "async.cuh"
+#include "attn_rows.cuh"
 #include "kernels.h"
 
 namespace slm {
@@ -38,23 +39,6 @@ namespace {
 constexpr int SCORE_T = 128;  // key positions per scores CTA
 constexpr int FUSED_STAGES = 4;
 constexpr size_t FUSED_SMEM_MAX = 200 * 1024;
-
-// keys attended by row r: pos+1, never beyond the cache nor the launch's
-// max_len (which sizes the grid and the softmax's shared memory)
-__device__ __forceinline__ int row_len(const AttnArgs &a, int r) {
-    int p = a.pos ? a.pos[r] : a.pos_const;
-    int L = p + 1;
-    L = L < a.max_seq ? L : a.max_seq;
-    return L < a.max_len ? L : a.max_len;
-}
-__device__ __forceinline__ size_t row_slot(const AttnArgs &a, int r) {
-    return a.slot ? (size_t)a.slot[r] : 0;
-}
-// whether this rank computes (row r, KV head g) of a sharded batched prefill
-__device__ __forceinline__ bool unit_owned(const AttnArgs &a, int r, int g) {
-    return a.shard_n <= 1 ||
-           ((r / a.rows_per_seq) * a.num_kv_heads + g) % a.shard_n == a.shard_r;
-}
 
 __global__ void __launch_bounds__(SCORE_T) attn_scores_kernel(AttnArgs a) {
     extern __shared__ float s_q[];  // [kv_mul][head_dim]
@@ -1400,6 +1384,10 @@ bool attention_fused_ok(const AttnArgs &a) {
 void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,
                        const CUtensorMap *amap, cudaStream_t s) {
     if (args.rows <= 0) return;
+    if (args.prefill_tc && attn_prefill_tc_ok(args)) {
+        launch_attn_prefill_tc(args, s);
+        return;
+    }
     AttnArgs a = args;
     const int kv_mul = a.num_heads / a.num_kv_heads;
     dim3 g1((a.max_len + TILE_KEYS - 1) / TILE_KEYS, a.num_kv_heads, a.rows);
@@ -1498,6 +1486,7 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
 }
 
 void set_attention_smem_limit(int bytes) {
+    set_attn_prefill_tc_smem();
     set_softmax_pv_smem<1>(bytes);
     set_softmax_pv_smem<2>(bytes);
     set_softmax_pv_smem<3>(bytes);

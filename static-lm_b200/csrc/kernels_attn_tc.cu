@@ -1,0 +1,305 @@
+// kernels_attn_tc.cu -- causal prefill attention on the 5th-generation tensor
+// cores (opt-in mode; the default prefill path is the bit-exact one of
+// kernels_attn.cu).
+//
+// Same result definition as causal_multi_head_attention_jit
+// (src/model/transformer.rs:273-321): score = (q.k) * scale, softmax with the
+// row maximum subtracted and the polynomial exp (graph.rs:168-179), out =
+// sum_t p_t v_t.  What differs is the summation order: QK^T and PV run as
+// tcgen05 kind::tf32 MMAs with a 3xTF32 split of both operands (hi = x cut to
+// tf32, lo = x - hi; a.b ~ ah.bh + ah.bl + al.bh, ~2^-21 relative error per
+// product), accumulated in f32 in TMEM, and out = (sum_t e_t v_t) * (1/sum)
+// instead of sum_t (e_t/sum) v_t.  Results agree with the exact path to about
+// 1e-6 relative, not bit for bit.
+//
+// One CTA of 128 threads per (128 query rows of one prompt, query head); the
+// tile loop runs twice over the keys of the tile's causal range in tiles of 64:
+//   pass 1: S = Q K^T (M=128 rows, N=64 keys, K=head_dim) -> row maxima;
+//   pass 2: S again -> e = exp(s - max) with the reference's four lane sums,
+//           E written to shared memory as the A operand, O += E V (N=head_dim)
+//           with V^T as the K-major B operand.
+// Thread i owns query row i = TMEM lane i (warp w reads lanes 32w..32w+31).
+// All operands are staged by the threads (global -> registers -> hi/lo split ->
+// 128-byte swizzled shared memory); MMAs are issued by thread 0 and complete on
+// one mbarrier (bounded waits: on a timeout the kernel sets the error flag,
+// frees its TMEM and writes nothing).
+#include "attn_rows.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace slm {
+
+namespace {
+
+constexpr int TC_M = 128;   // query rows per CTA (MMA M, TMEM lanes)
+constexpr int TC_N = 64;    // keys per tile
+constexpr int TC_COLS = 128;  // TMEM columns: S at 0..63, O at 64..64+hd-1
+
+template <int HD>
+constexpr size_t tc_smem_bytes() {
+    // Q hi/lo [128][HD], K hi/lo [64][HD], V^T hi/lo [HD][64], E hi/lo [128][64]
+    return 2 * sizeof(float) * ((size_t)TC_M * HD + (size_t)TC_N * HD + (size_t)HD * TC_N + (size_t)TC_M * TC_N) +
+           1024;
+}
+
+// Rows [row0, row0+R) of a K-major operand whose element (r, k) is src(r, k),
+// K = KW f32 (multiple of 32), written as hi and lo copies.  Each thread moves
+// one 16-byte chunk per step.
+template <int R, int KW, class Src>
+__device__ __forceinline__ void stage_operand(unsigned char *hi, unsigned char *lo, Src src, int tid) {
+    for (int e = tid; e < R * (KW / 4); e += TC_M) {
+        const int r = e / (KW / 4), k = (e % (KW / 4)) * 4;
+        const float4 x = src(r, k);
+        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        const unsigned o = sw128_off(r, k, R);
+        *reinterpret_cast<float4 *>(hi + o) = h;
+        *reinterpret_cast<float4 *>(lo + o) =
+            make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
+    }
+}
+
+// The three tf32 products of one operand pair over K = KW, M = 128 rows of A
+// (RA = 128) and RB rows of B, accumulating into d.
+template <int KW, int RB>
+__device__ __forceinline__ void mma_3xtf32(unsigned d, const unsigned char *ahi, const unsigned char *alo,
+                                           const unsigned char *bhi, const unsigned char *blo,
+                                           unsigned idesc, bool accumulate) {
+    const unsigned char *as[3] = {ahi, ahi, alo}, *bs[3] = {bhi, blo, bhi};
+#pragma unroll
+    for (int p = 0; p < 3; p++)
+#pragma unroll
+        for (int ks = 0; ks < KW / 8; ks++) {
+            const unsigned ao = (unsigned)((ks >> 2) * TC_M * 128 + (ks & 3) * 32);
+            const unsigned bo = (unsigned)((ks >> 2) * RB * 128 + (ks & 3) * 32);
+            tc_mma_tf32(d, umma_desc_sw128(smem_addr(as[p]) + ao), umma_desc_sw128(smem_addr(bs[p]) + bo),
+                        idesc, accumulate || p > 0 || ks > 0);
+        }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int run) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ unsigned s_taddr;
+    __shared__ int s_abort;
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    unsigned char *q_hi = base;
+    unsigned char *q_lo = q_hi + TC_M * HD * 4;
+    unsigned char *k_hi = q_lo + TC_M * HD * 4;
+    unsigned char *k_lo = k_hi + TC_N * HD * 4;
+    unsigned char *v_hi = k_lo + TC_N * HD * 4;
+    unsigned char *v_lo = v_hi + HD * TC_N * 4;
+    unsigned char *e_hi = v_lo + HD * TC_N * 4;
+    unsigned char *e_lo = e_hi + TC_M * TC_N * 4;
+
+    const int nqt = gridDim.x;
+    const int qt = nqt - 1 - (int)blockIdx.x;  // longest causal ranges first
+    const int h = blockIdx.y, seq = blockIdx.z;
+    const int kvm = a.num_heads / a.num_kv_heads, g = h / kvm;
+    const int r0 = seq * run + qt * TC_M;
+    const int nr = run - qt * TC_M < TC_M ? run - qt * TC_M : TC_M;
+    if (!unit_owned(a, r0, g)) return;  // CTA-uniform: another rank's unit
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    if (warp == 0) tc_alloc(&s_taddr, TC_COLS);
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    pdl_wait();  // q and the K/V rows of this prompt come from the QKV kernel
+
+    const int p0 = a.pos ? a.pos[r0] : a.pos_const;
+    int lmax = p0 + nr;  // keys of the tile's last row
+    lmax = lmax < a.max_seq ? lmax : a.max_seq;
+    lmax = lmax < a.max_len ? lmax : a.max_len;
+    const int ntile = (lmax + TC_N - 1) / TC_N;
+    const size_t kv_row0 = row_slot(a, r0) * a.slot_stride + a.layer_off + (size_t)g * HD;
+    const float *kb = a.k_base + kv_row0;
+    const float *vb = a.v_base + kv_row0;
+
+    // this thread's query row
+    const int i = tid;
+    int li = p0 + i + 1;
+    li = li < a.max_seq ? li : a.max_seq;
+    li = li < a.max_len ? li : a.max_len;
+    if (i >= nr) li = 0;
+
+    tc_fence_before();  // the TMEM address is read after the barrier below
+    stage_operand<TC_M, HD>(
+        q_hi, q_lo,
+        [&](int r, int k) {
+            return r < nr ? *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r) * a.ldq + (size_t)h * HD + k)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        },
+        tid);
+    __syncthreads();
+    tc_fence_after();
+    const unsigned taddr = s_taddr;
+    const unsigned t_s = taddr + ((unsigned)(warp * 32) << 16);  // this warp's lanes, S columns
+    const unsigned t_o = t_s + TC_N;                             // O columns
+    const unsigned idesc_s = umma_idesc_tf32(TC_M, TC_N), idesc_o = umma_idesc_tf32(TC_M, HD);
+    unsigned phase = 0;
+    bool failed = false;
+
+    auto stage_k = [&](int t0) {
+        stage_operand<TC_N, HD>(
+            k_hi, k_lo,
+            [&](int t, int k) {
+                return t0 + t < lmax ? *reinterpret_cast<const float4 *>(kb + (size_t)(t0 + t) * a.kv_dim + k)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            },
+            tid);
+    };
+    // MMAs issued by thread 0 after every thread's shared-memory writes, then
+    // waited for by all; false when a wait gave up (same answer in every thread)
+    auto run_mma = [&](auto issue) {
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            issue();
+            tc_commit(&bar);
+        }
+        const bool ok = mbar_wait(&bar, phase & 1u, &s_abort, a.err);
+        phase++;
+        tc_fence_after();
+        return __syncthreads_and(ok) != 0;
+    };
+    auto load_s = [&](int c, float (&v)[32]) { tc_ld32(t_s + (unsigned)(c * 32), v); };
+
+    // ---- pass 1: row maxima of the scaled scores
+    float mx = -INFINITY;
+    for (int kt = 0; kt < ntile && !failed; kt++) {
+        const int t0 = kt * TC_N;
+        stage_k(t0);
+        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
+            failed = true;
+            break;
+        }
+#pragma unroll
+        for (int c = 0; c < TC_N / 32; c++) {
+            float v[32];
+            load_s(c, v);
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (t0 + c * 32 + j < li) mx = cl_fmax(mx, __fmul_rn(v[j], a.scale));
+        }
+        tc_fence_before();
+        __syncthreads();  // S columns and the K tile are free again
+    }
+
+    // ---- pass 2: e = exp(s - max), four lane sums, O += E V
+    float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
+    const int vl = li & ~3;
+    for (int kt = 0; kt < ntile && !failed; kt++) {
+        const int t0 = kt * TC_N;
+        stage_k(t0);
+        // V^T: row d, column t = V[t0 + t][d]; a thread moves 4 keys of one dim
+        for (int e = tid; e < HD * (TC_N / 4); e += TC_M) {
+            const int d = e % HD, t = (e / HD) * 4;
+            float x[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                x[u] = t0 + t + u < lmax ? vb[(size_t)(t0 + t + u) * a.kv_dim + d] : 0.0f;
+            const float4 hh = make_float4(tf32_hi(x[0]), tf32_hi(x[1]), tf32_hi(x[2]), tf32_hi(x[3]));
+            const unsigned o = sw128_off(d, t, HD);
+            *reinterpret_cast<float4 *>(v_hi + o) = hh;
+            *reinterpret_cast<float4 *>(v_lo + o) = make_float4(__fsub_rn(x[0], hh.x), __fsub_rn(x[1], hh.y),
+                                                                __fsub_rn(x[2], hh.z), __fsub_rn(x[3], hh.w));
+        }
+        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
+            failed = true;
+            break;
+        }
+#pragma unroll
+        for (int c = 0; c < TC_N / 32; c++) {
+            float v[32];
+            load_s(c, v);
+#pragma unroll
+            for (int j4 = 0; j4 < 8; j4++) {
+                float ev[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int t = t0 + c * 32 + j4 * 4 + u;
+                    ev[u] = t < li ? exp_poly(__fsub_rn(__fmul_rn(v[j4 * 4 + u], a.scale), mx)) : 0.0f;
+                    if (t < vl)
+                        lane_sum[u] = __fadd_rn(lane_sum[u], ev[u]);
+                    else if (t < li)
+                        tail = __fadd_rn(tail, ev[u]);
+                }
+                const float4 hh = make_float4(tf32_hi(ev[0]), tf32_hi(ev[1]), tf32_hi(ev[2]), tf32_hi(ev[3]));
+                const unsigned o = sw128_off(i, c * 32 + j4 * 4, TC_M);
+                *reinterpret_cast<float4 *>(e_hi + o) = hh;
+                *reinterpret_cast<float4 *>(e_lo + o) = make_float4(
+                    __fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y), __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
+            }
+        }
+        if (!run_mma([&] { mma_3xtf32<TC_N, HD>(taddr + TC_N, e_hi, e_lo, v_hi, v_lo, idesc_o, kt > 0); })) {
+            failed = true;
+            break;
+        }
+    }
+
+    if (!failed) {
+        const float sum = __fadd_rn(__fadd_rn(__fadd_rn(lane_sum[0], lane_sum[1]), __fadd_rn(lane_sum[2], lane_sum[3])),
+                                    tail);
+        const float inv = __fdiv_rn(1.0f, sum);
+        const bool store = i < nr && li > 0;
+        float *orow = a.out + (size_t)(r0 + (store ? i : 0)) * a.ldo + (size_t)h * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 32; c++) {
+            float v[32];
+            tc_ld32(t_o + (unsigned)(c * 32), v);  // warp-wide: every lane, stores predicated
+            if (store)
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(orow + c * 32 + j) =
+                        make_float4(__fmul_rn(v[j], inv), __fmul_rn(v[j + 1], inv), __fmul_rn(v[j + 2], inv),
+                                    __fmul_rn(v[j + 3], inv));
+        }
+    }
+    pdl_release();
+    tc_fence_before();
+    __syncthreads();
+    if (failed && tid == 0) {
+        // a wait gave up: let the MMAs already committed finish (bounded)
+        // before the TMEM they write is freed
+        const long long tw = clock64();
+        while (!mbar_test(&bar, (phase - 1) & 1u) && clock64() - tw < WAIT_LIMIT) {
+        }
+    }
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tc_dealloc(taddr, TC_COLS);
+}
+
+}  // namespace
+
+bool attn_prefill_tc_ok(const AttnArgs &a) {
+    return a.prefill_run > 0 && a.rows % a.prefill_run == 0 && (a.head_dim == 32 || a.head_dim == 64) &&
+           (a.ldq & 3) == 0 && (a.kv_dim & 3) == 0 && (a.ldo & 3) == 0 && ((uintptr_t)a.q & 15) == 0 &&
+           ((uintptr_t)a.k_base & 15) == 0 && ((uintptr_t)a.out & 15) == 0 && (a.slot_stride & 3) == 0 &&
+           (a.layer_off & 3) == 0;
+}
+
+void launch_attn_prefill_tc(const AttnArgs &a, cudaStream_t s) {
+    const int run = a.prefill_run, nqt = (run + TC_M - 1) / TC_M;
+    const dim3 grid((unsigned)nqt, (unsigned)a.num_heads, (unsigned)(a.rows / run));
+    if (a.head_dim == 32)
+        launch_kernel(attn_prefill_tc_kernel<32>, grid, dim3(TC_M), tc_smem_bytes<32>(), s, a.pdl, a, run);
+    else
+        launch_kernel(attn_prefill_tc_kernel<64>, grid, dim3(TC_M), tc_smem_bytes<64>(), s, a.pdl, a, run);
+    if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
+}
+
+void set_attn_prefill_tc_smem() {
+    cudaFuncSetAttribute(attn_prefill_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc_smem_bytes<32>());
+    cudaFuncSetAttribute(attn_prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc_smem_bytes<64>());
+}
+
+}  // namespace slm

@@ -525,6 +525,54 @@ SLM_EXPORT int slm_causal_attention(const float *q, const float *k, const float 
     return launch_check("attention kernels");
 }
 
+SLM_EXPORT int slm_causal_attention_rows(const float *q, const float *k, const float *v, float *att,
+                                         float *out, const slm_config *cfg, uint32_t n, uint32_t start_pos,
+                                         int mode, void *stream) {
+    TRY(check_config(cfg));
+    if (!q || !k || !v || !att || !out) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    if (mode != SLM_PREFILL_EXACT && mode != SLM_PREFILL_TENSOR_CORES)
+        return fail(SLM_ERR_INVALID_ARG, "unknown prefill mode");
+    if ((uint64_t)start_pos + n > cfg->max_seq_len)
+        return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence position out of bounds");
+    if (n == 0) return SLM_OK;
+    ensure_kernel_attributes();
+    cudaStream_t st = (cudaStream_t)stream;
+    // row i sits at position start_pos + i (device array, as the model's rows)
+    std::vector<int32_t> hpos(n);
+    for (uint32_t i = 0; i < n; i++) hpos[i] = (int32_t)(start_pos + i);
+    int32_t *dpos = nullptr;
+    if (cudaMallocAsync((void **)&dpos, sizeof(int32_t) * n, st) != cudaSuccess)
+        return fail(SLM_ERR_CUDA, "position array");
+    cudaMemcpyAsync(dpos, hpos.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice, st);
+    AttnArgs a = attn_args_for(cfg);
+    a.q = q;
+    a.ldq = cfg->dim;
+    a.k_base = k;
+    a.v_base = v;
+    a.slot = nullptr;
+    a.pos = dpos;
+    a.att = att;
+    a.att_ld = cfg->max_seq_len;
+    a.out = out;
+    a.ldo = cfg->dim;
+    a.rows = (int)n;
+    a.max_len = (int)(start_pos + n);
+    a.prefill_run = (int)n;
+    a.prefill_tc = mode == SLM_PREFILL_TENSOR_CORES;
+    CUtensorMap vmap, kmap, amap;
+    const bool have_v = encode_v_map(&vmap, v, a.kv_dim, a.max_seq, 1, a.head_dim);
+    const bool have_k = encode_k_map(&kmap, k, a.kv_dim, a.max_seq, 1, a.head_dim);
+    const bool have_a = encode_att_map(&amap, att, a.max_seq, a.num_heads, n, a.num_heads / a.num_kv_heads);
+    if (have_v && attention_fused_ok(a))
+        launch_attn_fused(a, vmap, have_k ? &kmap : nullptr, have_a ? &amap : nullptr, st);
+    else
+        launch_attention(a, have_v ? &vmap : nullptr, have_k ? &kmap : nullptr, st);
+    cudaFreeAsync(dpos, st);
+    const int rc = launch_check("attention kernels");
+    cudaStreamSynchronize(st);  // hpos is read by the copy above
+    return rc;
+}
+
 SLM_EXPORT int slm_sample_argmax(const float *logits, uint64_t n, int32_t *out, void *stream) {
     if (n == 0) return fail(SLM_ERR_INVALID_ARG, "logits cannot be empty");
     if (!logits || !out) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
@@ -606,6 +654,7 @@ struct slm_model {
     bool fuse_norm = true;   // RMSNorm + Q8 inside the QKV and gate/up GEMVs
     bool use_pdl = true;     // programmatic dependent launch between decode kernels
     bool no_prefill_tiles = false;  // SLM_PREFILL_ROWWISE=1: prefill through the per-row kernels
+    int prefill_mode = SLM_PREFILL_EXACT;  // slm_model_set_prefill_mode
     int parts = 4;           // decode parts (streams) for batches of 16+ rows
     cudaStream_t side[MAX_PARTS - 1] = {};  // streams of parts 1..
     cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
@@ -757,6 +806,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     // prefill rows are runs of consecutive positions of one sequence
     aa.prefill_run = kind == STEP_PREFILL ? n : kind == STEP_PREFILL_BATCH ? seq_rows : 0;
     if (m->no_prefill_tiles) aa.prefill_run = 0;
+    aa.prefill_tc = aa.prefill_run > 0 && m->prefill_mode == SLM_PREFILL_TENSOR_CORES;
     if (kind == STEP_PREFILL_BATCH) {
         aa.rows_per_seq = seq_rows;
         aa.shard_n = sharded ? m->shard_n : 1;
@@ -1336,6 +1386,13 @@ SLM_EXPORT int slm_nccl_unique_id(void *id_out, uint64_t bytes) {
     const ncclResult_t r = api.get_id(&id);
     if (r != ncclSuccess) return fail(SLM_ERR_CUDA, std::string("ncclGetUniqueId: ") + api.error_string(r));
     std::memcpy(id_out, &id, sizeof(id));
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_set_prefill_mode(slm_model *m, int mode) {
+    if (!m) return SLM_ERR_INVALID_ARG;
+    if (mode != SLM_PREFILL_EXACT && mode != SLM_PREFILL_TENSOR_CORES) return SLM_ERR_INVALID_ARG;
+    m->prefill_mode = mode;
     return SLM_OK;
 }
 

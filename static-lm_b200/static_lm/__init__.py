@@ -219,6 +219,11 @@ class Model:
         buf = C.create_string_buffer(bytes(nccl_id), 128) if nranks > 1 else None
         lib().slm_model_attach_shard(self.h, buf, 128 if buf is not None else 0, nranks, rank)
 
+    def set_prefill_mode(self, tensor_cores: bool):
+        """Prefill attention on the tcgen05 tensor cores (3xTF32, ~1e-6
+        relative to the exact path) or bit-exact on the CUDA cores (default)."""
+        lib().slm_model_set_prefill_mode(self.h, 1 if tensor_cores else 0)
+
     def generate(self, prompt, n_out: int, eos: int = -1, seq: int = 0):
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.zeros(max(n_out, 1), dtype=np.int32)

@@ -91,6 +91,8 @@ SIGNATURES = {
     "slm_rope_tables": (C.c_int, [_U32, _U32, _V, _V], True),
     "slm_apply_rope_cached": (C.c_int, [_V, _U64, _V, _V, _U32, _V], True),
     "slm_causal_attention": (C.c_int, [_V, _V, _V, _V, _V, C.POINTER(Config), _U32, _V], True),
+    "slm_causal_attention_rows": (C.c_int, [_V, _V, _V, _V, _V, C.POINTER(Config), _U32, _U32, C.c_int, _V],
+                                  True),
     "slm_sample_argmax": (C.c_int, [_V, _U64, _V, _V], True),
     "slm_model_create": (C.c_int, [C.c_int, C.POINTER(Config), C.POINTER(ModelWeights), _U32, _U32,
                                    C.POINTER(_V)], True),
@@ -102,6 +104,7 @@ SIGNATURES = {
     "slm_model_prefill_batch": (C.c_int, [_V, _U32, _U32P, _I32P, _U32, _I32P], True),
     "slm_nccl_unique_id": (C.c_int, [_V, _U64], True),
     "slm_model_attach_shard": (C.c_int, [_V, _V, _U64, C.c_int, C.c_int], True),
+    "slm_model_set_prefill_mode": (C.c_int, [_V, C.c_int], True),
     "slm_shard_units": (_U32, [_U32, _U32, _U32, _U32, _U32P, _U32], False),
     "slm_model_generate": (C.c_int, [_V, _U32, _I32P, _U32, _I32P, _U32, C.c_int32, _U32P], True),
     "slm_model_embed_tokens": (C.c_int, [_V, _U32, _I32P, _U32, C.POINTER(C.c_float)], True),

@@ -1,0 +1,108 @@
+"""Tensor-core prefill (SLM_PREFILL_TENSOR_CORES): QK^T and PV on tcgen05 with
+a 3xTF32 split.  Not bit-exact by design.  Attention outputs are checked
+against the oracle with the north star's tolerance (1e-3 relative, 1e-4
+absolute); the exact mode of the same entry point stays bit-exact.  At model
+level every layer's attention output is quantized to Q8_0, so a 1e-6
+difference can move an int8 value by one step (~1/127 of its block's
+maximum): logits are compared with a bound of a few Q8 steps and the greedy
+tokens of these seeded cases are compared for equality.  Shapes the
+tensor-core kernel does not take (head_dim other than 32/64) fall back to the
+exact path."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+import static_lm as S
+from static_lm import synth
+from static_lm._lib import lib
+from static_lm.synth import Config
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got, want, rel=5e-2):
+    tol = rel * float(np.abs(want).max()) + 1e-4
+    err = float(np.abs(got - want).max())
+    assert err <= tol, (err, tol)
+    return err
+
+
+def _attention_rows(cuda, cfg, q, k, v, n, start, mode):
+    dim, heads, T = cfg.dim, cfg.num_heads, cfg.max_seq_len
+    qd, kd, vd = (cuda.from_numpy(np.ascontiguousarray(x)).cuda() for x in (q, k, v))
+    att = cuda.zeros(n * heads * T, dtype=cuda.float32, device="cuda")
+    out = cuda.zeros(n * dim, dtype=cuda.float32, device="cuda")
+    lib().slm_causal_attention_rows(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), att.data_ptr(),
+                                    out.data_ptr(), C.byref(cfg), n, start, mode, None)
+    cuda.cuda.synchronize()
+    return out.cpu().numpy().reshape(n, dim)
+
+
+# (dim, heads, kv_heads, max_seq, rows, start_pos): SmolLM2 GQA 3:1 with a
+# ragged last 128-row tile, a continued prefill, head_dim 32 with kv_mul 4
+ROW_CASES = [(576, 9, 3, 2112, 300, 0), (576, 9, 3, 2112, 150, 37), (256, 8, 2, 512, 200, 0)]
+
+
+@pytest.mark.parametrize("dim,heads,kvh,T,n,start", ROW_CASES)
+def test_attention_rows_exact_and_tensor_cores_against_oracle(cuda, dim, heads, kvh, T, n, start):
+    cfg_o = O.Config(dim, 4 * dim, heads, kvh, T, 1e-5)
+    cfg_s = Config(dim, 4 * dim, heads, kvh, T, 1e-5)
+    kvd = dim // heads * kvh
+    rng = np.random.default_rng(dim + n + start)
+    k = rng.standard_normal(T * kvd).astype(np.float32)
+    v = rng.standard_normal(T * kvd).astype(np.float32)
+    q = rng.standard_normal(n * dim).astype(np.float32)
+    ref = np.stack([O.attention(q[i * dim:(i + 1) * dim], k, v, cfg_o, start + i)[0] for i in range(n)])
+    exact = _attention_rows(cuda, cfg_s, q, k, v, n, start, 0)
+    assert np.array_equal(exact, ref), np.abs(exact - ref).max()
+    tc = _attention_rows(cuda, cfg_s, q, k, v, n, start, 1)
+    err = np.abs(tc - ref)
+    assert np.all(err <= 1e-3 * np.abs(ref) + 1e-4), float(err.max())
+    assert float(err.max()) < 1e-5  # 3xTF32: ~1e-6 in practice
+
+
+def _pair(cfg, layers, vocab, nseq, n, seed=31):
+    w = synth.synth_model(cfg, layers, vocab, seed=seed)
+    exact = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n)
+    tc = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n)
+    tc.set_prefill_mode(True)
+    return exact, tc
+
+
+@pytest.mark.parametrize("name,nseq,n", [("cfg3", 1, 300), ("cfg3", 3, 200), ("cfg1", 2, 130)])
+def test_tensor_core_prefill_within_tolerance(cuda, name, nseq, n):
+    cfg, _, vocab = synth.config(name)
+    exact, tc = _pair(cfg, 2, vocab, nseq, n)
+    prompts = np.random.default_rng(8).integers(0, vocab, (nseq, n)).astype(np.int32)
+    want = list(exact.prefill_batch(prompts))
+    got = list(tc.prefill_batch(prompts))
+    assert got == want
+    for s in range(nseq):
+        _close(tc.logits(s), exact.logits(s))
+    # decoding continues from the tensor-core prefill's KV cache (decode is exact)
+    nxt_e = exact.decode_batch(list(range(nseq)), want, [n] * nseq)
+    nxt_t = tc.decode_batch(list(range(nseq)), got, [n] * nseq)
+    assert list(nxt_t) == list(nxt_e)
+
+
+def test_tensor_core_prefill_head_dim_32_and_single_prompt(cuda):
+    """head_dim 32, kv_mul 4, a prompt that is not a multiple of the 128-row
+    tile, through prefill_tokens (one run of rows)."""
+    cfg = Config(256, 512, 8, 2, 512, 1e-5)
+    exact, tc = _pair(cfg, 2, 1024, 1, 200)
+    toks = np.random.default_rng(9).integers(0, 1024, 200).astype(np.int32)
+    assert tc.prefill_tokens(toks) == exact.prefill_tokens(toks)
+    _close(tc.logits(0), exact.logits(0))
+
+
+def test_tensor_core_mode_falls_back_to_exact_for_other_head_dims(cuda):
+    """cfg2 has head_dim 48: the tensor-core kernel does not take it, so the
+    mode changes nothing and results stay bit-exact."""
+    cfg, _, vocab = synth.config("cfg2")
+    exact, tc = _pair(cfg, 2, vocab, 2, 24)
+    prompts = np.random.default_rng(10).integers(0, vocab, (2, 24)).astype(np.int32)
+    assert list(tc.prefill_batch(prompts)) == list(exact.prefill_batch(prompts))
+    for s in range(2):
+        assert np.array_equal(tc.logits(s), exact.logits(s))
