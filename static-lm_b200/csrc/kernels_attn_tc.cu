@@ -43,21 +43,37 @@ constexpr size_t tc_smem_bytes() {
            1024;
 }
 
-// Rows [row0, row0+R) of a K-major operand whose element (r, k) is src(r, k),
-// K = KW f32 (multiple of 32), written as hi and lo copies.  Each thread moves
-// one 16-byte chunk per step.
-template <int R, int KW, class Src>
-__device__ __forceinline__ void stage_operand(unsigned char *hi, unsigned char *lo, Src src, int tid) {
-    for (int e = tid; e < R * (KW / 4); e += TC_M) {
-        const int r = e / (KW / 4), k = (e % (KW / 4)) * 4;
-        const float4 x = src(r, k);
-        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        const unsigned o = sw128_off(r, k, R);
-        *reinterpret_cast<float4 *>(hi + o) = h;
-        *reinterpret_cast<float4 *>(lo + o) =
-            make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
+// A K-major operand of R rows x KW f32 (KW a multiple of 32) moved by the 128
+// threads in 16-byte chunks: load() issues every global load of the thread
+// into registers first (one memory latency for the whole tile, and the loads
+// can be in flight while other work runs), store() writes the hi and lo
+// copies in the 128-byte swizzled layout.  src(r, k) returns the float4 at
+// row r, columns k..k+3.
+template <int R, int KW>
+struct OperandStage {
+    static constexpr int CH = R * (KW / 4) / TC_M;  // chunks per thread
+    static_assert(CH * TC_M == R * (KW / 4), "tile shape");
+    float4 x[CH];
+    template <class Src>
+    __device__ __forceinline__ void load(Src src, int tid) {
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int e = tid + c * TC_M;
+            x[c] = src(e / (KW / 4), (e % (KW / 4)) * 4);
+        }
     }
-}
+    __device__ __forceinline__ void store(unsigned char *hi, unsigned char *lo, int tid) const {
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const int e = tid + c * TC_M;
+            const float4 h = make_float4(tf32_hi(x[c].x), tf32_hi(x[c].y), tf32_hi(x[c].z), tf32_hi(x[c].w));
+            const unsigned o = sw128_off(e / (KW / 4), (e % (KW / 4)) * 4, R);
+            *reinterpret_cast<float4 *>(hi + o) = h;
+            *reinterpret_cast<float4 *>(lo + o) = make_float4(__fsub_rn(x[c].x, h.x), __fsub_rn(x[c].y, h.y),
+                                                              __fsub_rn(x[c].z, h.z), __fsub_rn(x[c].w, h.w));
+        }
+    }
+};
 
 // The three tf32 products of one operand pair over K = KW, M = 128 rows of A
 // (RA = 128) and RB rows of B, accumulating into d.
@@ -127,13 +143,16 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
     if (i >= nr) li = 0;
 
     tc_fence_before();  // the TMEM address is read after the barrier below
-    stage_operand<TC_M, HD>(
-        q_hi, q_lo,
-        [&](int r, int k) {
-            return r < nr ? *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r) * a.ldq + (size_t)h * HD + k)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        },
-        tid);
+    {
+        OperandStage<TC_M, HD> qs;
+        qs.load(
+            [&](int r, int k) {
+                return r < nr ? *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r) * a.ldq + (size_t)h * HD + k)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            },
+            tid);
+        qs.store(q_hi, q_lo, tid);
+    }
     __syncthreads();
     tc_fence_after();
     const unsigned taddr = s_taddr;
@@ -143,12 +162,26 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
     unsigned phase = 0;
     bool failed = false;
 
-    auto stage_k = [&](int t0) {
-        stage_operand<TC_N, HD>(
-            k_hi, k_lo,
+    // K tile kt: rows = keys, K = head_dim; V tile kt as V^T: rows = dims,
+    // K = keys (chunk = 4 keys of one dim, gathered from 4 V rows)
+    OperandStage<TC_N, HD> ks;
+    OperandStage<HD, TC_N> vs;
+    auto load_k = [&](int t0) {
+        ks.load(
             [&](int t, int k) {
                 return t0 + t < lmax ? *reinterpret_cast<const float4 *>(kb + (size_t)(t0 + t) * a.kv_dim + k)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            },
+            tid);
+    };
+    auto load_v = [&](int t0) {
+        vs.load(
+            [&](int d, int t) {
+                float x[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    x[u] = t0 + t + u < lmax ? vb[(size_t)(t0 + t + u) * a.kv_dim + d] : 0.0f;
+                return make_float4(x[0], x[1], x[2], x[3]);
             },
             tid);
     };
@@ -172,9 +205,12 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
 
     // ---- pass 1: row maxima of the scaled scores
     float mx = -INFINITY;
+    load_k(0);
     for (int kt = 0; kt < ntile && !failed; kt++) {
         const int t0 = kt * TC_N;
-        stage_k(t0);
+        ks.store(k_hi, k_lo, tid);
+        if (kt + 1 < ntile) load_k(t0 + TC_N);  // in flight during the MMAs
+        else load_k(0);                        // the first tile of pass 2
         if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
             failed = true;
             break;
@@ -194,21 +230,14 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
     // ---- pass 2: e = exp(s - max), four lane sums, O += E V
     float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
     const int vl = li & ~3;
+    load_v(0);
     for (int kt = 0; kt < ntile && !failed; kt++) {
         const int t0 = kt * TC_N;
-        stage_k(t0);
-        // V^T: row d, column t = V[t0 + t][d]; a thread moves 4 keys of one dim
-        for (int e = tid; e < HD * (TC_N / 4); e += TC_M) {
-            const int d = e % HD, t = (e / HD) * 4;
-            float x[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                x[u] = t0 + t + u < lmax ? vb[(size_t)(t0 + t + u) * a.kv_dim + d] : 0.0f;
-            const float4 hh = make_float4(tf32_hi(x[0]), tf32_hi(x[1]), tf32_hi(x[2]), tf32_hi(x[3]));
-            const unsigned o = sw128_off(d, t, HD);
-            *reinterpret_cast<float4 *>(v_hi + o) = hh;
-            *reinterpret_cast<float4 *>(v_lo + o) = make_float4(__fsub_rn(x[0], hh.x), __fsub_rn(x[1], hh.y),
-                                                                __fsub_rn(x[2], hh.z), __fsub_rn(x[3], hh.w));
+        ks.store(k_hi, k_lo, tid);
+        vs.store(v_hi, v_lo, tid);
+        if (kt + 1 < ntile) {  // in flight during this tile's MMAs and exps
+            load_k(t0 + TC_N);
+            load_v(t0 + TC_N);
         }
         if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
             failed = true;
