@@ -12,13 +12,14 @@
 // instead of sum_t (e_t/sum) v_t.  Results agree with the exact path to about
 // 1e-6 relative, not bit for bit.
 //
-// One CTA of 128 threads per (128 query rows of one prompt, query head); the
+// One CTA of 256 threads per (128 query rows of one prompt, query head); the
 // tile loop runs twice over the keys of the tile's causal range in tiles of 64:
 //   pass 1: S = Q K^T (M=128 rows, N=64 keys, K=head_dim) -> row maxima;
 //   pass 2: S again -> e = exp(s - max) with the reference's four lane sums,
 //           E written to shared memory as the A operand, O += E V (N=head_dim)
 //           with V^T as the K-major B operand.
-// Thread i owns query row i = TMEM lane i (warp w reads lanes 32w..32w+31).
+// Threads i and i+128 own query row i = TMEM lane i (warp w reads lanes
+// 32*(w%4)..+31), each half of every tile's key columns and output dims.
 // All operands are staged by the threads (global -> registers -> hi/lo split ->
 // 128-byte swizzled shared memory); MMAs are issued by thread 0 and complete on
 // one mbarrier (bounded waits: on a timeout the kernel sets the error flag,
@@ -33,6 +34,7 @@ namespace slm {
 namespace {
 
 constexpr int TC_M = 128;   // query rows per CTA (MMA M, TMEM lanes)
+constexpr int TC_THREADS = 256;  // two threads per query row
 constexpr int TC_N = 64;    // keys per tile
 constexpr int TC_COLS = 128;  // TMEM columns: S at 0..63, O at 64..64+hd-1
 
@@ -51,21 +53,21 @@ constexpr size_t tc_smem_bytes() {
 // row r, columns k..k+3.
 template <int R, int KW>
 struct OperandStage {
-    static constexpr int CH = R * (KW / 4) / TC_M;  // chunks per thread
-    static_assert(CH * TC_M == R * (KW / 4), "tile shape");
+    static constexpr int CH = R * (KW / 4) / TC_THREADS;  // chunks per thread
+    static_assert(CH * TC_THREADS == R * (KW / 4), "tile shape");
     float4 x[CH];
     template <class Src>
     __device__ __forceinline__ void load(Src src, int tid) {
 #pragma unroll
         for (int c = 0; c < CH; c++) {
-            const int e = tid + c * TC_M;
+            const int e = tid + c * TC_THREADS;
             x[c] = src(e / (KW / 4), (e % (KW / 4)) * 4);
         }
     }
     __device__ __forceinline__ void store(unsigned char *hi, unsigned char *lo, int tid) const {
 #pragma unroll
         for (int c = 0; c < CH; c++) {
-            const int e = tid + c * TC_M;
+            const int e = tid + c * TC_THREADS;
             const float4 h = make_float4(tf32_hi(x[c].x), tf32_hi(x[c].y), tf32_hi(x[c].z), tf32_hi(x[c].w));
             const unsigned o = sw128_off(e / (KW / 4), (e % (KW / 4)) * 4, R);
             *reinterpret_cast<float4 *>(hi + o) = h;
@@ -74,6 +76,20 @@ struct OperandStage {
         }
     }
 };
+
+// 16 consecutive f32 columns of this thread's TMEM lane, waited for.
+__device__ __forceinline__ void tc_ld16(unsigned taddr, float (&v)[16]) {
+    unsigned r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
+}
 
 // The three tf32 products of one operand pair over K = KW, M = 128 rows of A
 // (RA = 128) and RB rows of B, accumulating into d.
@@ -94,11 +110,12 @@ __device__ __forceinline__ void mma_3xtf32(unsigned d, const unsigned char *ahi,
 }
 
 template <int HD>
-__global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int run) {
+__global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a, int run) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t bar;
     __shared__ unsigned s_taddr;
     __shared__ int s_abort;
+    __shared__ float s_mx[TC_THREADS], s_part[5][TC_THREADS];  // halves' maxima, lane sums, tails
     unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char *q_hi = base;
     unsigned char *q_lo = q_hi + TC_M * HD * 4;
@@ -135,8 +152,9 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
     const float *kb = a.k_base + kv_row0;
     const float *vb = a.v_base + kv_row0;
 
-    // this thread's query row
-    const int i = tid;
+    // this thread's query row = TMEM lane (warp w reads lanes 32*(w%4)..), and
+    // its half of every key tile's columns
+    const int i = tid & (TC_M - 1), hf = tid / TC_M;
     int li = p0 + i + 1;
     li = li < a.max_seq ? li : a.max_seq;
     li = li < a.max_len ? li : a.max_len;
@@ -201,7 +219,7 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
         tc_fence_after();
         return __syncthreads_and(ok) != 0;
     };
-    auto load_s = [&](int c, float (&v)[32]) { tc_ld32(t_s + (unsigned)(c * 32), v); };
+    auto load_s = [&](float (&v)[32]) { tc_ld32(t_s + (unsigned)(hf * 32), v); };
 
     // ---- pass 1: row maxima of the scaled scores
     float mx = -INFINITY;
@@ -215,17 +233,21 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
             failed = true;
             break;
         }
-#pragma unroll
-        for (int c = 0; c < TC_N / 32; c++) {
+        {
             float v[32];
-            load_s(c, v);
+            load_s(v);
 #pragma unroll
             for (int j = 0; j < 32; j++)
-                if (t0 + c * 32 + j < li) mx = cl_fmax(mx, __fmul_rn(v[j], a.scale));
+                if (t0 + hf * 32 + j < li) mx = cl_fmax(mx, __fmul_rn(v[j], a.scale));
         }
         tc_fence_before();
         __syncthreads();  // S columns and the K tile are free again
     }
+
+    // the row maximum from the two halves
+    s_mx[tid] = mx;
+    __syncthreads();
+    mx = cl_fmax(s_mx[i], s_mx[i + TC_M]);
 
     // ---- pass 2: e = exp(s - max), four lane sums, O += E V
     float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
@@ -243,10 +265,10 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
             failed = true;
             break;
         }
-#pragma unroll
-        for (int c = 0; c < TC_N / 32; c++) {
+        {
+            const int c = hf;
             float v[32];
-            load_s(c, v);
+            load_s(v);
 #pragma unroll
             for (int j4 = 0; j4 < 8; j4++) {
                 float ev[4];
@@ -273,22 +295,30 @@ __global__ void __launch_bounds__(TC_M) attn_prefill_tc_kernel(AttnArgs a, int r
     }
 
     if (!failed) {
-        const float sum = __fadd_rn(__fadd_rn(__fadd_rn(lane_sum[0], lane_sum[1]), __fadd_rn(lane_sum[2], lane_sum[3])),
-                                    tail);
+        // the two halves' lane sums and tails (each half summed its columns in key order)
+#pragma unroll
+        for (int u = 0; u < 4; u++) s_part[u][tid] = lane_sum[u];
+        s_part[4][tid] = tail;
+        __syncthreads();
+        float l[5];
+#pragma unroll
+        for (int u = 0; u < 5; u++) l[u] = __fadd_rn(s_part[u][i], s_part[u][i + TC_M]);
+        const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[1]), __fadd_rn(l[2], l[3])), l[4]);
         const float inv = __fdiv_rn(1.0f, sum);
         const bool store = i < nr && li > 0;
-        float *orow = a.out + (size_t)(r0 + (store ? i : 0)) * a.ldo + (size_t)h * HD;
+        // half hf writes output columns [hf*HD/2, (hf+1)*HD/2)
+        constexpr int OC = HD / 2;
+        float *orow = a.out + (size_t)(r0 + (store ? i : 0)) * a.ldo + (size_t)h * HD + hf * OC;
+        float v[OC];
+        if constexpr (OC == 32)
+            tc_ld32(t_o + (unsigned)(hf * OC), v);  // warp-wide: every lane, stores predicated
+        else
+            tc_ld16(t_o + (unsigned)(hf * OC), v);
+        if (store)
 #pragma unroll
-        for (int c = 0; c < HD / 32; c++) {
-            float v[32];
-            tc_ld32(t_o + (unsigned)(c * 32), v);  // warp-wide: every lane, stores predicated
-            if (store)
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4 *>(orow + c * 32 + j) =
-                        make_float4(__fmul_rn(v[j], inv), __fmul_rn(v[j + 1], inv), __fmul_rn(v[j + 2], inv),
-                                    __fmul_rn(v[j + 3], inv));
-        }
+            for (int j = 0; j < OC; j += 4)
+                *reinterpret_cast<float4 *>(orow + j) = make_float4(__fmul_rn(v[j], inv), __fmul_rn(v[j + 1], inv),
+                                                                    __fmul_rn(v[j + 2], inv), __fmul_rn(v[j + 3], inv));
     }
     pdl_release();
     tc_fence_before();
@@ -318,9 +348,9 @@ void launch_attn_prefill_tc(const AttnArgs &a, cudaStream_t s) {
     const int run = a.prefill_run, nqt = (run + TC_M - 1) / TC_M;
     const dim3 grid((unsigned)nqt, (unsigned)a.num_heads, (unsigned)(a.rows / run));
     if (a.head_dim == 32)
-        launch_kernel(attn_prefill_tc_kernel<32>, grid, dim3(TC_M), tc_smem_bytes<32>(), s, a.pdl, a, run);
+        launch_kernel(attn_prefill_tc_kernel<32>, grid, dim3(TC_THREADS), tc_smem_bytes<32>(), s, a.pdl, a, run);
     else
-        launch_kernel(attn_prefill_tc_kernel<64>, grid, dim3(TC_M), tc_smem_bytes<64>(), s, a.pdl, a, run);
+        launch_kernel(attn_prefill_tc_kernel<64>, grid, dim3(TC_THREADS), tc_smem_bytes<64>(), s, a.pdl, a, run);
     if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
 }
 
