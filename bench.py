@@ -442,22 +442,39 @@ def run_ours(args):
             pm.attach_shard(obj[0], ws, rank)
         prompts = np.random.default_rng(args.seed).integers(
             0, vocab, (nps, PREFILL_LEN)).astype(np.int32)
-        pm.prefill_batch(prompts)  # warm-up
-        barrier()
-        pev0, pev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         pstream = torch.cuda.ExternalStream(pm.stream)
-        pev0.record(pstream)
-        first = pm.prefill_batch(prompts)
-        pev1.record(pstream)
-        pstream.synchronize()
-        pms = max_ranks(pev0.elapsed_time(pev1))
+
+        def timed_prefill():
+            pm.prefill_batch(prompts)  # warm-up
+            barrier()
+            pev0, pev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            pev0.record(pstream)
+            nxt = pm.prefill_batch(prompts)
+            pev1.record(pstream)
+            pstream.synchronize()
+            return nxt, max_ranks(pev0.elapsed_time(pev1))
+
+        first, pms = timed_prefill()
+        tc = None
+        if ws == 1:
+            # the opt-in tensor-core mode (3xTF32; not bit-exact) on the same prompts
+            exact_logits = pm.logits(0)
+            pm.set_prefill_mode(True)
+            first_tc, pms_tc = timed_prefill()
+            tc = {"value": nps * PREFILL_LEN / (pms_tc / 1000.0), "unit": "tok/s", "ms": pms_tc,
+                  "arithmetic": "QK^T and PV on tcgen05 (kind::tf32, 3xTF32 split), opt-in via "
+                                "slm_model_set_prefill_mode; not bit-exact",
+                  "first_tokens_equal": [int(t) for t in first_tc] == [int(t) for t in first],
+                  "max_abs_logit_diff_prompt0": float(np.abs(pm.logits(0) - exact_logits).max())}
         prefill = {"value": nps * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
                    "ms": pms, "workload": f"{nps} prompts x {PREFILL_LEN} tokens, "
                    "SmolLM2-135M shape, batched causal prefill to the first greedy token",
                    "sharding": (f"(sequence, KV head) units over {ws} ranks, one NCCL "
                                 "all-gather of attention outputs per layer before Wo")
                    if ws > 1 else "one GPU",
-                   "first_tokens": [int(t) for t in first[:4]]}
+                   "first_tokens": [int(t) for t in first[:4]],
+                   "arithmetic": "bit-exact f32 chains on the CUDA cores (default mode)",
+                   "tensor_cores": tc}
         pm.close()
 
     line = {

@@ -92,20 +92,21 @@ __device__ __forceinline__ void tc_ld16(unsigned taddr, float (&v)[16]) {
 }
 
 // The three tf32 products of one operand pair over K = KW, M = 128 rows of A
-// (RA = 128) and RB rows of B, accumulating into d.
+// and RB rows of B, accumulating into d.  The descriptors are the operands'
+// base descriptors: a K step moves the 14-bit start-address field (bits 0-13,
+// in 16-byte units, never carrying: shared addresses are below 256 KB) by
+// the step's byte offset / 16.
 template <int KW, int RB>
-__device__ __forceinline__ void mma_3xtf32(unsigned d, const unsigned char *ahi, const unsigned char *alo,
-                                           const unsigned char *bhi, const unsigned char *blo,
+__device__ __forceinline__ void mma_3xtf32(unsigned d, uint64_t ahi, uint64_t alo, uint64_t bhi, uint64_t blo,
                                            unsigned idesc, bool accumulate) {
-    const unsigned char *as[3] = {ahi, ahi, alo}, *bs[3] = {bhi, blo, bhi};
+    const uint64_t as[3] = {ahi, ahi, alo}, bs[3] = {bhi, blo, bhi};
 #pragma unroll
     for (int p = 0; p < 3; p++)
 #pragma unroll
         for (int ks = 0; ks < KW / 8; ks++) {
             const unsigned ao = (unsigned)((ks >> 2) * TC_M * 128 + (ks & 3) * 32);
             const unsigned bo = (unsigned)((ks >> 2) * RB * 128 + (ks & 3) * 32);
-            tc_mma_tf32(d, umma_desc_sw128(smem_addr(as[p]) + ao), umma_desc_sw128(smem_addr(bs[p]) + bo),
-                        idesc, accumulate || p > 0 || ks > 0);
+            tc_mma_tf32(d, as[p] + (ao >> 4), bs[p] + (bo >> 4), idesc, accumulate || p > 0 || ks > 0);
         }
 }
 
@@ -177,6 +178,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     const unsigned t_s = taddr + ((unsigned)(warp * 32) << 16);  // this warp's lanes, S columns
     const unsigned t_o = t_s + TC_N;                             // O columns
     const unsigned idesc_s = umma_idesc_tf32(TC_M, TC_N), idesc_o = umma_idesc_tf32(TC_M, HD);
+    const uint64_t dq_hi = umma_desc_sw128(smem_addr(q_hi)), dq_lo = umma_desc_sw128(smem_addr(q_lo));
+    const uint64_t dk_hi = umma_desc_sw128(smem_addr(k_hi)), dk_lo = umma_desc_sw128(smem_addr(k_lo));
+    const uint64_t dv_hi = umma_desc_sw128(smem_addr(v_hi)), dv_lo = umma_desc_sw128(smem_addr(v_lo));
+    const uint64_t de_hi = umma_desc_sw128(smem_addr(e_hi)), de_lo = umma_desc_sw128(smem_addr(e_lo));
     unsigned phase = 0;
     bool failed = false;
 
@@ -229,7 +234,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
         ks.store(k_hi, k_lo, tid);
         if (kt + 1 < ntile) load_k(t0 + TC_N);  // in flight during the MMAs
         else load_k(0);                        // the first tile of pass 2
-        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
+        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false); })) {
             failed = true;
             break;
         }
@@ -261,7 +266,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             load_k(t0 + TC_N);
             load_v(t0 + TC_N);
         }
-        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, q_hi, q_lo, k_hi, k_lo, idesc_s, false); })) {
+        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false); })) {
             failed = true;
             break;
         }
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
                     __fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y), __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
             }
         }
-        if (!run_mma([&] { mma_3xtf32<TC_N, HD>(taddr + TC_N, e_hi, e_lo, v_hi, v_lo, idesc_o, kt > 0); })) {
+        if (!run_mma([&] { mma_3xtf32<TC_N, HD>(taddr + TC_N, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); })) {
             failed = true;
             break;
         }
