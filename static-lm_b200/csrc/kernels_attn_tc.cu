@@ -239,11 +239,16 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             break;
         }
         {
+            // masked scaled scores, then a max tree (max is exact in any order)
             float v[32];
             load_s(v);
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-                if (t0 + hf * 32 + j < li) mx = cl_fmax(mx, __fmul_rn(v[j], a.scale));
+            for (int j = 0; j < 32; j++) v[j] = t0 + hf * 32 + j < li ? __fmul_rn(v[j], a.scale) : -INFINITY;
+#pragma unroll
+            for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+                for (int j = 0; j < w; j++) v[j] = cl_fmax(v[j], v[j + w]);
+            mx = cl_fmax(mx, v[0]);
         }
         tc_fence_before();
         __syncthreads();  // S columns and the K tile are free again
@@ -274,17 +279,22 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             const int c = hf;
             float v[32];
             load_s(v);
+            // the 32 exps are independent (masked afterwards): ILP for the
+            // polynomial's dependent steps; s - max is finite or +inf (row
+            // without keys, max = -inf), which exp_poly clamps
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = exp_poly(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
 #pragma unroll
             for (int j4 = 0; j4 < 8; j4++) {
                 float ev[4];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
                     const int t = t0 + c * 32 + j4 * 4 + u;
-                    ev[u] = t < li ? exp_poly(__fsub_rn(__fmul_rn(v[j4 * 4 + u], a.scale), mx)) : 0.0f;
+                    ev[u] = t < li ? v[j4 * 4 + u] : 0.0f;
                     if (t < vl)
                         lane_sum[u] = __fadd_rn(lane_sum[u], ev[u]);
-                    else if (t < li)
-                        tail = __fadd_rn(tail, ev[u]);
+                    else
+                        tail = __fadd_rn(tail, ev[u]);  // 0 past li
                 }
                 const float4 hh = make_float4(tf32_hi(ev[0]), tf32_hi(ev[1]), tf32_hi(ev[2]), tf32_hi(ev[3]));
                 const unsigned o = sw128_off(i, c * 32 + j4 * 4, TC_M);
