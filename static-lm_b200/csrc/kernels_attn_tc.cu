@@ -36,7 +36,7 @@ namespace {
 constexpr int TC_M = 128;   // query rows per CTA (MMA M, TMEM lanes)
 constexpr int TC_THREADS = 256;  // two threads per query row
 constexpr int TC_N = 64;    // keys per tile
-constexpr int TC_COLS = 128;  // TMEM columns: S at 0..63, O at 64..64+hd-1
+constexpr int TC_COLS = 256;  // TMEM columns: two S buffers at 0 and 64, O at 128..128+hd-1
 
 template <int HD>
 constexpr size_t tc_smem_bytes() {
@@ -175,8 +175,9 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     __syncthreads();
     tc_fence_after();
     const unsigned taddr = s_taddr;
-    const unsigned t_s = taddr + ((unsigned)(warp * 32) << 16);  // this warp's lanes, S columns
-    const unsigned t_o = t_s + TC_N;                             // O columns
+    const unsigned t_s = taddr + ((unsigned)(warp * 32) << 16);  // this warp's lanes, S buffers
+    const unsigned t_o_col = taddr + 2 * TC_N;                   // O columns (MMA destination)
+    const unsigned t_o = t_s + 2 * TC_N;                         // O columns, this warp's lanes
     const unsigned idesc_s = umma_idesc_tf32(TC_M, TC_N), idesc_o = umma_idesc_tf32(TC_M, HD);
     const uint64_t dq_hi = umma_desc_sw128(smem_addr(q_hi)), dq_lo = umma_desc_sw128(smem_addr(q_lo));
     const uint64_t dk_hi = umma_desc_sw128(smem_addr(k_hi)), dk_lo = umma_desc_sw128(smem_addr(k_lo));
@@ -208,40 +209,63 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             },
             tid);
     };
-    // MMAs issued by thread 0 after every thread's shared-memory writes, then
-    // waited for by all; false when a wait gave up (same answer in every thread)
-    auto run_mma = [&](auto issue) {
+    // Thread 0 issues MMAs after every thread's shared-memory writes (the
+    // barrier orders them, and the TMEM reads before it); `commit` makes the
+    // next wait cover everything issued so far.
+    auto issue = [&](auto body, bool commit) {
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            issue();
-            tc_commit(&bar);
+            body();
+            if (commit) tc_commit(&bar);
         }
+    };
+    // wait for the oldest outstanding commit; false when a wait gave up (same
+    // answer in every thread)
+    auto wait_mma = [&]() {
         const bool ok = mbar_wait(&bar, phase & 1u, &s_abort, a.err);
         phase++;
         tc_fence_after();
         return __syncthreads_and(ok) != 0;
     };
-    auto load_s = [&](float (&v)[32]) { tc_ld32(t_s + (unsigned)(hf * 32), v); };
-
-    // ---- pass 1: row maxima of the scaled scores
+    // S tiles u = 0 .. 2*ntile-1 in one stream: u < ntile is pass 1 (row
+    // maxima), u >= ntile pass 2 (exps, O += E V) over key tile u % ntile.
+    // S(u) sits in TMEM buffer u & 1; S(u+1) is issued before the thread work
+    // of tile u, so the tensor core computes it meanwhile.
+    auto issue_s = [&](int u) {
+        mma_3xtf32<HD, TC_N>(taddr + (unsigned)((u & 1) * TC_N), dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false);
+    };
+    const int nu = 2 * ntile;
     float mx = -INFINITY;
+    float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
+    const int vl = li & ~3;
     load_k(0);
-    for (int kt = 0; kt < ntile && !failed; kt++) {
-        const int t0 = kt * TC_N;
-        ks.store(k_hi, k_lo, tid);
-        if (kt + 1 < ntile) load_k(t0 + TC_N);  // in flight during the MMAs
-        else load_k(0);                        // the first tile of pass 2
-        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false); })) {
+    ks.store(k_hi, k_lo, tid);
+    load_k(ntile > 1 ? TC_N : 0);
+    issue([&] { issue_s(0); }, true);
+    for (int u = 0; u < nu && !failed; u++) {
+        const int kt = u % ntile, t0 = kt * TC_N;
+        const bool pass2 = u >= ntile;
+        if (!wait_mma()) {  // S(u) and every PV before it
             failed = true;
             break;
         }
-        {
+        float v[32];
+        tc_ld32(t_s + (unsigned)((u & 1) * TC_N + hf * 32), v);
+        if (u + 1 < nu) {
+            ks.store(k_hi, k_lo, tid);  // K((u+1) % ntile); the K stage is free: S(u) is done
+            load_k(((u + 2) % ntile) * TC_N);
+        }
+        if (u == ntile - 1) load_v(0);
+        if (pass2) {
+            vs.store(v_hi, v_lo, tid);  // V(kt); free: PV(kt-1) is done
+            if (kt + 1 < ntile) load_v(t0 + TC_N);
+        }
+        issue([&] { if (u + 1 < nu) issue_s(u + 1); }, !pass2);
+        if (!pass2) {
             // masked scaled scores, then a max tree (max is exact in any order)
-            float v[32];
-            load_s(v);
 #pragma unroll
             for (int j = 0; j < 32; j++) v[j] = t0 + hf * 32 + j < li ? __fmul_rn(v[j], a.scale) : -INFINITY;
 #pragma unroll
@@ -249,65 +273,40 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
 #pragma unroll
                 for (int j = 0; j < w; j++) v[j] = cl_fmax(v[j], v[j + w]);
             mx = cl_fmax(mx, v[0]);
-        }
-        tc_fence_before();
-        __syncthreads();  // S columns and the K tile are free again
-    }
-
-    // the row maximum from the two halves
-    s_mx[tid] = mx;
-    __syncthreads();
-    mx = cl_fmax(s_mx[i], s_mx[i + TC_M]);
-
-    // ---- pass 2: e = exp(s - max), four lane sums, O += E V
-    float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
-    const int vl = li & ~3;
-    load_v(0);
-    for (int kt = 0; kt < ntile && !failed; kt++) {
-        const int t0 = kt * TC_N;
-        ks.store(k_hi, k_lo, tid);
-        vs.store(v_hi, v_lo, tid);
-        if (kt + 1 < ntile) {  // in flight during this tile's MMAs and exps
-            load_k(t0 + TC_N);
-            load_v(t0 + TC_N);
-        }
-        if (!run_mma([&] { mma_3xtf32<HD, TC_N>(taddr, dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false); })) {
-            failed = true;
-            break;
-        }
-        {
-            const int c = hf;
-            float v[32];
-            load_s(v);
-            // the 32 exps are independent (masked afterwards): ILP for the
-            // polynomial's dependent steps; s - max is finite or +inf (row
-            // without keys, max = -inf), which exp_poly clamps
-#pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = exp_poly(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
-#pragma unroll
-            for (int j4 = 0; j4 < 8; j4++) {
-                float ev[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int t = t0 + c * 32 + j4 * 4 + u;
-                    ev[u] = t < li ? v[j4 * 4 + u] : 0.0f;
-                    if (t < vl)
-                        lane_sum[u] = __fadd_rn(lane_sum[u], ev[u]);
-                    else
-                        tail = __fadd_rn(tail, ev[u]);  // 0 past li
-                }
-                const float4 hh = make_float4(tf32_hi(ev[0]), tf32_hi(ev[1]), tf32_hi(ev[2]), tf32_hi(ev[3]));
-                const unsigned o = sw128_off(i, c * 32 + j4 * 4, TC_M);
-                *reinterpret_cast<float4 *>(e_hi + o) = hh;
-                *reinterpret_cast<float4 *>(e_lo + o) = make_float4(
-                    __fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y), __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
+            if (u == ntile - 1) {  // the row maximum from the two halves
+                s_mx[tid] = mx;
+                __syncthreads();
+                mx = cl_fmax(s_mx[i], s_mx[i + TC_M]);
             }
+            continue;
         }
-        if (!run_mma([&] { mma_3xtf32<TC_N, HD>(taddr + TC_N, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); })) {
-            failed = true;
-            break;
+        // the 32 exps are independent (masked afterwards): ILP for the
+        // polynomial's dependent steps; s - max is finite or +inf (row
+        // without keys, max = -inf), which exp_poly clamps
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = exp_poly(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
+#pragma unroll
+        for (int j4 = 0; j4 < 8; j4++) {
+            float ev[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int t = t0 + hf * 32 + j4 * 4 + q;
+                ev[q] = t < li ? v[j4 * 4 + q] : 0.0f;
+                if (t < vl)
+                    lane_sum[q] = __fadd_rn(lane_sum[q], ev[q]);
+                else
+                    tail = __fadd_rn(tail, ev[q]);  // 0 past li
+            }
+            const float4 hh = make_float4(tf32_hi(ev[0]), tf32_hi(ev[1]), tf32_hi(ev[2]), tf32_hi(ev[3]));
+            const unsigned o = sw128_off(i, hf * 32 + j4 * 4, TC_M);
+            *reinterpret_cast<float4 *>(e_hi + o) = hh;
+            *reinterpret_cast<float4 *>(e_lo + o) = make_float4(__fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y),
+                                                                __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
         }
+        // O += E V(kt); the commit also covers S(u+1) issued above
+        issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); }, true);
     }
+    if (!failed && !wait_mma()) failed = true;  // the last PV
 
     if (!failed) {
         // the two halves' lane sums and tails (each half summed its columns in key order)
