@@ -4,13 +4,14 @@
 //
 // Same result definition as causal_multi_head_attention_jit
 // (src/model/transformer.rs:273-321): score = (q.k) * scale, softmax with the
-// row maximum subtracted and the polynomial exp (graph.rs:168-179), out =
-// sum_t p_t v_t.  What differs is the summation order: QK^T and PV run as
-// tcgen05 kind::tf32 MMAs with a 3xTF32 split of both operands (hi = x cut to
-// tf32, lo = x - hi; a.b ~ ah.bh + ah.bl + al.bh, ~2^-21 relative error per
-// product), accumulated in f32 in TMEM, and out = (sum_t e_t v_t) * (1/sum)
-// instead of sum_t (e_t/sum) v_t.  Results agree with the exact path to about
-// 1e-6 relative, not bit for bit.
+// row maximum subtracted (graph.rs:168-179), out = sum_t p_t v_t.  What
+// differs is the arithmetic: QK^T and PV run as tcgen05 kind::tf32 MMAs with a
+// 3xTF32 split of both operands (hi = x cut to tf32, lo = x - hi; a.b ~ ah.bh
+// + ah.bl + al.bh, ~2^-21 relative error per product), accumulated in f32 in
+// TMEM; exp is the hardware exp2 (__expf, a few ulp) instead of the
+// reference's polynomial; out = (sum_t e_t v_t) * (1/sum) instead of
+// sum_t (e_t/sum) v_t.  Results agree with the exact path to about 1e-6
+// relative, not bit for bit.
 //
 // One CTA of 256 threads per (128 query rows of one prompt, query head); the
 // tile loop runs twice over the keys of the tile's causal range in tiles of 64:
@@ -108,6 +109,13 @@ __device__ __forceinline__ void mma_3xtf32(unsigned d, uint64_t ahi, uint64_t al
             const unsigned bo = (unsigned)((ks >> 2) * RB * 128 + (ks & 3) * 32);
             tc_mma_tf32(d, as[p] + (ao >> 4), bs[p] + (bo >> 4), idesc, accumulate || p > 0 || ks > 0);
         }
+}
+
+// max with NaN propagation (one instruction; the maximum itself is exact)
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
 }
 
 template <int HD>
@@ -271,20 +279,19 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
 #pragma unroll
             for (int w = 16; w >= 1; w >>= 1)
 #pragma unroll
-                for (int j = 0; j < w; j++) v[j] = cl_fmax(v[j], v[j + w]);
-            mx = cl_fmax(mx, v[0]);
+                for (int j = 0; j < w; j++) v[j] = max_nan(v[j], v[j + w]);
+            mx = max_nan(mx, v[0]);
             if (u == ntile - 1) {  // the row maximum from the two halves
                 s_mx[tid] = mx;
                 __syncthreads();
-                mx = cl_fmax(s_mx[i], s_mx[i + TC_M]);
+                mx = max_nan(s_mx[i], s_mx[i + TC_M]);
             }
             continue;
         }
-        // the 32 exps are independent (masked afterwards): ILP for the
-        // polynomial's dependent steps; s - max is finite or +inf (row
-        // without keys, max = -inf), which exp_poly clamps
+        // the 32 exps (masked afterwards); s - max is finite or +inf for a
+        // row without keys (max = -inf), whose values are masked
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = exp_poly(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
+        for (int j = 0; j < 32; j++) v[j] = __expf(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
 #pragma unroll
         for (int j4 = 0; j4 < 8; j4++) {
             float ev[4];
