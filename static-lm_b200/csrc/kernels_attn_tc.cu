@@ -220,23 +220,26 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     // Thread 0 issues MMAs after every thread's shared-memory writes (the
     // barrier orders them, and the TMEM reads before it); `commit` makes the
     // next wait cover everything issued so far.
+    // The same barrier tells every thread whether any thread's wait gave up
+    // (then nothing is issued and the caller stops).
+    bool waits_ok = true;
     auto issue = [&](auto body, bool commit) {
         fence_async_smem();
         tc_fence_before();
-        __syncthreads();
+        if (__syncthreads_or(!waits_ok)) return false;
         if (tid == 0) {
             tc_fence_after();
             body();
             if (commit) tc_commit(&bar);
         }
+        return true;
     };
-    // wait for the oldest outstanding commit; false when a wait gave up (same
-    // answer in every thread)
+    // wait for the oldest outstanding commit (a give-up is acted on at the
+    // next issue barrier)
     auto wait_mma = [&]() {
-        const bool ok = mbar_wait(&bar, phase & 1u, &s_abort, a.err);
+        waits_ok = mbar_wait(&bar, phase & 1u, &s_abort, a.err) && waits_ok;
         phase++;
         tc_fence_after();
-        return __syncthreads_and(ok) != 0;
     };
     // S tiles u = 0 .. 2*ntile-1 in one stream: u < ntile is pass 1 (row
     // maxima), u >= ntile pass 2 (exps, O += E V) over key tile u % ntile.
@@ -256,10 +259,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     for (int u = 0; u < nu && !failed; u++) {
         const int kt = u % ntile, t0 = kt * TC_N;
         const bool pass2 = u >= ntile;
-        if (!wait_mma()) {  // S(u) and every PV before it
-            failed = true;
-            break;
-        }
+        wait_mma();  // S(u) and every PV before it
         float v[32];
         tc_ld32(t_s + (unsigned)((u & 1) * TC_N + hf * 32), v);
         if (u + 1 < nu) {
@@ -271,7 +271,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             vs.store(v_hi, v_lo, tid);  // V(kt); free: PV(kt-1) is done
             if (kt + 1 < ntile) load_v(t0 + TC_N);
         }
-        issue([&] { if (u + 1 < nu) issue_s(u + 1); }, !pass2);
+        if (!issue([&] { if (u + 1 < nu) issue_s(u + 1); }, !pass2)) {
+            failed = true;
+            break;
+        }
         if (!pass2) {
             // masked scaled scores, then a max tree (max is exact in any order)
 #pragma unroll
@@ -311,9 +314,15 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
                                                                 __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
         }
         // O += E V(kt); the commit also covers S(u+1) issued above
-        issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); }, true);
+        if (!issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); }, true)) {
+            failed = true;
+            break;
+        }
     }
-    if (!failed && !wait_mma()) failed = true;  // the last PV
+    if (!failed) {  // the last PV
+        wait_mma();
+        failed = __syncthreads_or(!waits_ok) != 0;
+    }
 
     if (!failed) {
         // the two halves' lane sums and tails (each half summed its columns in key order)

@@ -44,7 +44,7 @@ def test_prefill_batch_matches_per_sequence_prefill(cuda, name, layers, nseq, n)
 SH = ("cfg3", 2, 4, 48)  # name, layers, sequences, tokens: 12 (sequence, KV head) units
 
 
-def _sharded_rank(rank, world, q_in, q_out):
+def _sharded_rank(rank, world, q_in, q_out, tensor_cores=False):
     import torch
     try:
         torch.cuda.set_device(rank)
@@ -52,6 +52,7 @@ def _sharded_rank(rank, world, q_in, q_out):
         cfg, _, vocab = synth.config(name)
         w = synth.synth_model(cfg, layers, vocab, seed=22)
         m = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n, device=rank)
+        m.set_prefill_mode(tensor_cores)
         if rank == 0:
             uid = S.nccl_unique_id()
             for _ in range(world - 1):
@@ -67,7 +68,10 @@ def _sharded_rank(rank, world, q_in, q_out):
         raise
 
 
-def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda):
+@pytest.mark.parametrize("tensor_cores", [False, True])
+def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda, tensor_cores):
+    """Either arithmetic mode: a (sequence, KV head) unit is computed by the
+    same kernel whichever rank owns it, so two GPUs match one bit for bit."""
     if cuda.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -75,7 +79,8 @@ def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda):
     world = 2
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_sharded_rank, args=(r, world, q_in, q_out)) for r in range(world)]
+    procs = [ctx.Process(target=_sharded_rank, args=(r, world, q_in, q_out, tensor_cores))
+             for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -91,6 +96,7 @@ def test_sharded_prefill_on_two_gpus_matches_one_gpu(cuda):
     cfg, _, vocab = synth.config(name)
     w = synth.synth_model(cfg, layers, vocab, seed=22)
     ref = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * n)
+    ref.set_prefill_mode(tensor_cores)
     want = list(ref.prefill_batch(_prompts(vocab, nseq, n, 4)))
     for rank, nxt, logits in res:
         assert nxt == want, rank
