@@ -9,16 +9,20 @@
 // 3xTF32 split of both operands (hi = x cut to tf32, lo = x - hi; a.b ~ ah.bh
 // + ah.bl + al.bh, ~2^-21 relative error per product), accumulated in f32 in
 // TMEM; exp is the hardware exp2 (__expf, a few ulp) instead of the
-// reference's polynomial; out = (sum_t e_t v_t) * (1/sum) instead of
-// sum_t (e_t/sum) v_t.  Results agree with the exact path to about 1e-6
-// relative, not bit for bit.
+// reference's polynomial; the subtracted maximum is a running one (online
+// softmax), and out = (sum_t e_t v_t) * (1/sum) instead of sum_t (e_t/sum)
+// v_t.  Results agree with the exact path to about 1e-6 relative, not bit
+// for bit.
 //
-// One CTA of 256 threads per (128 query rows of one prompt, query head); the
-// tile loop runs twice over the keys of the tile's causal range in tiles of 64:
-//   pass 1: S = Q K^T (M=128 rows, N=64 keys, K=head_dim) -> row maxima;
-//   pass 2: S again -> e = exp(s - max) with the reference's four lane sums,
-//           E written to shared memory as the A operand, O += E V (N=head_dim)
-//           with V^T as the K-major B operand.
+// One CTA of 256 threads per (128 query rows of one prompt, query head); one
+// pass over the keys of the tile's causal range in tiles of 64:
+//   S = Q K^T (M=128 rows, N=64 keys, K=head_dim, TMEM, double-buffered so
+//   that S of the next tile is computed during this tile's thread work) ->
+//   running row maximum m (moved only when a tile exceeds it by more than 8;
+//   then O and the lane sums are scaled by exp(m_old - m_new)) -> e =
+//   exp(s - m) with the reference's four lane sums -> E written to shared
+//   memory as the A operand -> O += E V (N=head_dim) with V^T as the K-major
+//   B operand.
 // Threads i and i+128 own query row i = TMEM lane i (warp w reads lanes
 // 32*(w%4)..+31), each half of every tile's key columns and output dims.
 // All operands are staged by the threads (global -> registers -> hi/lo split ->
@@ -109,6 +113,42 @@ __device__ __forceinline__ void mma_3xtf32(unsigned d, uint64_t ahi, uint64_t al
             const unsigned bo = (unsigned)((ks >> 2) * RB * 128 + (ks & 3) * 32);
             tc_mma_tf32(d, as[p] + (ao >> 4), bs[p] + (bo >> 4), idesc, accumulate || p > 0 || ks > 0);
         }
+}
+
+// Multiply this thread's half of its TMEM row of O (columns hf*HD/2 ..) by
+// alpha: load, scale, store back, wait for the store.  Warp-wide.
+template <int HD>
+__device__ __forceinline__ void tmem_scale_half(unsigned t_o, int hf, float alpha) {
+    constexpr int OC = HD / 2;
+    const unsigned ta = t_o + (unsigned)(hf * OC);
+    if constexpr (OC == 32) {
+        float v[32];
+        tc_ld32(ta, v);
+        unsigned r[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fmul_rn(v[j], alpha));
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+            "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(ta),
+            "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+            "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+            "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+            "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+            : "memory");
+    } else {
+        float v[16];
+        tc_ld16(ta, v);
+        unsigned r[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) r[j] = __float_as_uint(__fmul_rn(v[j], alpha));
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16};\n" ::"r"(ta),
+            "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+            "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+            : "memory");
+    }
+    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 
 // max with NaN propagation (one instruction; the maximum itself is exact)
@@ -241,60 +281,69 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
         phase++;
         tc_fence_after();
     };
-    // S tiles u = 0 .. 2*ntile-1 in one stream: u < ntile is pass 1 (row
-    // maxima), u >= ntile pass 2 (exps, O += E V) over key tile u % ntile.
-    // S(u) sits in TMEM buffer u & 1; S(u+1) is issued before the thread work
-    // of tile u, so the tensor core computes it meanwhile.
-    auto issue_s = [&](int u) {
-        mma_3xtf32<HD, TC_N>(taddr + (unsigned)((u & 1) * TC_N), dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false);
+    // S(kt) sits in TMEM buffer kt & 1; S(kt+1) is issued before the thread
+    // work of tile kt, so the tensor core computes it meanwhile.
+    auto issue_s = [&](int kt) {
+        mma_3xtf32<HD, TC_N>(taddr + (unsigned)((kt & 1) * TC_N), dq_hi, dq_lo, dk_hi, dk_lo, idesc_s, false);
     };
-    const int nu = 2 * ntile;
-    float mx = -INFINITY;
+    // Online softmax: m is the row's running reference maximum; it moves only
+    // when a tile's maximum exceeds it by more than RESCALE_AT (the exps then
+    // stay below e^RESCALE_AT), and then O (TMEM) and the lane sums are scaled
+    // by exp(m_old - m_new).  The halves of a row agree on m through s_mx.
+    constexpr float RESCALE_AT = 8.0f;
+    float m = -INFINITY;
     float lane_sum[4] = {0.f, 0.f, 0.f, 0.f}, tail = 0.f;
     const int vl = li & ~3;
     load_k(0);
     ks.store(k_hi, k_lo, tid);
-    load_k(ntile > 1 ? TC_N : 0);
+    if (ntile > 1) load_k(TC_N);
+    load_v(0);
     issue([&] { issue_s(0); }, true);
-    for (int u = 0; u < nu && !failed; u++) {
-        const int kt = u % ntile, t0 = kt * TC_N;
-        const bool pass2 = u >= ntile;
-        wait_mma();  // S(u) and every PV before it
+    for (int kt = 0; kt < ntile && !failed; kt++) {
+        const int t0 = kt * TC_N;
+        wait_mma();  // S(kt) and PV(kt-1)
         float v[32];
-        tc_ld32(t_s + (unsigned)((u & 1) * TC_N + hf * 32), v);
-        if (u + 1 < nu) {
-            ks.store(k_hi, k_lo, tid);  // K((u+1) % ntile); the K stage is free: S(u) is done
-            load_k(((u + 2) % ntile) * TC_N);
+        tc_ld32(t_s + (unsigned)((kt & 1) * TC_N + hf * 32), v);
+        // masked scaled scores and their maximum (a tree: max is exact in any order)
+        float tm[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            v[j] = __fmul_rn(v[j], a.scale);
+            tm[j] = t0 + hf * 32 + j < li ? v[j] : -INFINITY;
         }
-        if (u == ntile - 1) load_v(0);
-        if (pass2) {
-            vs.store(v_hi, v_lo, tid);  // V(kt); free: PV(kt-1) is done
-            if (kt + 1 < ntile) load_v(t0 + TC_N);
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; j++) tm[j] = max_nan(tm[j], tm[j + w]);
+        s_mx[tid] = tm[0];
+        if (kt + 1 < ntile) {
+            ks.store(k_hi, k_lo, tid);  // K(kt+1); the K stage is free: S(kt) is done
+            if (kt + 2 < ntile) load_k(t0 + 2 * TC_N);
         }
-        if (!issue([&] { if (u + 1 < nu) issue_s(u + 1); }, !pass2)) {
+        vs.store(v_hi, v_lo, tid);  // V(kt); free: PV(kt-1) is done
+        if (kt + 1 < ntile) load_v(t0 + TC_N);
+        if (!issue([&] { if (kt + 1 < ntile) issue_s(kt + 1); }, false)) {
             failed = true;
             break;
         }
-        if (!pass2) {
-            // masked scaled scores, then a max tree (max is exact in any order)
+        // the row's tile maximum from both halves (written before the barrier)
+        const float rm = max_nan(s_mx[i], s_mx[i + TC_M]);
+        const bool move = rm > m + RESCALE_AT || (m == -INFINITY && rm > -INFINITY);
+        const float m_new = move ? rm : m;
+        const float alpha = move ? __expf(__fsub_rn(m, m_new)) : 1.0f;  // 0 when m was -inf
+        if (move) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = t0 + hf * 32 + j < li ? __fmul_rn(v[j], a.scale) : -INFINITY;
-#pragma unroll
-            for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-                for (int j = 0; j < w; j++) v[j] = max_nan(v[j], v[j + w]);
-            mx = max_nan(mx, v[0]);
-            if (u == ntile - 1) {  // the row maximum from the two halves
-                s_mx[tid] = mx;
-                __syncthreads();
-                mx = max_nan(s_mx[i], s_mx[i + TC_M]);
-            }
-            continue;
+            for (int q = 0; q < 4; q++) lane_sum[q] = __fmul_rn(lane_sum[q], alpha);
+            tail = __fmul_rn(tail, alpha);
         }
-        // the 32 exps (masked afterwards); s - max is finite or +inf for a
-        // row without keys (max = -inf), whose values are masked
+        m = m_new;
+        // O *= alpha for this thread's half of the row, once O holds PV(0..kt-1);
+        // warp-wide TMEM access when any lane of the warp moved
+        if (kt > 0 && __any_sync(0xffffffffu, move)) tmem_scale_half<HD>(t_o, hf, alpha);
+        // the 32 exps (masked afterwards; rows without keys have m = -inf and
+        // s - m = +inf there, masked too)
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = __expf(__fsub_rn(__fmul_rn(v[j], a.scale), mx));
+        for (int j = 0; j < 32; j++) v[j] = __expf(__fsub_rn(v[j], m));
 #pragma unroll
         for (int j4 = 0; j4 < 8; j4++) {
             float ev[4];
@@ -313,7 +362,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             *reinterpret_cast<float4 *>(e_lo + o) = make_float4(__fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y),
                                                                 __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
         }
-        // O += E V(kt); the commit also covers S(u+1) issued above
+        // O += E V(kt); the commit also covers S(kt+1) issued above
         if (!issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); }, true)) {
             failed = true;
             break;
