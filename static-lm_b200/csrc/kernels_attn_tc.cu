@@ -14,7 +14,9 @@
 // v_t.  Results agree with the exact path to about 1e-6 relative, not bit
 // for bit.
 //
-// One CTA of 256 threads per (128 query rows of one prompt, query head); one
+// One CTA of 256 threads per (128/kv_mul query rows of one prompt, KV head):
+// MMA row m is query row m/kv_mul of head m%kv_mul of the group, so the group's
+// heads share every staged K and V tile; one
 // pass over the keys of the tile's causal range in tiles of 64:
 //   S = Q K^T (M=128 rows, N=64 keys, K=head_dim, TMEM, double-buffered so
 //   that S of the next tile is computed during this tile's thread work) ->
@@ -23,7 +25,7 @@
 //   exp(s - m) with the reference's four lane sums -> E written to shared
 //   memory as the A operand -> O += E V (N=head_dim) with V^T as the K-major
 //   B operand.
-// Threads i and i+128 own query row i = TMEM lane i (warp w reads lanes
+// Threads i and i+128 own MMA row i = TMEM lane i (warp w reads lanes
 // 32*(w%4)..+31), each half of every tile's key columns and output dims.
 // All operands are staged by the threads (global -> registers -> hi/lo split ->
 // 128-byte swizzled shared memory); MMAs are issued by thread 0 and complete on
@@ -175,12 +177,14 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     unsigned char *e_hi = v_lo + HD * TC_N * 4;
     unsigned char *e_lo = e_hi + TC_M * TC_N * 4;
 
+    // MMA row m = (query row m / kvm, head g*kvm + m % kvm): the kvm heads of
+    // KV group g share every K and V tile, staged once
     const int nqt = gridDim.x;
     const int qt = nqt - 1 - (int)blockIdx.x;  // longest causal ranges first
-    const int h = blockIdx.y, seq = blockIdx.z;
-    const int kvm = a.num_heads / a.num_kv_heads, g = h / kvm;
-    const int r0 = seq * run + qt * TC_M;
-    const int nr = run - qt * TC_M < TC_M ? run - qt * TC_M : TC_M;
+    const int g = blockIdx.y, seq = blockIdx.z;
+    const int kvm = a.num_heads / a.num_kv_heads, qr = TC_M / kvm;  // query rows per CTA
+    const int r0 = seq * run + qt * qr;
+    const int nr = run - qt * qr < qr ? run - qt * qr : qr;
     if (!unit_owned(a, r0, g)) return;  // CTA-uniform: another rank's unit
     const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -204,18 +208,20 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     // this thread's query row = TMEM lane (warp w reads lanes 32*(w%4)..), and
     // its half of every key tile's columns
     const int i = tid & (TC_M - 1), hf = tid / TC_M;
-    int li = p0 + i + 1;
+    const int qi = i / kvm, h = g * kvm + i % kvm;  // query row in the tile, head
+    int li = p0 + qi + 1;
     li = li < a.max_seq ? li : a.max_seq;
     li = li < a.max_len ? li : a.max_len;
-    if (i >= nr) li = 0;
+    if (qi >= nr) li = 0;  // also the rows past qr*kvm
 
     tc_fence_before();  // the TMEM address is read after the barrier below
     {
         OperandStage<TC_M, HD> qs;
         qs.load(
             [&](int r, int k) {
-                return r < nr ? *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r) * a.ldq + (size_t)h * HD + k)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                return r / kvm < nr ? *reinterpret_cast<const float4 *>(a.q + (size_t)(r0 + r / kvm) * a.ldq +
+                                                                        (size_t)(g * kvm + r % kvm) * HD + k)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
             },
             tid);
         qs.store(q_hi, q_lo, tid);
@@ -384,10 +390,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
         for (int u = 0; u < 5; u++) l[u] = __fadd_rn(s_part[u][i], s_part[u][i + TC_M]);
         const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[1]), __fadd_rn(l[2], l[3])), l[4]);
         const float inv = __fdiv_rn(1.0f, sum);
-        const bool store = i < nr && li > 0;
+        const bool store = qi < nr && li > 0;
         // half hf writes output columns [hf*HD/2, (hf+1)*HD/2)
         constexpr int OC = HD / 2;
-        float *orow = a.out + (size_t)(r0 + (store ? i : 0)) * a.ldo + (size_t)h * HD + hf * OC;
+        float *orow = a.out + (size_t)(r0 + (store ? qi : 0)) * a.ldo + (size_t)h * HD + hf * OC;
         float v[OC];
         if constexpr (OC == 32)
             tc_ld32(t_o + (unsigned)(hf * OC), v);  // warp-wide: every lane, stores predicated
@@ -418,14 +424,16 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
 
 bool attn_prefill_tc_ok(const AttnArgs &a) {
     return a.prefill_run > 0 && a.rows % a.prefill_run == 0 && (a.head_dim == 32 || a.head_dim == 64) &&
+           a.num_heads / a.num_kv_heads <= 16 &&
            (a.ldq & 3) == 0 && (a.kv_dim & 3) == 0 && (a.ldo & 3) == 0 && ((uintptr_t)a.q & 15) == 0 &&
            ((uintptr_t)a.k_base & 15) == 0 && ((uintptr_t)a.out & 15) == 0 && (a.slot_stride & 3) == 0 &&
            (a.layer_off & 3) == 0;
 }
 
 void launch_attn_prefill_tc(const AttnArgs &a, cudaStream_t s) {
-    const int run = a.prefill_run, nqt = (run + TC_M - 1) / TC_M;
-    const dim3 grid((unsigned)nqt, (unsigned)a.num_heads, (unsigned)(a.rows / run));
+    const int kvm = a.num_heads / a.num_kv_heads, qr = TC_M / kvm;
+    const int run = a.prefill_run, nqt = (run + qr - 1) / qr;
+    const dim3 grid((unsigned)nqt, (unsigned)a.num_kv_heads, (unsigned)(a.rows / run));
     if (a.head_dim == 32)
         launch_kernel(attn_prefill_tc_kernel<32>, grid, dim3(TC_THREADS), tc_smem_bytes<32>(), s, a.pdl, a, run);
     else
