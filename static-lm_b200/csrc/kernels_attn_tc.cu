@@ -24,7 +24,8 @@
 //   then O and the lane sums are scaled by exp(m_old - m_new)) -> e =
 //   exp(s - m) with the reference's four lane sums -> E written to shared
 //   memory as the A operand -> O += E V (N=head_dim) with V^T as the K-major
-//   B operand.
+//   B operand (two V buffers; S and PV complete on separate mbarriers, so PV
+//   of one tile runs while the threads read and stage the next).
 // Threads i and i+128 own MMA row i = TMEM lane i (warp w reads lanes
 // 32*(w%4)..+31), each half of every tile's key columns and output dims.
 // All operands are staged by the threads (global -> registers -> hi/lo split ->
@@ -47,8 +48,9 @@ constexpr int TC_COLS = 256;  // TMEM columns: two S buffers at 0 and 64, O at 1
 
 template <int HD>
 constexpr size_t tc_smem_bytes() {
-    // Q hi/lo [128][HD], K hi/lo [64][HD], V^T hi/lo [HD][64], E hi/lo [128][64]
-    return 2 * sizeof(float) * ((size_t)TC_M * HD + (size_t)TC_N * HD + (size_t)HD * TC_N + (size_t)TC_M * TC_N) +
+    // Q hi/lo [128][HD], K hi/lo [64][HD], two V^T hi/lo [HD][64], E hi/lo [128][64]
+    return 2 * sizeof(float) *
+               ((size_t)TC_M * HD + (size_t)TC_N * HD + 2 * (size_t)HD * TC_N + (size_t)TC_M * TC_N) +
            1024;
 }
 
@@ -163,18 +165,18 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 template <int HD>
 __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a, int run) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bar_s, bar_p;  // completions of S and of PV MMAs
     __shared__ unsigned s_taddr;
     __shared__ int s_abort;
-    __shared__ float s_mx[TC_THREADS], s_part[5][TC_THREADS];  // halves' maxima, lane sums, tails
+    __shared__ float s_mx[TC_THREADS];  // the halves' tile maxima
     unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     unsigned char *q_hi = base;
     unsigned char *q_lo = q_hi + TC_M * HD * 4;
     unsigned char *k_hi = q_lo + TC_M * HD * 4;
     unsigned char *k_lo = k_hi + TC_N * HD * 4;
-    unsigned char *v_hi = k_lo + TC_N * HD * 4;
-    unsigned char *v_lo = v_hi + HD * TC_N * 4;
-    unsigned char *e_hi = v_lo + HD * TC_N * 4;
+    unsigned char *v_hi = k_lo + TC_N * HD * 4;         // two buffers: V(kt) at (kt & 1)
+    unsigned char *v_lo = v_hi + 2 * HD * TC_N * 4;
+    unsigned char *e_hi = v_lo + 2 * HD * TC_N * 4;
     unsigned char *e_lo = e_hi + TC_M * TC_N * 4;
 
     // MMA row m = (query row m / kvm, head g*kvm + m % kvm): the kvm heads of
@@ -190,7 +192,8 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
 
     if (warp == 0) tc_alloc(&s_taddr, TC_COLS);
     if (tid == 0) {
-        mbar_init(&bar, 1);
+        mbar_init(&bar_s, 1);
+        mbar_init(&bar_p, 1);
         s_abort = 0;
         mbar_fence_init();
     }
@@ -236,8 +239,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     const uint64_t dq_hi = umma_desc_sw128(smem_addr(q_hi)), dq_lo = umma_desc_sw128(smem_addr(q_lo));
     const uint64_t dk_hi = umma_desc_sw128(smem_addr(k_hi)), dk_lo = umma_desc_sw128(smem_addr(k_lo));
     const uint64_t dv_hi = umma_desc_sw128(smem_addr(v_hi)), dv_lo = umma_desc_sw128(smem_addr(v_lo));
+    const uint64_t dv_step = (uint64_t)((HD * TC_N * 4) >> 4);  // descriptor offset of V buffer 1
     const uint64_t de_hi = umma_desc_sw128(smem_addr(e_hi)), de_lo = umma_desc_sw128(smem_addr(e_lo));
-    unsigned phase = 0;
+    unsigned n_s = 0, n_p = 0;            // commits issued on bar_s / bar_p
+    unsigned w_s = 0, w_p = 0;            // commits waited for
     bool failed = false;
 
     // K tile kt: rows = keys, K = head_dim; V tile kt as V^T: rows = dims,
@@ -264,27 +269,28 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             tid);
     };
     // Thread 0 issues MMAs after every thread's shared-memory writes (the
-    // barrier orders them, and the TMEM reads before it); `commit` makes the
-    // next wait cover everything issued so far.
-    // The same barrier tells every thread whether any thread's wait gave up
-    // (then nothing is issued and the caller stops).
+    // barrier orders them, and the TMEM reads before it), then commits them
+    // to `done` (bar_s for S, bar_p for PV: a commit covers everything the
+    // thread issued before it).  The same barrier tells every thread whether
+    // any thread's wait gave up (then nothing is issued and the caller stops).
     bool waits_ok = true;
-    auto issue = [&](auto body, bool commit) {
+    auto issue = [&](auto body, uint64_t *done, unsigned &n_done) {
         fence_async_smem();
         tc_fence_before();
         if (__syncthreads_or(!waits_ok)) return false;
         if (tid == 0) {
             tc_fence_after();
             body();
-            if (commit) tc_commit(&bar);
+            tc_commit(done);
         }
+        n_done++;
         return true;
     };
-    // wait for the oldest outstanding commit (a give-up is acted on at the
-    // next issue barrier)
-    auto wait_mma = [&]() {
-        waits_ok = mbar_wait(&bar, phase & 1u, &s_abort, a.err) && waits_ok;
-        phase++;
+    // wait for the next commit of `done` (a give-up is acted on at the next
+    // issue barrier)
+    auto wait_on = [&](uint64_t *done, unsigned &w) {
+        waits_ok = mbar_wait(done, w & 1u, &s_abort, a.err) && waits_ok;
+        w++;
         tc_fence_after();
     };
     // S(kt) sits in TMEM buffer kt & 1; S(kt+1) is issued before the thread
@@ -304,10 +310,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     ks.store(k_hi, k_lo, tid);
     if (ntile > 1) load_k(TC_N);
     load_v(0);
-    issue([&] { issue_s(0); }, true);
+    issue([&] { issue_s(0); }, &bar_s, n_s);
     for (int kt = 0; kt < ntile && !failed; kt++) {
-        const int t0 = kt * TC_N;
-        wait_mma();  // S(kt) and PV(kt-1)
+        const int t0 = kt * TC_N, vbuf = kt & 1;
+        wait_on(&bar_s, w_s);  // S(kt); PV(kt-1) may still run
         float v[32];
         tc_ld32(t_s + (unsigned)((kt & 1) * TC_N + hf * 32), v);
         // masked scaled scores and their maximum (a tree: max is exact in any order)
@@ -326,12 +332,15 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             ks.store(k_hi, k_lo, tid);  // K(kt+1); the K stage is free: S(kt) is done
             if (kt + 2 < ntile) load_k(t0 + 2 * TC_N);
         }
-        vs.store(v_hi, v_lo, tid);  // V(kt); free: PV(kt-1) is done
+        // V(kt) into buffer kt & 1, last read by PV(kt-2), which completed
+        // before E(kt-1) was written
+        vs.store(v_hi + vbuf * HD * TC_N * 4, v_lo + vbuf * HD * TC_N * 4, tid);
         if (kt + 1 < ntile) load_v(t0 + TC_N);
-        if (!issue([&] { if (kt + 1 < ntile) issue_s(kt + 1); }, false)) {
+        if (kt + 1 < ntile && !issue([&] { issue_s(kt + 1); }, &bar_s, n_s)) {
             failed = true;
             break;
         }
+        if (kt + 1 == ntile) __syncthreads();  // s_mx complete (no S issue barrier)
         // the row's tile maximum from both halves (written before the barrier)
         const float rm = max_nan(s_mx[i], s_mx[i + TC_M]);
         const bool move = rm > m + RESCALE_AT || (m == -INFINITY && rm > -INFINITY);
@@ -343,13 +352,14 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             tail = __fmul_rn(tail, alpha);
         }
         m = m_new;
-        // O *= alpha for this thread's half of the row, once O holds PV(0..kt-1);
-        // warp-wide TMEM access when any lane of the warp moved
-        if (kt > 0 && __any_sync(0xffffffffu, move)) tmem_scale_half<HD>(t_o, hf, alpha);
         // the 32 exps (masked afterwards; rows without keys have m = -inf and
         // s - m = +inf there, masked too)
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] = __expf(__fsub_rn(v[j], m));
+        if (kt > 0) wait_on(&bar_p, w_p);  // PV(kt-1): E and O are free
+        // O *= alpha for this thread's half of the row, once O holds PV(0..kt-1);
+        // warp-wide TMEM access when any lane of the warp moved
+        if (kt > 0 && __any_sync(0xffffffffu, move)) tmem_scale_half<HD>(t_o, hf, alpha);
 #pragma unroll
         for (int j4 = 0; j4 < 8; j4++) {
             float ev[4];
@@ -368,17 +378,21 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
             *reinterpret_cast<float4 *>(e_lo + o) = make_float4(__fsub_rn(ev[0], hh.x), __fsub_rn(ev[1], hh.y),
                                                                 __fsub_rn(ev[2], hh.z), __fsub_rn(ev[3], hh.w));
         }
-        // O += E V(kt); the commit also covers S(kt+1) issued above
-        if (!issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi, dv_lo, idesc_o, kt > 0); }, true)) {
+        // O += E V(kt), running while the next tile's S is read and staged
+        if (!issue([&] { mma_3xtf32<TC_N, HD>(t_o_col, de_hi, de_lo, dv_hi + vbuf * dv_step, dv_lo + vbuf * dv_step,
+                                              idesc_o, kt > 0); },
+                   &bar_p, n_p)) {
             failed = true;
             break;
         }
     }
     if (!failed) {  // the last PV
-        wait_mma();
+        wait_on(&bar_p, w_p);
         failed = __syncthreads_or(!waits_ok) != 0;
     }
 
+    // [5][TC_THREADS] lane sums and tails in the E buffer (free after the last PV)
+    float(*s_part)[TC_THREADS] = reinterpret_cast<float(*)[TC_THREADS]>(e_hi);
     if (!failed) {
         // the two halves' lane sums and tails (each half summed its columns in key order)
 #pragma unroll
@@ -412,8 +426,10 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
         // a wait gave up: let the MMAs already committed finish (bounded)
         // before the TMEM they write is freed
         const long long tw = clock64();
-        while (!mbar_test(&bar, (phase - 1) & 1u) && clock64() - tw < WAIT_LIMIT) {
-        }
+        while (w_s < n_s && clock64() - tw < WAIT_LIMIT)
+            if (mbar_test(&bar_s, w_s & 1u)) w_s++;
+        while (w_p < n_p && clock64() - tw < WAIT_LIMIT)
+            if (mbar_test(&bar_p, w_p & 1u)) w_p++;
     }
     __syncthreads();
     tc_fence_after();
