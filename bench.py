@@ -464,7 +464,10 @@ def run_ours(args):
             tc = {"value": nps * PREFILL_LEN / (pms_tc / 1000.0), "unit": "tok/s", "ms": pms_tc,
                   "arithmetic": "QK^T and PV on tcgen05 (kind::tf32, 3xTF32 split), opt-in via "
                                 "slm_model_set_prefill_mode; not bit-exact",
-                  "first_tokens_equal": [int(t) for t in first_tc] == [int(t) for t in first],
+                  # Q8_0 quantization after every attention can turn the mode's ~1e-6
+                  # differences into one-step int8 changes, so near-ties may flip
+                  "first_tokens_equal_to_exact": sum(int(x) == int(y) for x, y in zip(first_tc, first)),
+                  "of_prompts": len(first),
                   "max_abs_logit_diff_prompt0": float(np.abs(pm.logits(0) - exact_logits).max())}
         prefill = {"value": nps * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
                    "ms": pms, "workload": f"{nps} prompts x {PREFILL_LEN} tokens, "
