@@ -16,8 +16,8 @@
 //
 // One CTA of 256 threads per (128/kv_mul query rows of one prompt, KV head):
 // MMA row m is query row m/kv_mul of head m%kv_mul of the group, so the group's
-// heads share every staged K and V tile; one
-// pass over the keys of the tile's causal range in tiles of 64:
+// heads share every staged K and V tile.  One pass over the keys of the
+// tile's causal range in tiles of 64:
 //   S = Q K^T (M=128 rows, N=64 keys, K=head_dim, TMEM, double-buffered so
 //   that S of the next tile is computed during this tile's thread work) ->
 //   running row maximum m (moved only when a tile exceeds it by more than 8;
@@ -30,8 +30,8 @@
 // 32*(w%4)..+31), each half of every tile's key columns and output dims.
 // All operands are staged by the threads (global -> registers -> hi/lo split ->
 // 128-byte swizzled shared memory); MMAs are issued by thread 0 and complete on
-// one mbarrier (bounded waits: on a timeout the kernel sets the error flag,
-// frees its TMEM and writes nothing).
+// two mbarriers (bounded waits: on a timeout the kernel sets the error flag,
+// lets the committed MMAs finish, frees its TMEM and writes nothing).
 #include "attn_rows.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -41,8 +41,8 @@ namespace slm {
 
 namespace {
 
-constexpr int TC_M = 128;   // query rows per CTA (MMA M, TMEM lanes)
-constexpr int TC_THREADS = 256;  // two threads per query row
+constexpr int TC_M = 128;   // MMA rows per CTA (M, TMEM lanes): (query row, head) pairs
+constexpr int TC_THREADS = 256;  // two threads per MMA row
 constexpr int TC_N = 64;    // keys per tile
 constexpr int TC_COLS = 256;  // TMEM columns: two S buffers at 0 and 64, O at 128..128+hd-1
 
@@ -54,7 +54,7 @@ constexpr size_t tc_smem_bytes() {
            1024;
 }
 
-// A K-major operand of R rows x KW f32 (KW a multiple of 32) moved by the 128
+// A K-major operand of R rows x KW f32 (KW a multiple of 32) moved by the 256
 // threads in 16-byte chunks: load() issues every global load of the thread
 // into registers first (one memory latency for the whole tile, and the loads
 // can be in flight while other work runs), store() writes the hi and lo
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     const float *kb = a.k_base + kv_row0;
     const float *vb = a.v_base + kv_row0;
 
-    // this thread's query row = TMEM lane (warp w reads lanes 32*(w%4)..), and
+    // this thread's MMA row = TMEM lane (warp w reads lanes 32*(w%4)..), and
     // its half of every key tile's columns
     const int i = tid & (TC_M - 1), hf = tid / TC_M;
     const int qi = i / kvm, h = g * kvm + i % kvm;  // query row in the tile, head
