@@ -39,7 +39,8 @@ enum {
     SLM_ERR_SHAPE = 4,        /* sizes that do not match (cols % 32, lengths) */
     SLM_ERR_CAPACITY = 5,     /* arena or scratch too small */
     SLM_ERR_CUDA = 6,         /* a CUDA runtime call failed */
-    SLM_ERR_DEVICE_INPUT = 7  /* a device-side input check failed (e.g. token id) */
+    SLM_ERR_DEVICE_INPUT = 7, /* a device-side input check failed (e.g. token id) */
+    SLM_ERR_TIMEOUT = 8       /* a communicator set-up or collective did not complete in time */
 };
 
 /* Attention arithmetic of prefill (slm_model_set_prefill_mode,
@@ -136,7 +137,10 @@ uint64_t slm_gemm_q4_0_scratch_bytes(uint64_t batch, uint64_t cols);
  * the library's device image, so batch*cols/32 blocks of 68 bytes must fit:
  * batch*cols <= 1,973,760; larger sizes return SLM_ERR_CAPACITY.  The first
  * call on a device looks the buffer's address up (cudaGetSymbolAddress), so
- * make that first call before any stream capture.  All calls share the one
+ * make that first call before any stream capture.  The address is cached per
+ * process and device ordinal for the life of the process: after a
+ * cudaDeviceReset (which destroys the context that holds the buffer) this
+ * entry point must not be called again in that process.  All calls share the one
  * buffer: calls that overlap on the GPU (different streams, or different
  * host threads without ordering) race on it and must be serialized by the
  * caller.  inputs_dev is [batch][cols] f32, output_dev [batch][rows] f32,
@@ -144,6 +148,15 @@ uint64_t slm_gemm_q4_0_scratch_bytes(uint64_t batch, uint64_t cols);
 #define SLM_NOALLOC_SCRATCH_BYTES (4u << 20)
 int slm_gemm_q4_0_f32_noalloc(const slm_qmatrix *w, const float *inputs_dev, float *output_dev,
                               uint64_t batch, uint64_t rows, uint64_t cols, void *stream);
+/* No reference counterpart (the reference has no device waits).  Runs, on
+ * `device`, one CTA whose threads wait on an mbarrier that nothing arrives
+ * on, through the same bounded wait every TMA pipeline of this library uses,
+ * with limit_cycles (1 .. 2e9 SM clock cycles; the kernels use 2e9, about
+ * 1 s) as its bound.  The wait gives up, the kernel sets the device error
+ * flag and returns, and this call reports it the way the model entry points
+ * do: SLM_ERR_DEVICE_INPUT "a device wait timed out".  The context stays
+ * usable.  Any other return means the bounded-wait path is broken. */
+int slm_selftest_bounded_wait(int device, uint64_t limit_cycles);
 /* quantize_row_q8_0 (src/quant/blocks.rs:102-123) into BlockQ8_0 (34 B). */
 int slm_quantize_row_q8_0(const float *src_dev, void *dst_blocks_dev, uint64_t n, void *stream);
 
@@ -255,8 +268,20 @@ int slm_model_set_prefill_mode(slm_model *m, int mode);
 int slm_nccl_unique_id(void *id_out, uint64_t bytes);
 /* Join a group of nranks models (one per GPU, collective: every rank calls it
  * with the same id) for KV-head-sharded batched prefill.  NCCL is loaded at
- * run time (libnccl.so.2).  nranks = 1 detaches nothing and needs no id. */
+ * run time (libnccl.so.2).  nranks = 1 detaches nothing and needs no id.
+ * The communicator is set up non-blocking: if the group is not complete
+ * within the model's communicator timeout (a rank never joins), the call
+ * aborts it and returns SLM_ERR_TIMEOUT; it may then be called again.  No
+ * reference counterpart (the reference is single-process; it aborts on any
+ * fault, Cargo.toml:21). */
 int slm_model_attach_shard(slm_model *m, const void *id, uint64_t bytes, int nranks, int rank);
+/* Bound, in milliseconds (default 120000), on the communicator set-up of
+ * slm_model_attach_shard and on every sharded batched prefill's wait for its
+ * collectives.  A prefill whose collectives do not complete in time (a rank
+ * stopped taking part) aborts the communicator, which ends its waiting NCCL
+ * kernels, and returns SLM_ERR_TIMEOUT; later sharded prefills return
+ * SLM_ERR_INVALID_ARG until the group is attached again. */
+int slm_model_set_comm_timeout(slm_model *m, uint32_t timeout_ms);
 /* Units (sequence*num_kv_heads + KV head) that `rank` computes in a sharded
  * batched prefill, in all-gather order (unit i*nranks + rank); returns their
  * count (0 when nseq*num_kv_heads does not divide by nranks). */

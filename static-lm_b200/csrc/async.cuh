@@ -50,19 +50,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
 // soon as another thread of the CTA gave up (*abort set): on a timeout the
 // thread sets *abort and the kernel's error flag, and returns false.
 constexpr long long WAIT_LIMIT = 2000000000LL;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
-                                          int32_t *err) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, unsigned parity, volatile int *abort,
+                                                int32_t *err, long long limit) {
     if (mbar_test(bar, parity)) return true;  // fast path: the phase is already complete
     const long long t0 = clock64();
     while (!mbar_test(bar, parity)) {
         if (*abort) return false;
-        if (clock64() - t0 > WAIT_LIMIT) {
+        if (clock64() - t0 > limit) {
             *abort = 1;
             if (err) atomicExch(err, 3);
             return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, volatile int *abort,
+                                          int32_t *err) {
+    return mbar_wait_limit(bar, parity, abort, err, WAIT_LIMIT);
 }
 // One row copy global -> shared through the TMA engine, completing bytes on bar.
 __device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,

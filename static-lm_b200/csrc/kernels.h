@@ -67,6 +67,9 @@ void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows
                     cudaStream_t s);
 void launch_rope_vec(float *vec, size_t len, const float *cos_row, const float *sin_row,
                      int head_dim, cudaStream_t s);
+// One CTA waiting, with limit_cycles as its bound, on an mbarrier that
+// nothing arrives on: sets *err = 3 when the wait gives up.
+void launch_wait_selftest(long long limit_cycles, int32_t *err, cudaStream_t s);
 
 // ---- Q4_0 x Q8_0 GEMV / GEMM (kernels_gemv.cu)
 enum Epilogue : int {

@@ -433,6 +433,12 @@ __global__ void __launch_bounds__(TC_THREADS) attn_prefill_tc_kernel(AttnArgs a,
     }
     __syncthreads();
     tc_fence_after();
+    // The columns are freed even when that drain gave up too.  Keeping them
+    // would leave them allocated for good, and a later CTA's tcgen05.alloc on
+    // this SM would then wait for ever; freeing them can at worst let an MMA
+    // that is still running after the second bounded wait write into columns
+    // another CTA has allocated, and the launch has already set the error
+    // flag, so the call that owns this launch reports failure either way.
     if (warp == 0) tc_dealloc(taddr, TC_COLS);
 }
 

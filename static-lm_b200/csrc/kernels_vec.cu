@@ -9,6 +9,7 @@
 #include <float.h>
 #include <limits.h>
 
+#include "async.cuh"
 #include "kernels.h"
 
 namespace slm {
@@ -414,6 +415,26 @@ void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows
                     cudaStream_t s) {
     if (rows <= 0) return;
     advance_kernel<<<cdiv(rows, 128), 128, 0, s>>>(tokens, pos, next, rows);
+}
+
+// Self-test of the bounded mbarrier wait every TMA pipeline uses: thread 0
+// sets up a barrier that nothing ever arrives on, every thread waits on it
+// with the given limit; the first to give up sets the shared abort flag (the
+// others then leave at once) and the error flag (3).  Always ends.
+__global__ void wait_selftest_kernel(long long limit, int32_t *err) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int s_abort;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    mbar_wait_limit(&bar, 0u, &s_abort, err, limit);
+}
+
+void launch_wait_selftest(long long limit_cycles, int32_t *err, cudaStream_t s) {
+    wait_selftest_kernel<<<1, 64, 0, s>>>(limit_cycles, err);
 }
 
 void launch_rope_vec(float *vec, size_t len, const float *cos_row, const float *sin_row,

@@ -6,16 +6,19 @@
 #include <nccl.h>  // types and prototypes only: the library is resolved at run time
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
 #include "../../include/slm_b200.h"
+#include "async.cuh"
 #include "kernels.h"
 
 using namespace slm;
@@ -390,6 +393,24 @@ SLM_EXPORT int slm_gemm_q4_0_f32_noalloc(const slm_qmatrix *w, const float *inpu
     return gemm_into(w, x, output_dev, batch, rows, cols, st);
 }
 
+SLM_EXPORT int slm_selftest_bounded_wait(int device, uint64_t limit_cycles) {
+    if (limit_cycles == 0 || limit_cycles > (uint64_t)WAIT_LIMIT)
+        return fail(SLM_ERR_INVALID_ARG, "limit_cycles must be in [1, 2e9]");
+    DeviceScope ds(device);
+    int32_t *err = nullptr, host = 0;
+    CUDA_TRY(cudaMalloc(&err, sizeof(int32_t)));
+    cudaError_t e = cudaMemset(err, 0, sizeof(int32_t));
+    if (e == cudaSuccess) {
+        launch_wait_selftest((long long)limit_cycles, err, 0);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(&host, err, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    cudaFree(err);
+    if (e != cudaSuccess) return fail(SLM_ERR_CUDA, std::string("wait self-test: ") + cudaGetErrorString(e));
+    if (host == 3) return fail(SLM_ERR_DEVICE_INPUT, "a device wait timed out");
+    return fail(SLM_ERR_CUDA, "wait self-test: the wait did not report its timeout");
+}
+
 SLM_EXPORT int slm_quantize_row_q8_0(const float *src, void *dst, uint64_t n, void *stream) {
     if (n % QK) return fail(SLM_ERR_SHAPE, "src length must be a multiple of 32");
     if (n == 0) return SLM_OK;
@@ -601,11 +622,15 @@ enum StepKind { STEP_DECODE = 0, STEP_PREFILL = 1, STEP_EMBED = 2, STEP_PREFILL_
 // or the system's) so that the library itself has no link-time dependency.
 struct NcclApi {
     decltype(&ncclGetUniqueId) get_id = nullptr;
-    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
     decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclCommAbort) abort = nullptr;
+    decltype(&ncclCommGetAsyncError) async_error = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
-    bool ok() const { return get_id && init_rank && all_gather && destroy && error_string; }
+    bool ok() const {
+        return get_id && init_rank_config && all_gather && destroy && abort && async_error && error_string;
+    }
 };
 
 const NcclApi &nccl_api() {
@@ -615,14 +640,18 @@ const NcclApi &nccl_api() {
         if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
         if (!h) return a;
         a.get_id = reinterpret_cast<decltype(a.get_id)>(dlsym(h, "ncclGetUniqueId"));
-        a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+        a.init_rank_config =
+            reinterpret_cast<decltype(a.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
         a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
         a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+        a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
+        a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
         a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
         return a;
     }();
     return api;
 }
+
 
 }  // namespace
 
@@ -666,9 +695,85 @@ struct slm_model {
     int shard_n = 1, shard_r = 0;
     ncclComm_t comm = nullptr;
     float *shard_send = nullptr, *shard_recv = nullptr;  // R*dim floats each
+    // Communicator failures: every NCCL call and wait is bounded by
+    // comm_timeout_ms; the first failure of a forward is kept here (code,
+    // message) and returned by the entry point that ran the forward.
+    uint32_t comm_timeout_ms = 120000;
+    int comm_rc = SLM_OK;
+    std::string comm_msg;
 };
 
 namespace {
+
+// Drop the communicator after a failure (ncclCommAbort also ends any of its
+// kernels still waiting for a peer); the model stays usable, the shard group
+// does not (slm_model_prefill_batch then asks for a new attach).
+void comm_abort(slm_model *m) {
+    if (m->comm) nccl_api().abort(m->comm);
+    m->comm = nullptr;
+}
+
+// Wait, bounded by the model's communicator timeout, until the non-blocking
+// communicator has no operation in progress after a call that returned r.
+int comm_settle(slm_model *m, ncclResult_t r, const char *what) {
+    const NcclApi &api = nccl_api();
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress) {
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(m->comm_timeout_ms)) {
+            comm_abort(m);
+            return fail(SLM_ERR_TIMEOUT, std::string(what) + ": no progress within the communicator timeout "
+                                             "(a rank did not join); communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+        if (api.async_error(m->comm, &r) != ncclSuccess) break;
+    }
+    if (r != ncclSuccess) {
+        const std::string msg = std::string(what) + ": " + api.error_string(r);
+        comm_abort(m);
+        return fail(SLM_ERR_CUDA, msg);
+    }
+    return SLM_OK;
+}
+
+// Wait for everything enqueued on the model stream when its work includes
+// collectives: bounded by the communicator timeout, checking the
+// communicator's asynchronous error meanwhile; on a timeout or an error the
+// communicator is aborted (which ends its waiting kernels) before the stream
+// is drained.
+int comm_wait_stream(slm_model *m) {
+    const NcclApi &api = nccl_api();
+    cudaEvent_t ev = nullptr;
+    CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaEventRecord(ev, m->stream);
+    const auto t0 = std::chrono::steady_clock::now();
+    int rc = SLM_OK;
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) {
+            rc = fail(SLM_ERR_CUDA, std::string("collective step: ") + cudaGetErrorString(q));
+            break;
+        }
+        ncclResult_t ar = ncclSuccess;
+        if (m->comm && api.async_error(m->comm, &ar) == ncclSuccess && ar != ncclSuccess &&
+            ar != ncclInProgress) {
+            const std::string msg = std::string("collective step: ") + api.error_string(ar);
+            comm_abort(m);
+            rc = fail(SLM_ERR_CUDA, msg);
+            break;
+        }
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(m->comm_timeout_ms)) {
+            comm_abort(m);
+            rc = fail(SLM_ERR_TIMEOUT, "collective step: not complete within the communicator timeout "
+                                       "(a rank stopped taking part); communicator aborted");
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    cudaStreamSynchronize(m->stream);
+    cudaEventDestroy(ev);
+    return rc;
+}
 
 std::vector<uint8_t> concat_rows(const std::vector<std::pair<const void *, uint64_t>> &parts,
                                  uint64_t cols) {
@@ -861,8 +966,15 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
                 const int upr = n_units / m->shard_n, kd = kv_mul * m->hd;
                 launch_shard_pack(xb, d, m->shard_send, upr, m->shard_n, m->shard_r,
                                   (int)c.num_kv_heads, kd, seq_rows, st);
-                nccl_api().all_gather(m->shard_send, m->shard_recv, (size_t)upr * seq_rows * kd,
-                                      ncclFloat32, m->comm, st);
+                if (m->comm && m->comm_rc == SLM_OK) {
+                    const ncclResult_t r = nccl_api().all_gather(
+                        m->shard_send, m->shard_recv, (size_t)upr * seq_rows * kd, ncclFloat32, m->comm, st);
+                    const int rc = comm_settle(m, r, "ncclAllGather");
+                    if (rc != SLM_OK) {
+                        m->comm_rc = rc;
+                        m->comm_msg = g_err;
+                    }
+                }
                 launch_shard_unpack(m->shard_recv, xb, d, upr, m->shard_n, (int)c.num_kv_heads, kd,
                                     seq_rows, st);
             }
@@ -1354,6 +1466,9 @@ SLM_EXPORT int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32
     const int rows = (int)(nseq * n);
     TRY(check_tokens(m, rows, tokens));
     if (m->shard_n > 1) {
+        if (!m->comm)
+            return fail(SLM_ERR_INVALID_ARG, "the shard group failed earlier (communicator aborted); "
+                                             "call slm_model_attach_shard again");
         if ((nseq * m->cfg.num_kv_heads) % (uint32_t)m->shard_n)
             return fail(SLM_ERR_SHAPE, "nseq * num_kv_heads must divide by the number of ranks");
         AttnArgs probe = attn_args_for(&m->cfg);
@@ -1372,8 +1487,15 @@ SLM_EXPORT int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32
         pos[r] = (uint32_t)(r % n);
     }
     TRY(stage_rows(m, rows, tokens, slot.data(), 0, pos.data(), 0));
+    m->comm_rc = SLM_OK;
     enqueue_forward(m, 0, rows, (int)n, STEP_PREFILL_BATCH, m->stream, 0, nullptr, (int)n);
     TRY(launch_check("batched prefill"));
+    if (m->shard_n > 1) {
+        // the collectives make this forward wait on the other ranks: bounded
+        const int rc = comm_wait_stream(m);
+        if (m->comm_rc != SLM_OK) return fail(m->comm_rc, m->comm_msg);
+        TRY(rc);
+    }
     return fetch_next(m, (int)nseq, next);
 }
 
@@ -1396,6 +1518,12 @@ SLM_EXPORT int slm_model_set_prefill_mode(slm_model *m, int mode) {
     return SLM_OK;
 }
 
+SLM_EXPORT int slm_model_set_comm_timeout(slm_model *m, uint32_t timeout_ms) {
+    if (!m || timeout_ms == 0) return fail(SLM_ERR_INVALID_ARG, "model is null or timeout is 0");
+    m->comm_timeout_ms = timeout_ms;
+    return SLM_OK;
+}
+
 SLM_EXPORT int slm_model_attach_shard(slm_model *m, const void *id, uint64_t bytes, int nranks,
                                       int rank) {
     if (!m) return fail(SLM_ERR_INVALID_ARG, "model is null");
@@ -1410,15 +1538,27 @@ SLM_EXPORT int slm_model_attach_shard(slm_model *m, const void *id, uint64_t byt
     const NcclApi &api = nccl_api();
     if (!api.ok()) return fail(SLM_ERR_CUDA, "no NCCL library (libnccl.so.2) could be loaded");
     DeviceScope ds(m->device);
+    // the send/receive buffers are made once and kept across attach attempts
     const size_t bytes_buf = (size_t)m->R * m->cfg.dim * sizeof(float);
-    CUDA_TRY(cudaMalloc(&m->shard_send, bytes_buf));
-    CUDA_TRY(cudaMalloc(&m->shard_recv, bytes_buf));
+    if (!m->shard_send) CUDA_TRY(cudaMalloc(&m->shard_send, bytes_buf));
+    if (!m->shard_recv) CUDA_TRY(cudaMalloc(&m->shard_recv, bytes_buf));
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
+    // non-blocking set-up, so that a rank that never joins ends in a timeout
+    // here instead of a wait without end
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 0;
     ncclComm_t comm = nullptr;
-    const ncclResult_t r = api.init_rank(&comm, nranks, uid, rank);
-    if (r != ncclSuccess) return fail(SLM_ERR_CUDA, std::string("ncclCommInitRank: ") + api.error_string(r));
+    ncclResult_t r = api.init_rank_config(&comm, nranks, uid, rank, &config);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        if (comm) api.abort(comm);
+        return fail(SLM_ERR_CUDA, std::string("ncclCommInitRankConfig: ") + api.error_string(r));
+    }
     m->comm = comm;
+    m->shard_n = 1;  // not sharded until the group is complete
+    m->shard_r = 0;
+    if (r == ncclInProgress) api.async_error(comm, &r);
+    TRY(comm_settle(m, r, "ncclCommInitRankConfig"));
     m->shard_n = nranks;
     m->shard_r = rank;
     return SLM_OK;

@@ -219,6 +219,11 @@ class Model:
         buf = C.create_string_buffer(bytes(nccl_id), 128) if nranks > 1 else None
         lib().slm_model_attach_shard(self.h, buf, 128 if buf is not None else 0, nranks, rank)
 
+    def set_comm_timeout(self, ms: int):
+        """Bound (milliseconds) on the shard group's set-up and on each sharded
+        prefill's wait for its collectives; past it the call raises TIMEOUT."""
+        lib().slm_model_set_comm_timeout(self.h, ms)
+
     def set_prefill_mode(self, tensor_cores: bool):
         """Prefill attention on the tcgen05 tensor cores (3xTF32, ~1e-6
         relative to the exact path) or bit-exact on the CUDA cores (default)."""

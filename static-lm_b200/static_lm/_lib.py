@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(os.path.dirname(HERE), "libslm_b200.so")
 
 SLM_OK = 0
 STATUS_NAMES = {1: "INVALID_ARG", 2: "OUT_OF_BOUNDS", 3: "OVERLAP", 4: "SHAPE", 5: "CAPACITY",
-                6: "CUDA", 7: "DEVICE_INPUT"}
+                6: "CUDA", 7: "DEVICE_INPUT", 8: "TIMEOUT"}
 
 
 class SlmError(RuntimeError):
@@ -83,6 +83,7 @@ SIGNATURES = {
     "slm_gemm_q4_0_scratch_bytes": (_U64, [_U64, _U64], False),
     "slm_gemm_q4_0_f32_noalloc": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V], True),
     "slm_quantize_row_q8_0": (C.c_int, [_V, _V, _U64, _V], True),
+    "slm_selftest_bounded_wait": (C.c_int, [C.c_int, _U64], False),
     "slm_exec_rmsnorm": (C.c_int, [C.POINTER(_V), _V, _U64, C.c_float, _V], True),
     "slm_exec_softmax": (C.c_int, [C.POINTER(_V), _V, _U64, _V], True),
     "slm_exec_swiglu": (C.c_int, [C.POINTER(_V), _V, _U64, _V], True),
@@ -104,6 +105,7 @@ SIGNATURES = {
     "slm_model_prefill_batch": (C.c_int, [_V, _U32, _U32P, _I32P, _U32, _I32P], True),
     "slm_nccl_unique_id": (C.c_int, [_V, _U64], True),
     "slm_model_attach_shard": (C.c_int, [_V, _V, _U64, C.c_int, C.c_int], True),
+    "slm_model_set_comm_timeout": (C.c_int, [_V, _U32], True),
     "slm_model_set_prefill_mode": (C.c_int, [_V, C.c_int], True),
     "slm_shard_units": (_U32, [_U32, _U32, _U32, _U32, _U32P, _U32], False),
     "slm_model_generate": (C.c_int, [_V, _U32, _I32P, _U32, _I32P, _U32, C.c_int32, _U32P], True),

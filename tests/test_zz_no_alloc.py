@@ -1,10 +1,12 @@
-"""The allocation-free GEMM entry point (static device scratch) against the
-arena entry point, through the C ABI.  Collected last on purpose: it must
-pass alone in a fresh process and after every other test, since all calls
-share one static buffer that keeps the previous call's contents."""
+"""The allocation-free GEMM entry point (static device scratch) through the C
+ABI, against the CPU oracle's gemm_q4_0 and against the arena entry point.
+Collected last on purpose: it must pass alone in a fresh process and after
+every other test, since all calls share one static buffer that keeps the
+previous call's contents."""
 import numpy as np
 import pytest
 
+import oracle as O
 import static_lm as S
 from static_lm import synth
 from static_lm._lib import SlmError, lib
@@ -12,6 +14,7 @@ from static_lm._lib import SlmError, lib
 pytestmark = pytest.mark.gpu
 
 NOALLOC_SCRATCH_BYTES = 4 << 20  # SLM_NOALLOC_SCRATCH_BYTES
+Q8X_BLOCK_BYTES = 68             # one 32-element block in the scratch
 
 
 def _arena_gemm(qm, x, batch, rows, cols):
@@ -31,28 +34,32 @@ def _noalloc_gemm(torch, qm, x, batch, rows, cols):
     return out.cpu().numpy()
 
 
-def test_noalloc_gemm_matches_arena_gemm_on_consecutive_calls(cuda):
-    # two calls in a row with different inputs and sizes: the second must not
-    # see anything of the first call's scratch contents
+def test_noalloc_gemm_matches_oracle_and_arena_gemm_on_consecutive_calls(cuda):
+    # calls in a row with different inputs and sizes: a later call must not
+    # see anything of an earlier call's scratch contents
     for batch, rows, cols, seed in ((64, 960, 576, 1), (3, 300, 1536, 2), (64, 960, 576, 3)):
         w = synth.synth_q4(rows, cols, seed)
         qm = S.QMatrix(w, rows, cols)
         x = (np.random.default_rng(seed).standard_normal(batch * cols)).astype(np.float32)
-        want = _arena_gemm(qm, x, batch, rows, cols)
         got = _noalloc_gemm(cuda, qm, x, batch, rows, cols)
+        want = O.gemm_f32(w, x, batch, rows, cols, O.MODE_X86, 4)
         assert np.array_equal(got, want), (batch, rows, cols, np.abs(got - want).max())
+        assert np.array_equal(got, _arena_gemm(qm, x, batch, rows, cols))
 
 
 def test_noalloc_gemm_rejects_sizes_beyond_the_static_scratch(cuda):
     rows, cols = 32, 1536
-    qm = S.QMatrix(synth.synth_q4(rows, cols, 4), rows, cols)
-    batch = NOALLOC_SCRATCH_BYTES // 68 * 32 // cols + 1  # one row more than fits
+    w = synth.synth_q4(rows, cols, 4)
+    qm = S.QMatrix(w, rows, cols)
+    fit = NOALLOC_SCRATCH_BYTES // Q8X_BLOCK_BYTES * 32 // cols  # the largest batch that fits
+    batch = fit + 1
     x = cuda.zeros(batch * cols, dtype=cuda.float32, device="cuda")
     out = cuda.zeros(batch * rows, dtype=cuda.float32, device="cuda")
     with pytest.raises(SlmError) as e:
         lib().slm_gemm_q4_0_f32_noalloc(qm.h, x.data_ptr(), out.data_ptr(), batch, rows, cols, None)
     assert "static buffer" in str(e.value)
-    # the largest size that fits still runs
-    fit = NOALLOC_SCRATCH_BYTES // 68 * 32 // cols
-    lib().slm_gemm_q4_0_f32_noalloc(qm.h, x.data_ptr(), out.data_ptr(), fit, rows, cols, None)
-    cuda.cuda.synchronize()
+    # the largest size that fits runs and fills the buffer to its last block:
+    # its output is checked, so an off-by-one at the buffer's end would show
+    xf = (np.random.default_rng(5).standard_normal(fit * cols)).astype(np.float32)
+    got = _noalloc_gemm(cuda, qm, xf, fit, rows, cols)
+    assert np.array_equal(got, O.gemm_f32(w, xf, fit, rows, cols, O.MODE_X86, 4))
