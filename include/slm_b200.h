@@ -48,6 +48,18 @@ enum {
  * cores with a 3xTF32 split. */
 #define SLM_PREFILL_EXACT 0
 #define SLM_PREFILL_TENSOR_CORES 1
+/* slm_causal_attention_rows only: every row attended as a decode row with
+ * the split-K flash-decode kernel (see slm_model_set_decode_mode). */
+#define SLM_ATTN_FLASH_DECODE 2
+
+/* Attention arithmetic of decode steps (slm_model_set_decode_mode):
+ * SLM_DECODE_EXACT reproduces causal_multi_head_attention_jit bit for bit
+ * (every PV sum one sequential chain over the keys); SLM_DECODE_FLASH splits
+ * the keys into 128-key chunks (split-K flash-decode: per-chunk maximum, exp
+ * sums and PV, combined by the last chunk's CTA), about 1e-6 relative to the
+ * exact path. */
+#define SLM_DECODE_EXACT 0
+#define SLM_DECODE_FLASH 1
 
 /* Message of the calling thread's last failed call ("" if none). */
 const char *slm_last_error(void);
@@ -177,6 +189,29 @@ int slm_exec_residual_add(const float *const *inputs, float *out, uint64_t len, 
 int slm_exec_l2_norm(const float *const *inputs, float *out, uint64_t len, float eps,
                      void *stream);
 
+/* JitKernelFn (src/jit/engine.rs:15): the raw entry point of a compiled
+ * FuseGraph, (inputs, output, len).  Here inputs is a host array of device
+ * pointers and output a device pointer; the function enqueues the operator
+ * on the stream bound at compile time and returns (the reference's runs to
+ * completion before returning; here results are stream-ordered). */
+typedef void (*slm_jit_kernel_fn)(const float *const *inputs, float *output, size_t len);
+enum {
+    SLM_JIT_RMSNORM = 0,      /* FuseGraph::rmsnorm(n, eps), inputs {x, weight} (graph.rs:141-155) */
+    SLM_JIT_SOFTMAX = 1,      /* FuseGraph::softmax(), inputs {x} (graph.rs:168-179) */
+    SLM_JIT_SWIGLU = 2,       /* FuseGraph::swiglu(), inputs {gate, up} (graph.rs:131-138) */
+    SLM_JIT_RESIDUAL_ADD = 3, /* FuseGraph::residual_add(), inputs {a, b} (graph.rs:158-164) */
+    SLM_JIT_L2_NORM = 4       /* FuseGraph::l2_norm(eps), inputs {x} (graph.rs:182-193) */
+};
+/* JitEngine::compile (engine.rs:66-72): a function pointer with the
+ * JitKernelFn calling convention for operator `op`, with the constants its
+ * FuseGraph constructor bakes in (n: the element count whose 1/n RMSNorm
+ * uses; eps) and the stream (a cudaStream_t, NULL = legacy default) it
+ * enqueues on.  The same (op, n, eps, stream) returns the same pointer (the
+ * engine's graph cache); up to 64 distinct ones per process, then
+ * SLM_ERR_CAPACITY.  The functions stay valid until the process exits.  A
+ * launch failure inside one is reported by slm_last_error() on that thread. */
+int slm_jit_compile(int op, uint64_t n, float eps, void *stream, slm_jit_kernel_fn *kernel_out);
+
 /* RoPE tables of LayerWorkspace::allocate (transformer.rs:124-133), computed
  * on the host with the C library's powf/sinf/cosf; cos/sin hold
  * max_seq*head_dim/2 floats. */
@@ -195,8 +230,10 @@ int slm_causal_attention(const float *q_dev, const float *k_cache_dev, const flo
  * (transformer.rs:563-593) over causal_multi_head_attention_jit.  q [n][dim],
  * k/v caches [max_seq_len][kv_dim] holding positions < start_pos+n,
  * att [n][num_heads][max_seq_len] scratch, out [n][dim].  mode is
- * SLM_PREFILL_EXACT (bit-exact) or SLM_PREFILL_TENSOR_CORES (3xTF32 tensor
- * cores, head_dim 32 or 64; other shapes run exact).  Synchronizes `stream`. */
+ * SLM_PREFILL_EXACT (bit-exact), SLM_PREFILL_TENSOR_CORES (3xTF32 tensor
+ * cores, head_dim 32 or 64; other shapes run exact) or SLM_ATTN_FLASH_DECODE
+ * (each row through the split-K flash-decode kernel; head_dim 64 or 128,
+ * else SLM_ERR_SHAPE).  Synchronizes `stream`. */
 int slm_causal_attention_rows(const float *q_dev, const float *k_cache_dev,
                               const float *v_cache_dev, float *att_dev, float *out_dev,
                               const slm_config *cfg, uint32_t n, uint32_t start_pos, int mode,
@@ -263,6 +300,15 @@ int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
  * callers that accept the tolerance.  Decode is always exact.  No reference
  * counterpart (the reference has one CPU path). */
 int slm_model_set_prefill_mode(slm_model *m, int mode);
+/* Attention arithmetic of decode steps (decode_batch, forward_token,
+ * generate, decode_steps_device, embed excluded): SLM_DECODE_EXACT (default,
+ * bit-exact) or SLM_DECODE_FLASH (split-K flash-decode, head_dim 64 or 128
+ * and kv_mul 1, 2, 3, 4, 6 or 8; other shapes stay exact).  Flash results are
+ * within 1e-3 relative / 1e-4 absolute of the exact attention; greedy tokens
+ * may differ where Q8_0 rounding of the attention output flips a near-tie.
+ * Drops the captured decode graphs.  No reference counterpart (the reference
+ * has one CPU path). */
+int slm_model_set_decode_mode(slm_model *m, int mode);
 /* NCCL unique id (bytes = 128) for slm_model_attach_shard; made on one rank
  * and sent to the others by the host. */
 int slm_nccl_unique_id(void *id_out, uint64_t bytes);

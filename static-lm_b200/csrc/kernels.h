@@ -54,6 +54,9 @@ void launch_argmax(const float *logits, size_t ld, int n, int32_t *out, int rows
 void launch_softmax_vec(const float *x, float *out, size_t len, cudaStream_t s);
 void launch_rmsnorm_vec(const float *x, const float *w, float *out, size_t len, float eps,
                         cudaStream_t s);
+// The same with 1/n given (a graph built for n elements run on len)
+void launch_rmsnorm_vec_inv_n(const float *x, const float *w, float *out, size_t len, float eps,
+                              float inv_n, cudaStream_t s);
 void launch_swiglu_vec(const float *g, const float *u, float *out, size_t len, cudaStream_t s);
 void launch_residual_add_vec(const float *a, const float *b, float *out, size_t len,
                              cudaStream_t s);
@@ -126,7 +129,12 @@ bool gemv_fuses_norm(int rows, int nb, int epi, int batch);
 // Opt the GEMV kernels into `bytes` of dynamic shared memory (current device).
 void set_gemv_smem_limit(int bytes);
 
-// ---- attention (kernels_attn.cu)
+// ---- attention (kernels_attn.cu, kernels_attn_flash.cu, kernels_attn_tc.cu)
+// Boxes of the KV-cache tensor maps: K = 32 floats x K_BOX_KEYS positions
+// (128-byte swizzle), V = head_dim floats x V_BOX_POSITIONS positions.
+constexpr int K_BOX_KEYS = 128;
+constexpr int V_BOX_POSITIONS = 64;
+
 struct AttnArgs {
     const float *q;          // [rows][dim] (RoPE applied)
     size_t ldq;
@@ -163,11 +171,28 @@ struct AttnArgs {
     // prefill (fused path): 1 = attention on the tensor cores (tcgen05, 3xTF32;
     // ~1e-6 relative to the exact path instead of bit-exact)
     int prefill_tc;
+    // fused path, softmax + PV: 0 = one CTA per (row, KV head) running its
+    // kv_mul heads; 1 = one CTA per (row, query head), a thread per dim;
+    // 2 = the same with a thread per dim pair.  Same results.
+    int pv_per_head;
+    // decode (opt-in split-K flash-decode, kernels_attn_flash.cu): partial
+    // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)] and arrival
+    // counters [rows][num_kv_heads] (zero between launches)
+    float *fd_part;
+    int32_t *fd_cnt;
+    int fd_nch;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)
 void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
                       cudaStream_t s);
+// Split-K flash-decode (kernels_attn_flash.cu): one CTA per (128-key chunk,
+// KV head, row), the last CTA of a (row, KV head) combines the chunks; about
+// 1e-6 relative to the exact path.  kmap / vmap as for launch_attn_fused.
+bool flash_decode_ok(const AttnArgs &a);
+int flash_decode_chunks(int max_seq);
+void launch_flash_decode(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vmap, cudaStream_t s);
+void set_flash_decode_smem();
 // Tensor-core causal prefill (kernels_attn_tc.cu): one launch per layer over
 // (128 query rows, query head) tiles, then the Q8_0 of the output when asked.
 bool attn_prefill_tc_ok(const AttnArgs &a);

@@ -192,31 +192,36 @@ __global__ void __launch_bounds__(1024) attn_pv_kernel(AttnArgs a) {
 // Fused path: V comes through a 3-D tensor map over the cache planes
 // (x = kv_dim floats, y = positions, z = plane), one TMA box of TT_V rows x
 // head_dim floats per stage.
-constexpr int TT_V = 64;
+constexpr int TT_V = V_BOX_POSITIONS;
 constexpr int PV_THREADS = 256;
 
 struct FusedShape {
     int tt;      // V rows per stage (one TMA box)
     int lp;      // scores row stride (floats)
+    int nst;     // stages of the V ring
     size_t smem; // dynamic shared memory bytes (with 128 B of alignment slack)
 };
 
-__host__ __device__ inline FusedShape fused_shape(int kv_mul, int hd, int max_len) {
+// Shared memory of a softmax + PV CTA over `hpc` query heads with an
+// `nst`-stage V ring.
+__host__ __device__ inline FusedShape fused_shape(int hpc, int hd, int max_len, int nst = FUSED_STAGES) {
     FusedShape f;
     f.tt = TT_V;
     f.lp = (max_len + 31) / 32 * 32 + 4;
-    f.smem = sizeof(float) * ((size_t)FUSED_STAGES * TT_V * hd + (size_t)kv_mul * f.lp +
-                              (size_t)kv_mul * hd + 64 + 8 * 32) +
+    f.nst = nst;
+    f.smem = sizeof(float) * ((size_t)nst * TT_V * hd + (size_t)hpc * f.lp +
+                              (size_t)hpc * hd + 64 + 8 * 32) +
              128;
     return f;
 }
+constexpr int PV_MAX_STAGES = 16;
 
 // (A) scores: one CTA per (128 keys, KV head, row).  The 128 K rows go
 // global -> shared through the TMA engine, one bulk copy per row (rows padded
 // to hd+4 floats), all completing on one mbarrier; thread t then runs the
 // kv_mul query-head dot chains of key t side by side (kv_mul-way ILP), each
 // chain sequential in i.
-constexpr int TILE_KEYS = 128;
+constexpr int TILE_KEYS = K_BOX_KEYS;
 
 __global__ void __launch_bounds__(TILE_KEYS) attn_scores_tiled_kernel(AttnArgs a) {
     extern __shared__ __align__(16) float smem[];
@@ -975,22 +980,28 @@ struct PvVec {
     }
 };
 
+// KVM here is the number of query heads of one CTA (HPC): all kv_mul heads
+// of a KV head (grid.x = num_kv_heads), or one query head (grid.x =
+// num_heads; the kv_mul CTAs of a KV head then each stream its V rows, mostly
+// from L2).  NST is the depth of the V ring (<= PV_MAX_STAGES), chosen by the
+// launch from the CTAs each SM holds.
 template <int KVM, int NH, int ND>
 __global__ void __launch_bounds__(512)
-    attn_softmax_pv_kernel(AttnArgs a, int lp, const __grid_constant__ CUtensorMap vmap) {
+    attn_softmax_pv_kernel(AttnArgs a, int lp, int NST, const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t bar_full[FUSED_STAGES], bar_empty[FUSED_STAGES];
+    __shared__ __align__(8) uint64_t bar_full[PV_MAX_STAGES], bar_empty[PV_MAX_STAGES];
     __shared__ int s_abort, s_issued;
     // TMA destinations 128-byte aligned (the launch adds 128 B of slack)
     float *smem = reinterpret_cast<float *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
     constexpr int tt = TT_V;
     const int nth = blockDim.x;
-    const int g = blockIdx.x, r = blockIdx.y;
+    const int h0 = blockIdx.x * KVM, r = blockIdx.y;  // first query head of this CTA
+    const int g = h0 / (a.num_heads / a.num_kv_heads);  // its KV head
     if (!unit_owned(a, r, g)) return;  // CTA-uniform: another rank's unit
     const int hd = a.head_dim;
     const int tid = threadIdx.x;
-    float *s_ring = smem;                                   // [STAGES][tt][hd]
-    float *s_sc = s_ring + (size_t)FUSED_STAGES * tt * hd;  // [KVM][lp]
+    float *s_ring = smem;                                   // [NST][tt][hd]
+    float *s_sc = s_ring + (size_t)NST * tt * hd;           // [KVM][lp]
     float *s_out = s_sc + (size_t)KVM * lp;                 // [KVM*hd]
     float *s_red = s_out + (size_t)KVM * hd;                // 64 + 8*32 floats
     const int L = row_len(a, r);
@@ -1005,7 +1016,7 @@ __global__ void __launch_bounds__(512)
     const unsigned tile_bytes = (unsigned)tt * (unsigned)hd * 4u;
 
     if (tid == 0) {
-        for (int st = 0; st < FUSED_STAGES; st++) {
+        for (int st = 0; st < NST; st++) {
             mbar_init(&bar_full[st], 1);
             mbar_init(&bar_empty[st], (unsigned)n_cons);
         }
@@ -1016,7 +1027,7 @@ __global__ void __launch_bounds__(512)
     __syncthreads();
     if (producer && lane == 0) {
         int k = 0;
-        for (; k < FUSED_STAGES && k < ntiles; k++) {
+        for (; k < NST && k < ntiles; k++) {
             mbar_arrive_expect_tx(&bar_full[k], tile_bytes);
             tma_load_3d(s_ring + (size_t)k * tt * hd, &vmap, vx, k * tt, vz, &bar_full[k]);
         }
@@ -1026,7 +1037,7 @@ __global__ void __launch_bounds__(512)
     pdl_wait();
 
     // scores of the KVM heads of this group (cp.async, awaited before the softmax)
-    const float *att = a.att + ((size_t)r * a.num_heads + (size_t)g * KVM) * a.att_ld;
+    const float *att = a.att + ((size_t)r * a.num_heads + (size_t)h0) * a.att_ld;
     const bool vec = (a.att_ld & 3) == 0 && ((uintptr_t)att & 15) == 0;
     if (vec) {
         const int c4 = (L + 3) >> 2;
@@ -1123,7 +1134,7 @@ __global__ void __launch_bounds__(512)
     for (int h = 0; h < KVM; h++) {
         const float inv = s_red[48 + h];
         float *row = s_sc + h * lp;
-        float *prow = a.write_probs ? a.att + ((size_t)r * a.num_heads + g * KVM + h) * a.att_ld : nullptr;
+        float *prow = a.write_probs ? a.att + ((size_t)r * a.num_heads + h0 + h) * a.att_ld : nullptr;
         int t = tid;
         for (; t + 3 * nth < L; t += 4 * nth) {
             const float p0 = __fmul_rn(row[t], inv), p1 = __fmul_rn(row[t + nth], inv);
@@ -1150,13 +1161,13 @@ __global__ void __launch_bounds__(512)
     __syncthreads();  // probabilities complete
     if (producer) {
 #pragma unroll 1
-        for (int k = FUSED_STAGES; k < ntiles; k++) {
+        for (int k = NST; k < ntiles; k++) {
             // the stage is free once every consumer warp released tile k - STAGES
-            if (!mbar_wait(&bar_empty[k % FUSED_STAGES], (unsigned)((k / FUSED_STAGES) - 1) & 1u,
+            if (!mbar_wait(&bar_empty[k % NST], (unsigned)((k / NST) - 1) & 1u,
                            &s_abort, a.err))
                 break;
             if (lane == 0) {
-                const int st = k % FUSED_STAGES;
+                const int st = k % NST;
                 mbar_arrive_expect_tx(&bar_full[st], tile_bytes);
                 tma_load_3d(s_ring + (size_t)st * tt * hd, &vmap, vx, k * tt, vz, &bar_full[st]);
                 s_issued = k + 1;
@@ -1166,20 +1177,20 @@ __global__ void __launch_bounds__(512)
     } else if (warp < n_cons) {
         const bool active = tid < n_thr;
         const int dgrp = hd / ND;  // threads per head group
-        const int h0 = (tid / dgrp) * NH, jc = ND * (tid % dgrp);
-        float acc[NH][ND];  // out[h0 + h][jc + c]
+        const int hl = (tid / dgrp) * NH, jc = ND * (tid % dgrp);  // first head (of this CTA's), dim
+        float acc[NH][ND];  // out[hl + h][jc + c]
 #pragma unroll
         for (int h = 0; h < NH; h++)
 #pragma unroll
             for (int c = 0; c < ND; c++) acc[h][c] = 0.0f;
 #pragma unroll 1
         for (int k = 0; k < ntiles; k++) {
-            if (!mbar_wait(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u, &s_abort,
+            if (!mbar_wait(&bar_full[k % NST], (unsigned)(k / NST) & 1u, &s_abort,
                            a.err))
                 break;
             if (active) {
-                const float *vt = s_ring + (size_t)(k % FUSED_STAGES) * tt * hd + jc;  // row stride hd
-                const float *pp = s_sc + h0 * lp + k * tt;                               // head stride lp
+                const float *vt = s_ring + (size_t)(k % NST) * tt * hd + jc;  // row stride hd
+                const float *pp = s_sc + hl * lp + k * tt;                               // head stride lp
                 const int nrows = L - k * tt < tt ? L - k * tt : tt;
                 if (nrows == tt) {
                     // full tile in chunks of PV_CH positions: the shared-memory
@@ -1244,13 +1255,13 @@ __global__ void __launch_bounds__(512)
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_empty[k % FUSED_STAGES]);
+            if (lane == 0) mbar_arrive(&bar_empty[k % NST]);
         }
         if (active)
 #pragma unroll
             for (int h = 0; h < NH; h++)
 #pragma unroll
-                for (int c = 0; c < ND; c++) s_out[(h0 + h) * hd + jc + c] = acc[h][c];
+                for (int c = 0; c < ND; c++) s_out[(hl + h) * hd + jc + c] = acc[h][c];
     }
     __syncthreads();
     if (s_abort) {
@@ -1259,9 +1270,9 @@ __global__ void __launch_bounds__(512)
         if (tid == 0) {
             // the last tile issued into each stage is the one whose phase is pending
             const int n_iss = s_issued;
-            for (int k = n_iss - FUSED_STAGES < 0 ? 0 : n_iss - FUSED_STAGES; k < n_iss; k++) {
+            for (int k = n_iss - NST < 0 ? 0 : n_iss - NST; k < n_iss; k++) {
                 const long long t0 = clock64();
-                while (!mbar_test(&bar_full[k % FUSED_STAGES], (unsigned)(k / FUSED_STAGES) & 1u) &&
+                while (!mbar_test(&bar_full[k % NST], (unsigned)(k / NST) & 1u) &&
                        clock64() - t0 < WAIT_LIMIT) {
                 }
             }
@@ -1270,7 +1281,7 @@ __global__ void __launch_bounds__(512)
         return;
     }
     pdl_release();  // the successor may start while the outputs are written
-    float *orow = a.out + (size_t)r * a.ldo + (size_t)g * KVM * hd;
+    float *orow = a.out + (size_t)r * a.ldo + (size_t)h0 * hd;
     for (int k = tid; k < KVM * hd; k += nth) orow[k] = s_out[k];
     // Q8_0 of the attention output for the Wo GEMV: this CTA owns the
     // KVM*hd consecutive dims from g*KVM*hd, one 32-element block per warp
@@ -1279,10 +1290,11 @@ __global__ void __launch_bounds__(512)
         const int nbr = a.dim / 32;
         for (int blk = warp; blk < (KVM * hd) / 32; blk += nw)
             q8x_store_block(s_out[blk * 32 + lane], a.q8_out,
-                            (size_t)r * nbr + (size_t)(g * KVM * hd) / 32 + blk, lane);
+                            (size_t)r * nbr + (size_t)(h0 * hd) / 32 + blk, lane);
     }
 }
 
+// The (row, KV head) form: kv_mul heads per CTA, a 4-stage V ring.
 template <int KVM>
 void launch_softmax_pv(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t s) {
     const FusedShape f = fused_shape(KVM, a.head_dim, a.max_len);
@@ -1295,7 +1307,47 @@ void launch_softmax_pv(const AttnArgs &a, const CUtensorMap &vmap, cudaStream_t 
     // a thread per (head, dim pair): measured faster than a thread per dim
     // running every head (fewer warps) or per (head, dim) (more warps)
     launch_kernel(attn_softmax_pv_kernel<KVM, 1, 2>, grid, dim3(threads(KVM * a.head_dim / 2)), f.smem, s,
-                  a.pdl, a, f.lp, vmap);
+                  a.pdl, a, f.lp, (int)FUSED_STAGES, vmap);
+}
+
+int sm_count() {
+    static int sms = [] {
+        int dev = 0, n = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n;
+    }();
+    return sms;
+}
+
+// Depth of the per-head V ring: the shared memory an SM has, shared by the
+// CTAs it holds when the grid is spread evenly, in whole stages (2 to 16).
+// Few CTAs per SM (small batches) get deep rings, so that each CTA keeps
+// enough bytes in flight to stream its V rows at a useful rate on its own.
+FusedShape per_head_shape(const AttnArgs &a) {
+    const long long ctas = (long long)a.rows * a.num_heads;
+    const long long per_sm = (ctas + sm_count() - 1) / sm_count();
+    const size_t budget = (size_t)(FUSED_SMEM_MAX / (per_sm < 1 ? 1 : per_sm));
+    const size_t fixed = fused_shape(1, a.head_dim, a.max_len, 0).smem;
+    const size_t stage = (size_t)TT_V * a.head_dim * sizeof(float);
+    long long nst = budget > fixed ? (long long)((budget - fixed) / stage) : 0;
+    nst = nst < 2 ? 2 : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
+    return fused_shape(1, a.head_dim, a.max_len, (int)nst);
+}
+
+// The (row, query head) form: one head per CTA, a thread per dim (ND = 1) or
+// per dim pair (ND = 2); kv_mul times the CTAs of the (row, KV head) form.
+template <int ND>
+void launch_softmax_pv_per_head(const AttnArgs &args, const CUtensorMap &vmap, cudaStream_t s) {
+    AttnArgs a = args;
+    const FusedShape f = per_head_shape(a);
+    // the in-kernel Q8_0 of the output needs whole 32-element blocks per CTA
+    const bool q8_after = a.q8_out.qs && a.head_dim % 32 != 0;
+    if (q8_after) a.q8_out.qs = nullptr;
+    const int cons = (a.head_dim / ND + 31) / 32 * 32;
+    launch_kernel(attn_softmax_pv_kernel<1, 1, ND>, dim3(a.num_heads, a.rows), dim3(cons + 32), f.smem, s,
+                  a.pdl, a, f.lp, f.nst, vmap);
+    if (q8_after) launch_quantize_q8x(a.out, a.ldo, a.dim, args.q8_out, a.rows, s);
 }
 
 template <int KVM>
@@ -1473,6 +1525,13 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
         return;
     }
+    if (a.pv_per_head) {
+        if (a.pv_per_head == 2)
+            launch_softmax_pv_per_head<2>(a, vmap, s);
+        else
+            launch_softmax_pv_per_head<1>(a, vmap, s);
+        return;
+    }
     switch (kv_mul) {
         case 1: launch_softmax_pv<1>(a, vmap, s); break;
         case 2: launch_softmax_pv<2>(a, vmap, s); break;
@@ -1487,6 +1546,7 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
 
 void set_attention_smem_limit(int bytes) {
     set_attn_prefill_tc_smem();
+    set_flash_decode_smem();
     set_softmax_pv_smem<1>(bytes);
     set_softmax_pv_smem<2>(bytes);
     set_softmax_pv_smem<3>(bytes);
@@ -1495,6 +1555,7 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<6>(bytes);
     set_softmax_pv_smem<7>(bytes);
     set_softmax_pv_smem<8>(bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

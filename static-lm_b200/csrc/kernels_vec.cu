@@ -272,10 +272,9 @@ __global__ void softmax_vec_kernel(const float *x, float *out, size_t len) {
 
 // graph.rs:141-155 compiled with n = len
 __global__ void rmsnorm_vec_kernel(const float *x, const float *w, float *out, size_t len,
-                                   float eps) {
+                                   float eps, float inv_n) {
     __shared__ float sh[32];
     float s = block_lane4_sumsq(x, len, sh);
-    float inv_n = __fdiv_rn(1.0f, (float)len);
     float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_n), eps)));
     for (size_t i = threadIdx.x; i < len; i += blockDim.x)
         out[i] = __fmul_rn(__fmul_rn(x[i], rms), w[i]);
@@ -386,7 +385,15 @@ void launch_softmax_vec(const float *x, float *out, size_t len, cudaStream_t s) 
 void launch_rmsnorm_vec(const float *x, const float *w, float *out, size_t len, float eps,
                         cudaStream_t s) {
     if (!len) return;
-    rmsnorm_vec_kernel<<<1, 1024, 0, s>>>(x, w, out, len, eps);
+    // 1/n as FuseGraph::rmsnorm(n, eps) computes it (graph.rs:147): one IEEE
+    // single-precision division, identical on the host
+    rmsnorm_vec_kernel<<<1, 1024, 0, s>>>(x, w, out, len, eps, 1.0f / (float)len);
+}
+
+void launch_rmsnorm_vec_inv_n(const float *x, const float *w, float *out, size_t len, float eps,
+                              float inv_n, cudaStream_t s) {
+    if (!len) return;
+    rmsnorm_vec_kernel<<<1, 1024, 0, s>>>(x, w, out, len, eps, inv_n);
 }
 
 void launch_swiglu_vec(const float *g, const float *u, float *out, size_t len, cudaStream_t s) {

@@ -6,6 +6,7 @@
 #include <nccl.h>  // types and prototypes only: the library is resolved at run time
 
 #include <algorithm>
+#include <array>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -15,6 +16,7 @@
 #include <string>
 #include <thread>
 #include <tuple>
+#include <utility>
 #include <vector>
 
 #include "../../include/slm_b200.h"
@@ -452,6 +454,84 @@ SLM_EXPORT int slm_exec_l2_norm(const float *const *in, float *out, uint64_t len
     return launch_check("l2norm kernel");
 }
 
+// ---- JitKernelFn-compatible entry points (engine.rs:15, 66-72)
+
+namespace {
+
+// One compiled graph: the operator, the constants FuseGraph bakes in (n, eps)
+// and the stream the returned function enqueues on.
+struct JitSlot {
+    int op = -1;
+    uint64_t n = 0;
+    float eps = 0.0f;
+    float inv_n = 0.0f;
+    cudaStream_t stream = nullptr;
+};
+constexpr int JIT_SLOTS = 64;
+JitSlot g_jit[JIT_SLOTS];
+std::mutex g_jit_mu;
+
+void jit_run(int i, const float *const *in, float *out, size_t len) {
+    const JitSlot &k = g_jit[i];
+    if (!in || !out || len == 0) return;
+    switch (k.op) {
+        case SLM_JIT_RMSNORM: launch_rmsnorm_vec_inv_n(in[0], in[1], out, len, k.eps, k.inv_n, k.stream); break;
+        case SLM_JIT_SOFTMAX: launch_softmax_vec(in[0], out, len, k.stream); break;
+        case SLM_JIT_SWIGLU: launch_swiglu_vec(in[0], in[1], out, len, k.stream); break;
+        case SLM_JIT_RESIDUAL_ADD: launch_residual_add_vec(in[0], in[1], out, len, k.stream); break;
+        case SLM_JIT_L2_NORM: launch_l2norm_vec(in[0], out, len, k.eps, k.stream); break;
+        default: break;
+    }
+    launch_check("JIT kernel");  // a launch failure is left in slm_last_error()
+}
+
+// a distinct plain C function per slot, so that each carries its constants
+// without a closure argument
+template <int I>
+void jit_entry(const float *const *in, float *out, size_t len) {
+    jit_run(I, in, out, len);
+}
+template <int... I>
+constexpr std::array<slm_jit_kernel_fn, sizeof...(I)> jit_table(std::integer_sequence<int, I...>) {
+    return {&jit_entry<I>...};
+}
+const std::array<slm_jit_kernel_fn, JIT_SLOTS> g_jit_fn = jit_table(std::make_integer_sequence<int, JIT_SLOTS>{});
+
+}  // namespace
+
+SLM_EXPORT int slm_jit_compile(int op, uint64_t n, float eps, void *stream, slm_jit_kernel_fn *kernel_out) {
+    if (!kernel_out) return fail(SLM_ERR_INVALID_ARG, "kernel_out is null");
+    if (op < SLM_JIT_RMSNORM || op > SLM_JIT_L2_NORM) return fail(SLM_ERR_INVALID_ARG, "unknown JIT operator");
+    if (op == SLM_JIT_RMSNORM && n == 0) return fail(SLM_ERR_INVALID_ARG, "rmsnorm needs n > 0");
+    // constants the operator does not use do not tell graphs apart
+    if (op != SLM_JIT_RMSNORM) n = 0;
+    if (op != SLM_JIT_RMSNORM && op != SLM_JIT_L2_NORM) eps = 0.0f;
+    std::lock_guard<std::mutex> lock(g_jit_mu);
+    int free_slot = -1;
+    for (int i = 0; i < JIT_SLOTS; i++) {
+        const JitSlot &k = g_jit[i];
+        if (k.op < 0) {
+            if (free_slot < 0) free_slot = i;
+            continue;
+        }
+        // the engine's cache: the same graph gives the same function
+        if (k.op == op && k.n == n && std::memcmp(&k.eps, &eps, sizeof(float)) == 0 &&
+            k.stream == (cudaStream_t)stream) {
+            *kernel_out = g_jit_fn[i];
+            return SLM_OK;
+        }
+    }
+    if (free_slot < 0) return fail(SLM_ERR_CAPACITY, "all 64 JIT kernel slots are in use");
+    JitSlot &k = g_jit[free_slot];
+    k.op = op;
+    k.n = n;
+    k.eps = eps;
+    k.inv_n = n ? 1.0f / (float)n : 0.0f;  // FuseGraph::rmsnorm: 1.0 / (n as f32)
+    k.stream = (cudaStream_t)stream;
+    *kernel_out = g_jit_fn[free_slot];
+    return SLM_OK;
+}
+
 SLM_EXPORT int slm_rope_tables(uint32_t max_seq, uint32_t head_dim, float *cos_out,
                                float *sin_out) {
     if ((!cos_out || !sin_out) && max_seq) return fail(SLM_ERR_INVALID_ARG, "null pointer");
@@ -501,8 +581,17 @@ int check_config(const slm_config *c) {
     return SLM_OK;
 }
 
+// Softmax + PV form of the exact attention (AttnArgs::pv_per_head): one CTA
+// per (row, query head) unless SLM_PV_PER_HEAD says otherwise (0, 1 or 2);
+// every form gives the same results.
+int env_pv_per_head() {
+    const char *env = getenv("SLM_PV_PER_HEAD");
+    return env && env[0] >= '0' && env[0] <= '2' ? env[0] - '0' : 1;
+}
+
 AttnArgs attn_args_for(const slm_config *c) {
     AttnArgs a{};
+    a.pv_per_head = env_pv_per_head();
     a.dim = (int)c->dim;
     a.num_heads = (int)c->num_heads;
     a.num_kv_heads = (int)c->num_kv_heads;
@@ -551,8 +640,8 @@ SLM_EXPORT int slm_causal_attention_rows(const float *q, const float *k, const f
                                          int mode, void *stream) {
     TRY(check_config(cfg));
     if (!q || !k || !v || !att || !out) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
-    if (mode != SLM_PREFILL_EXACT && mode != SLM_PREFILL_TENSOR_CORES)
-        return fail(SLM_ERR_INVALID_ARG, "unknown prefill mode");
+    if (mode != SLM_PREFILL_EXACT && mode != SLM_PREFILL_TENSOR_CORES && mode != SLM_ATTN_FLASH_DECODE)
+        return fail(SLM_ERR_INVALID_ARG, "unknown attention mode");
     if ((uint64_t)start_pos + n > cfg->max_seq_len)
         return fail(SLM_ERR_OUT_OF_BOUNDS, "sequence position out of bounds");
     if (n == 0) return SLM_OK;
@@ -584,6 +673,37 @@ SLM_EXPORT int slm_causal_attention_rows(const float *q, const float *k, const f
     const bool have_v = encode_v_map(&vmap, v, a.kv_dim, a.max_seq, 1, a.head_dim);
     const bool have_k = encode_k_map(&kmap, k, a.kv_dim, a.max_seq, 1, a.head_dim);
     const bool have_a = encode_att_map(&amap, att, a.max_seq, a.num_heads, n, a.num_heads / a.num_kv_heads);
+    if (mode == SLM_ATTN_FLASH_DECODE) {
+        // every row as a decode row; the chunk partials and the (zeroed)
+        // arrival counters in one stream-ordered allocation
+        a.prefill_run = 0;
+        a.prefill_tc = 0;
+        a.fd_nch = flash_decode_chunks(a.max_seq);
+        const size_t pfloats = (size_t)n * a.num_kv_heads * a.fd_nch * (a.num_heads / a.num_kv_heads) *
+                               (a.head_dim + 2);
+        const size_t cbytes = sizeof(int32_t) * n * a.num_kv_heads;
+        char *scratch = nullptr;
+        if (!have_v || !have_k ||
+            cudaMallocAsync((void **)&scratch, pfloats * sizeof(float) + cbytes, st) != cudaSuccess) {
+            cudaFreeAsync(dpos, st);
+            cudaStreamSynchronize(st);
+            return fail(have_v && have_k ? SLM_ERR_CUDA : SLM_ERR_SHAPE, "flash-decode set-up");
+        }
+        a.fd_part = reinterpret_cast<float *>(scratch);
+        int32_t *cnt = reinterpret_cast<int32_t *>(scratch + pfloats * sizeof(float));
+        cudaMemsetAsync(cnt, 0, cbytes, st);
+        a.fd_cnt = cnt;
+        int rc = SLM_OK;
+        if (flash_decode_ok(a))
+            launch_flash_decode(a, kmap, vmap, st);
+        else
+            rc = fail(SLM_ERR_SHAPE, "flash-decode needs head_dim 64 or 128 and kv_mul 1, 2, 3, 4, 6 or 8");
+        cudaFreeAsync(scratch, st);
+        cudaFreeAsync(dpos, st);
+        if (rc == SLM_OK) rc = launch_check("flash-decode attention");
+        cudaStreamSynchronize(st);
+        return rc;
+    }
     if (have_v && attention_fused_ok(a))
         launch_attn_fused(a, vmap, have_k ? &kmap : nullptr, have_a ? &amap : nullptr, st);
     else
@@ -684,7 +804,12 @@ struct slm_model {
     bool use_pdl = true;     // programmatic dependent launch between decode kernels
     bool no_prefill_tiles = false;  // SLM_PREFILL_ROWWISE=1: prefill through the per-row kernels
     int prefill_mode = SLM_PREFILL_EXACT;  // slm_model_set_prefill_mode
-    int parts = 4;           // decode parts (streams) for batches of 16+ rows
+    int parts = 1;           // decode parts (streams) for batches of 16+ rows
+    int pv_per_head = 1;     // softmax + PV per (row, query head): AttnArgs::pv_per_head
+    int decode_mode = SLM_DECODE_EXACT;  // slm_model_set_decode_mode
+    float *fd_part = nullptr;  // flash-decode partials [R][kvh][fd_nch][kv_mul*(hd+2)]
+    int32_t *fd_cnt = nullptr; // flash-decode arrival counters [R][kvh], zero between launches
+    int fd_nch = 0;
     cudaStream_t side[MAX_PARTS - 1] = {};  // streams of parts 1..
     cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
@@ -900,6 +1025,10 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     aa.z_slot = 2LL * m->L;  // planes [slot][layer][K|V] from the first V plane
     aa.pdl = m->use_pdl;
     aa.tmax = row0 == 0 ? m->tmax : nullptr;
+    aa.pv_per_head = m->pv_per_head;
+    aa.fd_part = m->fd_part + r0 * c.num_kv_heads * (size_t)m->fd_nch * (c.num_heads / c.num_kv_heads) * (m->hd + 2);
+    aa.fd_cnt = m->fd_cnt + r0 * c.num_kv_heads;
+    aa.fd_nch = m->fd_nch;
     aa.tmax_ld = m->tmax_ld;
 
     Q8X qa8 = q8view(m->q8a[part], m->q8_blocks), qb8 = q8view(m->q8b[part], m->q8_blocks);
@@ -921,6 +1050,10 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         aa.write_probs = false;  // probabilities stay in shared memory
         if ((kv_mul * m->hd) % 32 == 0 && !sharded) aa.q8_out = qb8;
     }
+    // decode rows in the opt-in split-K flash-decode mode (the Q8_0 of the
+    // output inside the kernel)
+    const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && fused && m->have_kmap &&
+                       flash_decode_ok(aa);
     const int n_units = kind == STEP_PREFILL_BATCH && seq_rows > 0 ? (n / seq_rows) * (int)c.num_kv_heads : 0;
     const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
     const bool norm_gu = m->L > 0 && gate_up_norm_fused(m, n);
@@ -956,7 +1089,12 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         // attention (transformer.rs:430-443)
         aa.layer_off = (size_t)l * m->layer_stride;
         aa.z_layer = 2LL * l;
-        if (fused) {
+        if (flash) {
+            AttnArgs fa = aa;
+            fa.q8_out = qb8;
+            launch_flash_decode(fa, m->kmap, m->vmap, st);
+            mark(prof, SLM_PHASE_ATTN_FUSED);
+        } else if (fused) {
             // scores, then softmax + PV + the Q8_0 of the output
             launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr,
                               m->have_amap && row0 == 0 ? &m->amap : nullptr, st);
@@ -1078,11 +1216,32 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
 // layer: [rmsnorm], qkv, attention (fused: scores + softmax/PV, + quantize
 // unless fused into it; or scores, softmax, pv, quantize), wo, [rmsnorm],
 // gate/up, down; final rmsnorm, lm_head, argmax
+// The attention arguments of a decode step that decide which kernels run.
+AttnArgs decode_probe(const slm_model *m, int max_len) {
+    AttnArgs a = attn_args_for(&m->cfg);
+    a.ldq = m->cfg.dim;
+    a.k_base = m->kv;
+    a.v_base = m->kv + m->v_off;
+    a.att = m->att;
+    a.slot_stride = m->slot_stride;
+    a.max_len = max_len;
+    a.fd_part = m->fd_part;
+    a.fd_cnt = m->fd_cnt;
+    a.fd_nch = m->fd_nch;
+    return a;
+}
+
 uint32_t decode_launches(const slm_model *m, int n) {
-    uint32_t attn = 4;
-    if (m->use_fused_attention && m->have_vmap) {
-        const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
-        attn = ((kv_mul * m->hd) % 32 == 0) ? 2 : 3;
+    const AttnArgs pa = decode_probe(m, (int)m->cfg.max_seq_len);
+    const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
+    uint32_t attn = 4;  // scores, softmax, pv, quantize
+    if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
+        if (m->decode_mode == SLM_DECODE_FLASH && m->have_kmap && flash_decode_ok(pa))
+            attn = 1;  // flash-decode with the Q8_0 of the output inside
+        else if (m->pv_per_head)
+            attn = (m->hd % 32 == 0) ? 2 : 3;
+        else
+            attn = ((kv_mul * m->hd) % 32 == 0) ? 2 : 3;
     }
     uint32_t per_layer = 4u + attn;
     if (m->L > 0 && !qkv_norm_fused(m, n)) per_layer++;
@@ -1160,6 +1319,9 @@ int read_device_error(slm_model *m) {
     CUDA_TRY(cudaStreamSynchronize(m->stream));
     if (err) {
         CUDA_TRY(cudaMemsetAsync(m->d_err, 0, 4, m->stream));
+        // a flash-decode CTA that gave up never counted in: start the
+        // arrival counters from zero again
+        CUDA_TRY(cudaMemsetAsync(m->fd_cnt, 0, sizeof(int32_t) * m->R * m->cfg.num_kv_heads, m->stream));
         CUDA_TRY(cudaStreamSynchronize(m->stream));
         return fail(SLM_ERR_DEVICE_INPUT, err == 1   ? "token_id out of vocabulary bounds"
                                           : err == 2 ? "sequence position out of bounds"
@@ -1290,6 +1452,11 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->tmax_ld = (int)((T + 31) / 32);
     add_f(R * cfg->num_heads * (uint64_t)m->tmax_ld);  // score maxima
     for (int i = 0; i < 2 * slm_model::MAX_PARTS; i++) add_f(q8f);  // Q8X pair per decode part
+    m->fd_nch = flash_decode_chunks((int)T);
+    const uint64_t kvm = cfg->num_heads / cfg->num_kv_heads;
+    const uint64_t fd_floats = R * cfg->num_kv_heads * (uint64_t)m->fd_nch * kvm * (m->hd + 2);
+    add_f(fd_floats);                          // flash-decode partials
+    add_f(R * cfg->num_kv_heads);              // flash-decode counters (int32)
     for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
     add_f(S * m->slot_stride);                 // KV
     rc = slm_arena_create(device, cap + a16, &m->arena);
@@ -1311,6 +1478,9 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         if ((rc = alloc_view(m, q8f, &p))) return cleanup(rc);
         m->q8b[i] = p;
     }
+    if ((rc = alloc_view(m, fd_floats, &m->fd_part))) return cleanup(rc);
+    if ((rc = alloc_view(m, R * cfg->num_kv_heads, &p))) return cleanup(rc);
+    m->fd_cnt = (int32_t *)p;  // the arena starts zeroed
     int32_t **ints[] = {&m->d_tok, &m->d_pos, &m->d_slot, &m->d_next, &m->d_err};
     for (auto ip : ints) {
         if ((rc = alloc_view(m, R, &p))) return cleanup(rc);
@@ -1327,6 +1497,7 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->use_fused_attention = !(env && env[0] == '1');
     env = getenv("SLM_DECODE_ONE_STREAM");
     m->split_decode = !(env && env[0] == '1');
+    m->pv_per_head = env_pv_per_head();
     env = getenv("SLM_DECODE_PARTS");
     if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
     env = getenv("SLM_PREFILL_ROWWISE");
@@ -1515,6 +1686,18 @@ SLM_EXPORT int slm_model_set_prefill_mode(slm_model *m, int mode) {
     if (!m) return SLM_ERR_INVALID_ARG;
     if (mode != SLM_PREFILL_EXACT && mode != SLM_PREFILL_TENSOR_CORES) return SLM_ERR_INVALID_ARG;
     m->prefill_mode = mode;
+    return SLM_OK;
+}
+
+SLM_EXPORT int slm_model_set_decode_mode(slm_model *m, int mode) {
+    if (!m) return fail(SLM_ERR_INVALID_ARG, "model is null");
+    if (mode != SLM_DECODE_EXACT && mode != SLM_DECODE_FLASH) return fail(SLM_ERR_INVALID_ARG, "unknown decode mode");
+    if (mode == m->decode_mode) return SLM_OK;
+    DeviceScope ds(m->device);
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    for (auto &kv : m->graphs) cudaGraphExecDestroy(kv.second);  // captured with the other kernels
+    m->graphs.clear();
+    m->decode_mode = mode;
     return SLM_OK;
 }
 

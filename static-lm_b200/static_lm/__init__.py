@@ -15,9 +15,9 @@ import ctypes as C
 
 import numpy as np
 
-from ._lib import PHASES, Config, LayerWeights, ModelWeights, SlmError, Slice, lib
+from ._lib import JIT_KERNEL_FN, JIT_OPS, PHASES, Config, LayerWeights, ModelWeights, SlmError, Slice, lib
 
-__all__ = ["Config", "Slice", "SlmError", "Arena", "QMatrix", "Model", "lib",
+__all__ = ["Config", "Slice", "SlmError", "Arena", "QMatrix", "Model", "JitEngine", "lib",
            "gemv_q4_0_arena", "gemm_q4_0_arena", "rope_tables"]
 
 Q4_BLOCK_BYTES = 18
@@ -132,6 +132,41 @@ def rope_tables(max_seq: int, head_dim: int):
     return c, s
 
 
+class JitEngine:
+    """JitEngine (src/jit/engine.rs:28-206) on the device: compile() returns
+    a function with the JitKernelFn calling convention (slm_jit_compile), and
+    exec_unary / exec_binary / exec_with_weights call it on arena slices the
+    way the reference's do (engine.rs:153-206)."""
+
+    def __init__(self, stream: int = 0):
+        self.stream = stream
+
+    def compile(self, op: str, n: int = 0, eps: float = 0.0):
+        fp = C.c_void_p()
+        lib().slm_jit_compile(JIT_OPS[op], n, eps, self.stream or None, C.byref(fp))
+        return JIT_KERNEL_FN(fp.value)
+
+    @staticmethod
+    def _call(kernel, ptrs, out_ptr, n):
+        arr = (C.c_void_p * len(ptrs))(*ptrs)
+        kernel(C.cast(arr, C.POINTER(C.c_void_p)), out_ptr, n)
+
+    def exec_unary(self, kernel, arena: "Arena", src: Slice, dst: Slice):
+        if src.len != dst.len:
+            raise SlmError(4, "src and dst length mismatch")
+        self._call(kernel, [arena.device_ptr(src)], arena.device_ptr(dst), dst.len)
+
+    def exec_binary(self, kernel, arena: "Arena", a: Slice, b: Slice, dst: Slice):
+        if a.len != dst.len or b.len != dst.len:
+            raise SlmError(4, "src and dst length mismatch")
+        self._call(kernel, [arena.device_ptr(a), arena.device_ptr(b)], arena.device_ptr(dst), dst.len)
+
+    def exec_with_weights(self, kernel, arena: "Arena", src: Slice, weights_dev: int, dst: Slice):
+        if src.len != dst.len:
+            raise SlmError(4, "src and dst length mismatch")
+        self._call(kernel, [arena.device_ptr(src), weights_dev], arena.device_ptr(dst), dst.len)
+
+
 def _vp_array(ptrs):
     arr = (C.c_void_p * len(ptrs))(*ptrs)
     return C.cast(arr, C.POINTER(C.c_void_p)), arr
@@ -228,6 +263,11 @@ class Model:
         """Prefill attention on the tcgen05 tensor cores (3xTF32, ~1e-6
         relative to the exact path) or bit-exact on the CUDA cores (default)."""
         lib().slm_model_set_prefill_mode(self.h, 1 if tensor_cores else 0)
+
+    def set_decode_mode(self, flash: bool):
+        """Decode attention as split-K flash-decode (~1e-6 relative to the
+        exact path) or bit-exact sequential chains (default)."""
+        lib().slm_model_set_decode_mode(self.h, 1 if flash else 0)
 
     def generate(self, prompt, n_out: int, eos: int = -1, seq: int = 0):
         p = np.ascontiguousarray(prompt, dtype=np.int32)

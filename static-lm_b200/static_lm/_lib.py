@@ -89,6 +89,7 @@ SIGNATURES = {
     "slm_exec_swiglu": (C.c_int, [C.POINTER(_V), _V, _U64, _V], True),
     "slm_exec_residual_add": (C.c_int, [C.POINTER(_V), _V, _U64, _V], True),
     "slm_exec_l2_norm": (C.c_int, [C.POINTER(_V), _V, _U64, C.c_float, _V], True),
+    "slm_jit_compile": (C.c_int, [C.c_int, _U64, C.c_float, _V, C.POINTER(_V)], True),
     "slm_rope_tables": (C.c_int, [_U32, _U32, _V, _V], True),
     "slm_apply_rope_cached": (C.c_int, [_V, _U64, _V, _V, _U32, _V], True),
     "slm_causal_attention": (C.c_int, [_V, _V, _V, _V, _V, C.POINTER(Config), _U32, _V], True),
@@ -107,6 +108,7 @@ SIGNATURES = {
     "slm_model_attach_shard": (C.c_int, [_V, _V, _U64, C.c_int, C.c_int], True),
     "slm_model_set_comm_timeout": (C.c_int, [_V, _U32], True),
     "slm_model_set_prefill_mode": (C.c_int, [_V, C.c_int], True),
+    "slm_model_set_decode_mode": (C.c_int, [_V, C.c_int], True),
     "slm_shard_units": (_U32, [_U32, _U32, _U32, _U32, _U32P, _U32], False),
     "slm_model_generate": (C.c_int, [_V, _U32, _I32P, _U32, _I32P, _U32, C.c_int32, _U32P], True),
     "slm_model_embed_tokens": (C.c_int, [_V, _U32, _I32P, _U32, C.POINTER(C.c_float)], True),
@@ -121,6 +123,10 @@ SIGNATURES = {
                                            C.POINTER(C.c_float)], True),
     "slm_model_launches_per_decode_step": (_U32, [_V, _U32], False),
 }
+
+# JitKernelFn (src/jit/engine.rs:15) as returned by slm_jit_compile
+JIT_KERNEL_FN = C.CFUNCTYPE(None, C.POINTER(C.c_void_p), C.c_void_p, C.c_size_t)
+JIT_OPS = {"rmsnorm": 0, "softmax": 1, "swiglu": 2, "residual_add": 3, "l2_norm": 4}
 
 PHASES = ["embed", "rmsnorm_q8", "qkv_gemv_rope", "attn_scores", "attn_softmax", "attn_pv",
           "quantize_q8", "wo_gemv_residual", "gate_up_gemv_swiglu", "down_gemv_residual",

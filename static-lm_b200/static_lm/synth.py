@@ -137,6 +137,9 @@ CONFIGS = {
     "cfg2": dict(cfg=Config(288, 768, 6, 6, 256, 1e-5), layers=6, vocab=32000),
     # SmolLM2-135M shape; max_seq_len 2048 + room for the decode steps
     "cfg3": dict(cfg=Config(576, 1536, 9, 3, 2048 + 64, 1e-5), layers=30, vocab=49152),
+    # cfg4: one Llama-3-8B-shaped layer (dim 4096, hidden 14336, 32/8 heads,
+    # head_dim 128) for the attention and GEMV kernel sweeps; small vocab
+    "cfg4": dict(cfg=Config(4096, 14336, 32, 8, 8192 + 64, 1e-5), layers=1, vocab=2048),
     # cfg5: SmolLM2 shape with a 4096-token prompt and 128 decode steps
     "cfg5": dict(cfg=Config(576, 1536, 9, 3, 4096 + 128, 1e-5), layers=30, vocab=49152),
 }

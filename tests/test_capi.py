@@ -79,3 +79,28 @@ def test_product_path_has_no_oracle_dependency():
                 assert "import oracle" not in text and "liboracle" not in text, f
     syms = open(lib().path, "rb").read()
     assert b"orc_" not in syms
+
+
+def test_jit_compile_caches_like_the_engine_without_gpu():
+    """slm_jit_compile hands out JitKernelFn pointers (engine.rs:15, 66-72):
+    the same graph (operator, n, eps, stream) gives the same pointer, another
+    graph another pointer; unknown operators are rejected.  No GPU work."""
+    from static_lm._lib import JIT_OPS
+
+    def comp(op, n=0, eps=0.0, stream=None):
+        fp = C.c_void_p()
+        lib().slm_jit_compile(JIT_OPS[op], n, eps, stream, C.byref(fp))
+        return fp.value
+
+    a = comp("rmsnorm", 576, 1e-5)
+    assert a and comp("rmsnorm", 576, 1e-5) == a
+    assert comp("rmsnorm", 576, 1e-6) != a
+    assert comp("rmsnorm", 288, 1e-5) not in (a, None)
+    s = comp("softmax")
+    assert s not in (a, None) and comp("softmax", 7, 0.5) == s  # constants softmax ignores
+    with pytest.raises(SlmError) as e:
+        comp("rmsnorm", 0, 1e-5)
+    assert e.value.code == 1
+    fp = C.c_void_p()
+    with pytest.raises(SlmError):
+        lib().slm_jit_compile(9, 0, 0.0, None, C.byref(fp))

@@ -136,7 +136,11 @@ def test_two_stream_decode_matches_one_stream(cuda):
         one = S.Model(cfg, w, max_sequences=B, max_rows=B)
     finally:
         del os.environ["SLM_DECODE_ONE_STREAM"]
-    two = S.Model(cfg, w, max_sequences=B, max_rows=B)
+    os.environ["SLM_DECODE_PARTS"] = "2"
+    try:
+        two = S.Model(cfg, w, max_sequences=B, max_rows=B)
+    finally:
+        del os.environ["SLM_DECODE_PARTS"]
     assert two.launches_per_decode_step(B) > one.launches_per_decode_step(B)
     toks = [(s * 37 + 1) % vocab for s in range(B)]
     pos = [0] * B

@@ -9,7 +9,7 @@ import pytest
 import oracle as O
 import static_lm as S
 from static_lm import synth
-from static_lm._lib import Config, SlmError, lib
+from static_lm._lib import JIT_KERNEL_FN, JIT_OPS, Config, SlmError, lib
 
 pytestmark = pytest.mark.gpu
 
@@ -181,6 +181,44 @@ def test_jit_ops_bit_exact(cuda, n):
     assert np.array_equal(exec_op(cuda, "slm_exec_residual_add", [a, b], n), O.residual_add(a, b))
     assert np.array_equal(exec_op(cuda, "slm_exec_l2_norm", [a], n, C.c_float(1e-5)),
                           O.l2_norm(a, 1e-5))
+
+
+def jit_call(cuda, op, inputs, n, graph_n=0, eps=0.0):
+    """Compile `op` to a JitKernelFn pointer and call it exactly as the
+    reference's JitEngine::exec_* do: (host array of input pointers, output
+    pointer, len) (engine.rs:153-206)."""
+    fp = C.c_void_p()
+    lib().slm_jit_compile(JIT_OPS[op], graph_n, eps, None, C.byref(fp))
+    fn = JIT_KERNEL_FN(fp.value)
+    ins = [dev(cuda, a) for a in inputs]
+    out = cuda.full((n + 4,), -999.0, dtype=cuda.float32, device="cuda")
+    arr = (C.c_void_p * len(ins))(*[t.data_ptr() for t in ins])
+    fn(C.cast(arr, C.POINTER(C.c_void_p)), out.data_ptr(), n)
+    h = host(out)
+    assert np.all(h[n:] == -999.0), "wrote past len"
+    return h[:n]
+
+
+@pytest.mark.parametrize("n", [1, 7, 33, 576, 2049])
+def test_jit_kernel_fn_entry_points_bit_exact(cuda, n):
+    a = rand_f32(n, n + 7, 2.0)
+    b = rand_f32(n, n + 8, 2.0)
+    assert np.array_equal(jit_call(cuda, "softmax", [a], n), O.softmax(a))
+    assert np.array_equal(jit_call(cuda, "rmsnorm", [a, b], n, n, 1e-5), O.rmsnorm(a, b, 1e-5))
+    assert np.array_equal(jit_call(cuda, "swiglu", [a, b], n), O.swiglu(a, b))
+    assert np.array_equal(jit_call(cuda, "residual_add", [a, b], n), O.residual_add(a, b))
+    assert np.array_equal(jit_call(cuda, "l2_norm", [a], n, 0, 1e-5), O.l2_norm(a, 1e-5))
+
+
+def test_jit_rmsnorm_uses_the_graph_n(cuda):
+    """FuseGraph::rmsnorm(n, eps) bakes 1/n in (graph.rs:147): run on len != n
+    it scales the sum of squares by 1/n, not 1/len."""
+    n, graph_n = 64, 96
+    a, b = rand_f32(n, 1, 2.0), rand_f32(n, 2, 2.0)
+    got = jit_call(cuda, "rmsnorm", [a, b], n, graph_n, 1e-5)
+    s = O.rmsnorm(np.concatenate([a, np.zeros(graph_n - n, np.float32)]),
+                  np.concatenate([b, np.zeros(graph_n - n, np.float32)]), 1e-5)[:n]
+    assert np.array_equal(got, s)
 
 
 def test_softmax_in_place_and_extremes(cuda):
