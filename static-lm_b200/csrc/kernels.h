@@ -70,6 +70,10 @@ void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows
                     cudaStream_t s);
 void launch_rope_vec(float *vec, size_t len, const float *cos_row, const float *sin_row,
                      int head_dim, cudaStream_t s);
+// BlockQ4_0 rows [nrows][nb][18 B] (device, 2-byte aligned) -> rows
+// [row0, row0+nrows) of the repacked 576-byte row tiles.
+void launch_repack_q4(const void *raw, uint64_t nrows, int nb, uint64_t row0, uint8_t *tiles,
+                      cudaStream_t s);
 // One CTA waiting, with limit_cycles as its bound, on an mbarrier that
 // nothing arrives on: sets *err = 3 when the wait gives up.
 void launch_wait_selftest(long long limit_cycles, int32_t *err, cudaStream_t s);
@@ -134,6 +138,8 @@ void set_gemv_smem_limit(int bytes);
 // (128-byte swizzle), V = head_dim floats x V_BOX_POSITIONS positions.
 constexpr int K_BOX_KEYS = 128;
 constexpr int V_BOX_POSITIONS = 64;
+// keys of one flash-decode work item (one V box)
+constexpr int FD_ITEM_KEYS = V_BOX_POSITIONS;
 
 struct AttnArgs {
     const float *q;          // [rows][dim] (RoPE applied)
@@ -176,22 +182,21 @@ struct AttnArgs {
     // 2 = the same with a thread per dim pair.  Same results.
     int pv_per_head;
     // decode (opt-in split-K flash-decode, kernels_attn_flash.cu): partial
-    // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)] and arrival
-    // counters [rows][num_kv_heads] (zero between launches)
+    // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)]
     float *fd_part;
-    int32_t *fd_cnt;
     int fd_nch;
 };
 // vmap: the V tensor map of encode_v_map, or null for the three-phase path;
 // kmap: the K tensor map of encode_k_map, or null (per-row K copies)
 void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensorMap *kmap,
                       cudaStream_t s);
-// Split-K flash-decode (kernels_attn_flash.cu): one CTA per (128-key chunk,
-// KV head, row), the last CTA of a (row, KV head) combines the chunks; about
-// 1e-6 relative to the exact path.  kmap / vmap as for launch_attn_fused.
+// Split-K flash-decode (kernels_attn_flash.cu): (row, KV head, 64-key chunk)
+// work items walked by a persistent grid, then one combine launch per (row,
+// KV head); about 1e-6 relative to the exact path.
 bool flash_decode_ok(const AttnArgs &a);
 int flash_decode_chunks(int max_seq);
-void launch_flash_decode(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vmap, cudaStream_t s);
+// kmap64: K tensor map with FD_ITEM_KEYS-key boxes (encode_k_map)
+void launch_flash_decode(const AttnArgs &a, const CUtensorMap &kmap64, const CUtensorMap &vmap, cudaStream_t s);
 void set_flash_decode_smem();
 // Tensor-core causal prefill (kernels_attn_tc.cu): one launch per layer over
 // (128 query rows, query head) tiles, then the Q8_0 of the output when asked.
@@ -222,10 +227,11 @@ bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, u
 // then uses the three-phase path).
 bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
                   uint64_t planes, int head_dim);
-// The same planes for K, box = 32 floats x 128 positions with the 128-byte
-// swizzle (head_dim % 32 == 0 only).
+// The same planes for K, box = 32 floats x box_keys positions with the
+// 128-byte swizzle (head_dim % 32 == 0 only): K_BOX_KEYS for the exact
+// scores kernels, FD_ITEM_KEYS for the flash-decode kernel.
 bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
-                  uint64_t planes, int head_dim);
+                  uint64_t planes, int head_dim, int box_keys = K_BOX_KEYS);
 // Opt the attention kernels into `bytes` of dynamic shared memory (current device).
 void set_attention_smem_limit(int bytes);
 

@@ -415,6 +415,20 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
         s_issued = 0;
         mbar_fence_init();
     }
+    if (warp == SCORE_CONS_WARPS && lane == 0) {
+        // ask L2 for every K box this CTA's items will load, all at once, so
+        // that the HBM stream runs at full width while the pipeline below
+        // walks the items (L2 is where the QKV kernel's newest row lands, so
+        // prefetching before the wait reads nothing stale)
+        for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
+            const int k = (int)(it % ntile_max);
+            const long long rg = it / ntile_max;
+            const int g = (int)(rg % a.num_kv_heads), r = (int)(rg / a.num_kv_heads);
+            if (!unit_owned(a, r, g) || k * TILE_KEYS >= row_len(a, r)) continue;
+            const int kz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
+            for (int b = 0; b < nbox; b++) tma_prefetch_3d(&kmap, g * hd + 32 * b, k * TILE_KEYS, kz);
+        }
+    }
     __syncthreads();
     pdl_wait();  // q and the K row at pos come from the QKV kernel
     pdl_release();
@@ -985,7 +999,7 @@ struct PvVec {
 // num_heads; the kv_mul CTAs of a KV head then each stream its V rows, mostly
 // from L2).  NST is the depth of the V ring (<= PV_MAX_STAGES), chosen by the
 // launch from the CTAs each SM holds.
-template <int KVM, int NH, int ND>
+template <int KVM, int NH, int ND, int HDT = 0>
 __global__ void __launch_bounds__(512)
     attn_softmax_pv_kernel(AttnArgs a, int lp, int NST, const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -998,7 +1012,8 @@ __global__ void __launch_bounds__(512)
     const int h0 = blockIdx.x * KVM, r = blockIdx.y;  // first query head of this CTA
     const int g = h0 / (a.num_heads / a.num_kv_heads);  // its KV head
     if (!unit_owned(a, r, g)) return;  // CTA-uniform: another rank's unit
-    const int hd = a.head_dim;
+    // HDT: head_dim fixed at compile time (V rows at immediate offsets), or 0
+    const int hd = HDT ? HDT : a.head_dim;
     const int tid = threadIdx.x;
     float *s_ring = smem;                                   // [NST][tt][hd]
     float *s_sc = s_ring + (size_t)NST * tt * hd;           // [KVM][lp]
@@ -1032,6 +1047,11 @@ __global__ void __launch_bounds__(512)
             tma_load_3d(s_ring + (size_t)k * tt * hd, &vmap, vx, k * tt, vz, &bar_full[k]);
         }
         s_issued = k;
+        // the rest of the KV head's V stream into L2 at once (one CTA of the
+        // kv_mul that share it), so that the ring's loads above mostly wait
+        // for L2, not HBM
+        if (h0 % (a.num_heads / a.num_kv_heads) == 0)
+            for (int kk = k; kk < ntiles; kk++) tma_prefetch_3d(&vmap, vx, kk * tt, vz);
     }
     // V rows were written two kernels back (QKV), the scores by the previous one
     pdl_wait();
@@ -1193,31 +1213,22 @@ __global__ void __launch_bounds__(512)
                 const float *pp = s_sc + hl * lp + k * tt;                               // head stride lp
                 const int nrows = L - k * tt < tt ? L - k * tt : tt;
                 if (nrows == tt) {
-                    // full tile in chunks of PV_CH positions: the shared-memory
-                    // loads of chunk c+1 are in flight while chunk c is added
+                    // full tile in chunks of PV_CH positions, double-buffered in
+                    // two register sets (no copies): the shared-memory loads of
+                    // chunk c+1 are in flight while chunk c is added
                     constexpr int PV_CH = NH > 1 ? 8 : 16, NCH = TT_V / PV_CH;
-                    float4 pc[NH][PV_CH / 4], pn[NH][PV_CH / 4];
-                    PvVec<ND> vc[PV_CH], vn[PV_CH];
+                    float4 pa[NH][PV_CH / 4], pb[NH][PV_CH / 4];
+                    PvVec<ND> va[PV_CH], vb[PV_CH];
+                    auto load = [&](int ch, float4 (&pc)[NH][PV_CH / 4], PvVec<ND> (&vc)[PV_CH]) {
 #pragma unroll
-                    for (int h = 0; h < NH; h++)
+                        for (int h = 0; h < NH; h++)
 #pragma unroll
-                        for (int u = 0; u < PV_CH / 4; u++)
-                            pc[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp)[u];
+                            for (int u = 0; u < PV_CH / 4; u++)
+                                pc[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp + ch * PV_CH)[u];
 #pragma unroll
-                    for (int u = 0; u < PV_CH; u++) vc[u] = PvVec<ND>::load(vt + (size_t)u * hd);
-#pragma unroll
-                    for (int ch = 0; ch < NCH; ch++) {
-                        if (ch + 1 < NCH) {
-#pragma unroll
-                            for (int h = 0; h < NH; h++)
-#pragma unroll
-                                for (int u = 0; u < PV_CH / 4; u++)
-                                    pn[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp +
-                                                                                (ch + 1) * PV_CH)[u];
-#pragma unroll
-                            for (int u = 0; u < PV_CH; u++)
-                                vn[u] = PvVec<ND>::load(vt + (size_t)((ch + 1) * PV_CH + u) * hd);
-                        }
+                        for (int u = 0; u < PV_CH; u++) vc[u] = PvVec<ND>::load(vt + (size_t)(ch * PV_CH + u) * hd);
+                    };
+                    auto add = [&](const float4 (&pc)[NH][PV_CH / 4], const PvVec<ND> (&vc)[PV_CH]) {
 #pragma unroll
                         for (int u = 0; u < PV_CH / 4; u++) {
 #pragma unroll
@@ -1233,14 +1244,14 @@ __global__ void __launch_bounds__(512)
                                         acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vc[4 * u + e].v[c]));
                                 }
                         }
-                        if (ch + 1 < NCH) {
+                    };
+                    load(0, pa, va);
 #pragma unroll
-                            for (int h = 0; h < NH; h++)
-#pragma unroll
-                                for (int u = 0; u < PV_CH / 4; u++) pc[h][u] = pn[h][u];
-#pragma unroll
-                            for (int u = 0; u < PV_CH; u++) vc[u] = vn[u];
-                        }
+                    for (int ch = 0; ch < NCH; ch += 2) {
+                        if (ch + 1 < NCH) load(ch + 1, pb, vb);
+                        add(pa, va);
+                        if (ch + 2 < NCH) load(ch + 2, pa, va);
+                        if (ch + 1 < NCH) add(pb, vb);
                     }
                 } else {
                     for (int tl = 0; tl < nrows; tl++) {
@@ -1345,8 +1356,13 @@ void launch_softmax_pv_per_head(const AttnArgs &args, const CUtensorMap &vmap, c
     const bool q8_after = a.q8_out.qs && a.head_dim % 32 != 0;
     if (q8_after) a.q8_out.qs = nullptr;
     const int cons = (a.head_dim / ND + 31) / 32 * 32;
-    launch_kernel(attn_softmax_pv_kernel<1, 1, ND>, dim3(a.num_heads, a.rows), dim3(cons + 32), f.smem, s,
-                  a.pdl, a, f.lp, f.nst, vmap);
+    const dim3 grid(a.num_heads, a.rows), block(cons + 32);
+    if (a.head_dim == 64)
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 64>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+    else if (a.head_dim == 128)
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 128>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+    else
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
     if (q8_after) launch_quantize_q8x(a.out, a.ldo, a.dim, args.q8_out, a.rows, s);
 }
 
@@ -1393,14 +1409,15 @@ bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
 }
 
 bool encode_k_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
-                  uint64_t planes, int head_dim) {
+                  uint64_t planes, int head_dim, int box_keys) {
     const EncodeTiledFn fn = encode_tiled_fn();
     if (!fn || !base || ((uintptr_t)base & 15) || (kv_dim & 3) || (head_dim & 31) ||
         head_dim > kv_dim || max_seq <= 0 || planes == 0 || planes > 0x7fffffffULL)
         return false;
     const cuuint64_t dims[3] = {(cuuint64_t)kv_dim, (cuuint64_t)max_seq, (cuuint64_t)planes};
     const cuuint64_t strides[2] = {(cuuint64_t)kv_dim * 4, (cuuint64_t)kv_dim * 4 * (cuuint64_t)max_seq};
-    const cuuint32_t box[3] = {32, (cuuint32_t)TILE_KEYS, 1};
+    if (box_keys < 8 || box_keys > 256 || box_keys % 8) return false;
+    const cuuint32_t box[3] = {32, (cuuint32_t)box_keys, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1489,7 +1506,10 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const int per_sm = (int)((200 * 1024) / sk) < 3 ? (int)((200 * 1024) / sk) : 3;
+        // as many CTAs as the SM's 228 KB of shared memory holds (1 KB of it
+        // reserved per CTA), up to 3
+        const int fit = (int)((228 * 1024) / (sk + 1024));
+        const int per_sm = fit < 3 ? fit : 3;
         long long grid = (long long)sms * (per_sm > 0 ? per_sm : 1);
         if (grid > items) grid = items;
         launch_kernel(attn_scores_pipe_kernel, dim3((unsigned)grid), dim3(TILE_KEYS + 32), sk, s, a.pdl,
@@ -1556,6 +1576,10 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<7>(bytes);
     set_softmax_pv_smem<8>(bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

@@ -494,9 +494,18 @@ inline int gemm_nw(int rpt, int nb) {
                                                                                : STAGED_MAX_WARPS / 2;
 }
 
-inline bool gemm_shape(int rpt, int nb, int batch) {
-    return batch >= GEMM_MIN_BATCH &&
-           staged_smem(rpt, gemm_nw(rpt, nb) * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
+// The GEMM shape also serves decode-sized batches (32+) of matrices with
+// many row tiles, such as lm_head, when its CTAs still cover every SM twice:
+// four activation rows per warp cut the weight unpacking per row by four and
+// the CTA count by four against one row per warp.
+constexpr int GEMM_MIN_BATCH_WIDE = 32;
+
+inline bool gemm_shape(int rpt, int nb, int batch, int units) {
+    const bool fits = staged_smem(rpt, gemm_nw(rpt, nb) * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
+    if (!fits) return false;
+    if (batch >= GEMM_MIN_BATCH) return true;
+    const long groups = (batch + gemm_nw(rpt, nb) * GEMM_BT - 1) / (gemm_nw(rpt, nb) * GEMM_BT);
+    return batch >= GEMM_MIN_BATCH_WIDE && (long)units * groups >= 2L * 148;
 }
 
 template <int EPI>
@@ -505,7 +514,7 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
     const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
-    if (!norm && gemm_shape(RPT, a.nb, a.batch)) {
+    if (!norm && gemm_shape(RPT, a.nb, a.batch, units)) {
         launch_staged<GEMM_BT, EPI, false>(a, gemm_nw(RPT, a.nb), total_tiles, units, s);
         return;
     }
@@ -550,8 +559,8 @@ void set_gemv_smem_limit(int bytes) {
 
 bool gemv_fuses_norm(int rows, int nb, int epi, int batch) {
     const int rpt = epi == EPI_SWIGLU_Q8 ? 2 : 1;
-    if (gemm_shape(rpt, nb, batch)) return false;  // the GEMM shape takes normalized Q8X rows
     const int units = units_of(rows, epi);
+    if (gemm_shape(rpt, nb, batch, units)) return false;  // the GEMM shape takes normalized Q8X rows
     return staged_smem(rpt, pick_nw(units, batch), nb, true) <= STAGED_SMEM_MAX;
 }
 

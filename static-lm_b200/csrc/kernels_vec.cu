@@ -153,7 +153,25 @@ __global__ void argmax_kernel(const float *__restrict__ logits, size_t ld, int n
     float best = -FLT_MAX;
     int idx = INT_MAX;
     bool init = false;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    // eight independent loads in flight per thread, then compared in index order
+    constexpr int U = 8;
+    const int step = (int)blockDim.x;
+    int i0 = threadIdx.x;
+    for (; i0 + (U - 1) * step < n; i0 += U * step) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) v[u] = l[i0 + u * step];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (v[u] != v[u]) continue;
+            if (!init || v[u] > best) {
+                best = v[u];
+                idx = i0 + u * step;
+                init = true;
+            }
+        }
+    }
+    for (int i = i0; i < n; i += step) {
         float v = l[i];
         if (v != v) continue;
         if (!init || v > best) {
@@ -422,6 +440,33 @@ void launch_advance(int32_t *tokens, int32_t *pos, const int32_t *next, int rows
                     cudaStream_t s) {
     if (rows <= 0) return;
     advance_kernel<<<cdiv(rows, 128), 128, 0, s>>>(tokens, pos, next, rows);
+}
+
+// BlockQ4_0 rows (18 bytes per block, as GgufFile::tensor_q4_0 returns them,
+// src/memory/loader.rs:496-500) -> the 576-byte row tiles of common.cuh:
+// rows [row0, row0+nrows) of a matrix of nb blocks per row.  One thread per
+// (row, block); a block is 2-byte aligned, so it moves as nine 16-bit words.
+__global__ void repack_q4_kernel(const uint16_t *raw, uint64_t nrows, int nb, uint64_t row0,
+                                 uint8_t *tiles) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nrows * (uint64_t)nb) return;
+    const uint64_t r = row0 + i / (uint64_t)nb;
+    const int j = (int)(i % (uint64_t)nb);
+    const uint16_t *src = raw + i * 9;
+    uint8_t *dst = tiles + tile_offset(r / TILE_ROWS, (size_t)nb, (size_t)j);
+    const int lane = (int)(r % TILE_ROWS);
+    reinterpret_cast<uint16_t *>(dst + 512)[lane] = src[0];
+    uint16_t *nib = reinterpret_cast<uint16_t *>(dst + lane * 16);
+#pragma unroll
+    for (int k = 0; k < 8; k++) nib[k] = src[1 + k];
+}
+
+void launch_repack_q4(const void *raw, uint64_t nrows, int nb, uint64_t row0, uint8_t *tiles,
+                      cudaStream_t s) {
+    const uint64_t n = nrows * (uint64_t)nb;
+    if (!n) return;
+    repack_q4_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint16_t *>(raw), nrows, nb,
+                                                                  row0, tiles);
 }
 
 // Self-test of the bounded mbarrier wait every TMA pipeline uses: thread 0

@@ -182,21 +182,8 @@ SLM_EXPORT int slm_arena_read(slm_arena *a, slm_slice s, float *host, uint64_t n
 
 namespace {
 
-// BlockQ4_0 rows [rows x cols/32] (18 B each) -> 576-byte row tiles.
-void repack_rows(const uint8_t *src, uint64_t rows, uint64_t nb, uint8_t *dst) {
-    uint64_t tiles = (rows + TILE_ROWS - 1) / TILE_ROWS;
-    std::memset(dst, 0, tiles * nb * TILE_BYTES);
-    for (uint64_t r = 0; r < rows; r++) {
-        uint64_t t = r / TILE_ROWS, lane = r % TILE_ROWS;
-        for (uint64_t j = 0; j < nb; j++) {
-            const uint8_t *blk = src + (r * nb + j) * 18;
-            uint8_t *tp = dst + tile_offset(t, nb, j);
-            std::memcpy(tp + 512 + lane * 2, blk, 2);
-            std::memcpy(tp + lane * 16, blk + 2, 16);
-        }
-    }
-}
-
+// 576-byte row tiles -> BlockQ4_0 rows [rows x cols/32] (18 B each), the
+// inverse of the device repack (repack_q4_kernel).
 void unpack_rows(const uint8_t *tiles, uint64_t rows, uint64_t nb, uint8_t *dst) {
     for (uint64_t r = 0; r < rows; r++) {
         uint64_t t = r / TILE_ROWS, lane = r % TILE_ROWS;
@@ -213,6 +200,70 @@ uint64_t tiled_bytes(uint64_t rows, uint64_t cols) {
     return (rows + TILE_ROWS - 1) / TILE_ROWS * (cols / QK) * TILE_BYTES;
 }
 
+// Host -> device path of Q4_0 weights: the caller's blocks (typically the
+// mmap'd GGUF tensor, GgufFile::tensor_q4_0, loader.rs:496-500) are copied in
+// chunks into one of two pinned staging buffers, sent with cudaMemcpyAsync
+// into a device scratch of the same size, and repacked into the row tiles by
+// a kernel; while the GPU copies and repacks one chunk, the host fills the
+// other staging buffer.  Host memory is never repacked or held whole.
+class Q4Uploader {
+  public:
+    static constexpr size_t CHUNK = 8u << 20;  // bytes per staging buffer
+    ~Q4Uploader() { release(); }
+    int begin() {
+        CUDA_TRY(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; i++) {
+            CUDA_TRY(cudaMallocHost(&host_[i], CHUNK));
+            CUDA_TRY(cudaMalloc(&dev_[i], CHUNK));
+            CUDA_TRY(cudaEventCreateWithFlags(&done_[i], cudaEventDisableTiming));
+        }
+        return SLM_OK;
+    }
+    // rows [row0, row0+nrows) of a tiled matrix of nb blocks per row from
+    // nrows*nb host blocks
+    int rows(const void *src, uint64_t nrows, uint64_t nb, uint64_t row0, uint8_t *tiles) {
+        const uint64_t row_bytes = nb * 18;
+        const uint64_t per_chunk = std::max<uint64_t>(1, CHUNK / row_bytes);
+        if (per_chunk * row_bytes > CHUNK) return fail(SLM_ERR_SHAPE, "a Q4_0 row exceeds the staging buffer");
+        for (uint64_t r = 0; r < nrows; r += per_chunk) {
+            const uint64_t n = std::min(per_chunk, nrows - r);
+            const int b = next_++ & 1;
+            CUDA_TRY(cudaEventSynchronize(done_[b]));  // the buffer's previous chunk has been sent
+            std::memcpy(host_[b], static_cast<const uint8_t *>(src) + r * row_bytes, n * row_bytes);
+            CUDA_TRY(cudaMemcpyAsync(dev_[b], host_[b], n * row_bytes, cudaMemcpyHostToDevice, st_));
+            launch_repack_q4(dev_[b], n, (int)nb, row0 + r, tiles, st_);
+            CUDA_TRY(cudaGetLastError());
+            CUDA_TRY(cudaEventRecord(done_[b], st_));
+        }
+        return SLM_OK;
+    }
+    cudaStream_t stream() const { return st_; }
+    int finish() {
+        CUDA_TRY(cudaStreamSynchronize(st_));
+        return SLM_OK;
+    }
+    void release() {
+        if (st_) cudaStreamSynchronize(st_);
+        for (int i = 0; i < 2; i++) {
+            if (host_[i]) cudaFreeHost(host_[i]);
+            if (dev_[i]) cudaFree(dev_[i]);
+            if (done_[i]) cudaEventDestroy(done_[i]);
+            host_[i] = nullptr;
+            dev_[i] = nullptr;
+            done_[i] = nullptr;
+        }
+        if (st_) cudaStreamDestroy(st_);
+        st_ = nullptr;
+    }
+
+  private:
+    cudaStream_t st_ = nullptr;
+    void *host_[2] = {nullptr, nullptr};
+    void *dev_[2] = {nullptr, nullptr};
+    cudaEvent_t done_[2] = {nullptr, nullptr};
+    unsigned next_ = 0;
+};
+
 }  // namespace
 
 struct slm_qmatrix {
@@ -227,16 +278,21 @@ SLM_EXPORT int slm_qmatrix_upload(int device, const void *blocks, uint64_t rows,
     *out = nullptr;
     if (cols == 0 || cols % QK) return fail(SLM_ERR_SHAPE, "cols must be a multiple of 32");
     if (rows == 0) return fail(SLM_ERR_SHAPE, "rows must be positive");
+    if ((uintptr_t)blocks & 1) return fail(SLM_ERR_INVALID_ARG, "Q4_0 blocks must be 2-byte aligned");
     DeviceScope ds(device);
     uint64_t bytes = tiled_bytes(rows, cols);
-    std::vector<uint8_t> host(bytes);
-    repack_rows((const uint8_t *)blocks, rows, cols / QK, host.data());
     uint8_t *d = nullptr;
     CUDA_TRY(cudaMalloc(&d, bytes));
-    cudaError_t e = cudaMemcpy(d, host.data(), bytes, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
+    Q4Uploader up;
+    int rc = up.begin();
+    if (rc == SLM_OK && cudaMemsetAsync(d, 0, bytes, up.stream()) != cudaSuccess)  // rows past the last
+        rc = fail(SLM_ERR_CUDA, "cudaMemsetAsync");
+    if (rc == SLM_OK) rc = up.rows(blocks, rows, cols / QK, 0, d);
+    if (rc == SLM_OK) rc = up.finish();
+    if (rc != SLM_OK) {
+        up.release();
         cudaFree(d);
-        return fail(SLM_ERR_CUDA, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+        return rc;
     }
     *out = new slm_qmatrix{device, d, rows, cols, bytes};
     return SLM_OK;
@@ -674,28 +730,30 @@ SLM_EXPORT int slm_causal_attention_rows(const float *q, const float *k, const f
     const bool have_k = encode_k_map(&kmap, k, a.kv_dim, a.max_seq, 1, a.head_dim);
     const bool have_a = encode_att_map(&amap, att, a.max_seq, a.num_heads, n, a.num_heads / a.num_kv_heads);
     if (mode == SLM_ATTN_FLASH_DECODE) {
-        // every row as a decode row; the chunk partials and the (zeroed)
-        // arrival counters in one stream-ordered allocation
+        // every row as a decode row; the chunk partials in a stream-ordered
+        // allocation
         a.prefill_run = 0;
         a.prefill_tc = 0;
         a.fd_nch = flash_decode_chunks(a.max_seq);
         const size_t pfloats = (size_t)n * a.num_kv_heads * a.fd_nch * (a.num_heads / a.num_kv_heads) *
                                (a.head_dim + 2);
-        const size_t cbytes = sizeof(int32_t) * n * a.num_kv_heads;
-        char *scratch = nullptr;
-        if (!have_v || !have_k ||
-            cudaMallocAsync((void **)&scratch, pfloats * sizeof(float) + cbytes, st) != cudaSuccess) {
+        float *scratch = nullptr;
+        if (!have_v || !have_k || cudaMallocAsync((void **)&scratch, pfloats * sizeof(float), st) != cudaSuccess) {
             cudaFreeAsync(dpos, st);
             cudaStreamSynchronize(st);
             return fail(have_v && have_k ? SLM_ERR_CUDA : SLM_ERR_SHAPE, "flash-decode set-up");
         }
-        a.fd_part = reinterpret_cast<float *>(scratch);
-        int32_t *cnt = reinterpret_cast<int32_t *>(scratch + pfloats * sizeof(float));
-        cudaMemsetAsync(cnt, 0, cbytes, st);
-        a.fd_cnt = cnt;
+        CUtensorMap kmap64;
+        if (!encode_k_map(&kmap64, k, a.kv_dim, a.max_seq, 1, a.head_dim, FD_ITEM_KEYS)) {
+            cudaFreeAsync(scratch, st);
+            cudaFreeAsync(dpos, st);
+            cudaStreamSynchronize(st);
+            return fail(SLM_ERR_SHAPE, "flash-decode needs head_dim 64 or 128");
+        }
+        a.fd_part = scratch;
         int rc = SLM_OK;
         if (flash_decode_ok(a))
-            launch_flash_decode(a, kmap, vmap, st);
+            launch_flash_decode(a, kmap64, vmap, st);
         else
             rc = fail(SLM_ERR_SHAPE, "flash-decode needs head_dim 64 or 128 and kv_mul 1, 2, 3, 4, 6 or 8");
         cudaFreeAsync(scratch, st);
@@ -808,12 +866,13 @@ struct slm_model {
     int pv_per_head = 1;     // softmax + PV per (row, query head): AttnArgs::pv_per_head
     int decode_mode = SLM_DECODE_EXACT;  // slm_model_set_decode_mode
     float *fd_part = nullptr;  // flash-decode partials [R][kvh][fd_nch][kv_mul*(hd+2)]
-    int32_t *fd_cnt = nullptr; // flash-decode arrival counters [R][kvh], zero between launches
     int fd_nch = 0;
     cudaStream_t side[MAX_PARTS - 1] = {};  // streams of parts 1..
     cudaEvent_t ev_fork = nullptr, ev_join[MAX_PARTS - 1] = {};
     CUtensorMap vmap;        // V planes of the KV cache, for the fused attention
     CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
+    CUtensorMap kmap64;      // K planes, FD_ITEM_KEYS-key boxes for the flash-decode kernel
+    bool have_kmap64 = false;
     CUtensorMap amap;        // att scratch, probability tiles of the prefill softmax/PV
     bool have_vmap = false, have_kmap = false, have_amap = false;
     // KV-head-sharded batched prefill (slm_model_attach_shard)
@@ -900,29 +959,26 @@ int comm_wait_stream(slm_model *m) {
     return rc;
 }
 
-std::vector<uint8_t> concat_rows(const std::vector<std::pair<const void *, uint64_t>> &parts,
-                                 uint64_t cols) {
-    uint64_t nb = cols / QK, total = 0;
-    for (auto &p : parts) total += p.second;
-    std::vector<uint8_t> v(total * nb * 18);
-    uint64_t off = 0;
-    for (auto &p : parts) {
-        std::memcpy(v.data() + off, p.first, p.second * nb * 18);
-        off += p.second * nb * 18;
-    }
-    return v;
-}
-
-// Upload a row-concatenation of Q4_0 matrices into wbuf at `*cursor`.
-int upload_qmat(slm_model *m, const std::vector<std::pair<const void *, uint64_t>> &parts,
+// Upload a row-concatenation of Q4_0 matrices into wbuf at `*cursor`
+// through the pinned staging path.
+int upload_qmat(slm_model *m, Q4Uploader &up, const std::vector<std::pair<const void *, uint64_t>> &parts,
                 uint64_t cols, uint64_t *cursor, QMat *out) {
-    std::vector<uint8_t> src = concat_rows(parts, cols);
-    uint64_t rows = src.size() / ((cols / QK) * 18);
-    uint64_t bytes = tiled_bytes(rows, cols);
-    std::vector<uint8_t> tiles(bytes);
-    repack_rows(src.data(), rows, cols / QK, tiles.data());
-    CUDA_TRY(cudaMemcpy(m->wbuf + *cursor, tiles.data(), bytes, cudaMemcpyHostToDevice));
-    out->tiles = m->wbuf + *cursor;
+    const uint64_t nb = cols / QK;
+    uint64_t rows = 0;
+    for (auto &p : parts) {
+        if (!p.first) return fail(SLM_ERR_INVALID_ARG, "a weight tensor is null");
+        if ((uintptr_t)p.first & 1) return fail(SLM_ERR_INVALID_ARG, "Q4_0 blocks must be 2-byte aligned");
+        rows += p.second;
+    }
+    const uint64_t bytes = tiled_bytes(rows, cols);
+    uint8_t *tiles = m->wbuf + *cursor;
+    CUDA_TRY(cudaMemsetAsync(tiles, 0, bytes, up.stream()));  // rows past the last of the tile
+    uint64_t row0 = 0;
+    for (auto &p : parts) {
+        TRY(up.rows(p.first, p.second, nb, row0, tiles));
+        row0 += p.second;
+    }
+    out->tiles = tiles;
     out->rows = (int)rows;
     out->cols = (int)cols;
     *cursor += round_up(bytes, 256);
@@ -1027,7 +1083,6 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     aa.tmax = row0 == 0 ? m->tmax : nullptr;
     aa.pv_per_head = m->pv_per_head;
     aa.fd_part = m->fd_part + r0 * c.num_kv_heads * (size_t)m->fd_nch * (c.num_heads / c.num_kv_heads) * (m->hd + 2);
-    aa.fd_cnt = m->fd_cnt + r0 * c.num_kv_heads;
     aa.fd_nch = m->fd_nch;
     aa.tmax_ld = m->tmax_ld;
 
@@ -1052,7 +1107,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     }
     // decode rows in the opt-in split-K flash-decode mode (the Q8_0 of the
     // output inside the kernel)
-    const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && fused && m->have_kmap &&
+    const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && fused && m->have_kmap64 &&
                        flash_decode_ok(aa);
     const int n_units = kind == STEP_PREFILL_BATCH && seq_rows > 0 ? (n / seq_rows) * (int)c.num_kv_heads : 0;
     const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
@@ -1092,7 +1147,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         if (flash) {
             AttnArgs fa = aa;
             fa.q8_out = qb8;
-            launch_flash_decode(fa, m->kmap, m->vmap, st);
+            launch_flash_decode(fa, m->kmap64, m->vmap, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
         } else if (fused) {
             // scores, then softmax + PV + the Q8_0 of the output
@@ -1226,7 +1281,6 @@ AttnArgs decode_probe(const slm_model *m, int max_len) {
     a.slot_stride = m->slot_stride;
     a.max_len = max_len;
     a.fd_part = m->fd_part;
-    a.fd_cnt = m->fd_cnt;
     a.fd_nch = m->fd_nch;
     return a;
 }
@@ -1236,8 +1290,8 @@ uint32_t decode_launches(const slm_model *m, int n) {
     const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
     uint32_t attn = 4;  // scores, softmax, pv, quantize
     if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
-        if (m->decode_mode == SLM_DECODE_FLASH && m->have_kmap && flash_decode_ok(pa))
-            attn = 1;  // flash-decode with the Q8_0 of the output inside
+        if (m->decode_mode == SLM_DECODE_FLASH && m->have_kmap64 && flash_decode_ok(pa))
+            attn = 2;  // flash-decode chunks, then the combine (with the Q8_0 of the output)
         else if (m->pv_per_head)
             attn = (m->hd % 32 == 0) ? 2 : 3;
         else
@@ -1319,9 +1373,6 @@ int read_device_error(slm_model *m) {
     CUDA_TRY(cudaStreamSynchronize(m->stream));
     if (err) {
         CUDA_TRY(cudaMemsetAsync(m->d_err, 0, 4, m->stream));
-        // a flash-decode CTA that gave up never counted in: start the
-        // arrival counters from zero again
-        CUDA_TRY(cudaMemsetAsync(m->fd_cnt, 0, sizeof(int32_t) * m->R * m->cfg.num_kv_heads, m->stream));
         CUDA_TRY(cudaStreamSynchronize(m->stream));
         return fail(SLM_ERR_DEVICE_INPUT, err == 1   ? "token_id out of vocabulary bounds"
                                           : err == 2 ? "sequence position out of bounds"
@@ -1412,22 +1463,24 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->wbytes = need;
     uint64_t cur = 0;
     m->layers.resize(m->L);
+    Q4Uploader up;
+    int rc = up.begin();
+    if (rc) return cleanup(rc);
     for (int l = 0; l < m->L; l++) {
         const slm_layer_weights &lw = w->layers[l];
         LayerDev &ld = m->layers[l];
-        int rc;
-        if ((rc = upload_qmat(m, {{lw.wq, d}, {lw.wk, kvd}, {lw.wv, kvd}}, d, &cur, &ld.wqkv)) ||
-            (rc = upload_qmat(m, {{lw.wo, d}}, d, &cur, &ld.wo)) ||
-            (rc = upload_qmat(m, {{lw.w_gate, h}, {lw.w_up, h}}, d, &cur, &ld.wgu)) ||
-            (rc = upload_qmat(m, {{lw.w_down, d}}, h, &cur, &ld.wdown)) ||
+        if ((rc = upload_qmat(m, up, {{lw.wq, d}, {lw.wk, kvd}, {lw.wv, kvd}}, d, &cur, &ld.wqkv)) ||
+            (rc = upload_qmat(m, up, {{lw.wo, d}}, d, &cur, &ld.wo)) ||
+            (rc = upload_qmat(m, up, {{lw.w_gate, h}, {lw.w_up, h}}, d, &cur, &ld.wgu)) ||
+            (rc = upload_qmat(m, up, {{lw.w_down, d}}, h, &cur, &ld.wdown)) ||
             (rc = upload_f32(m, lw.rms_att_weight, d, &cur, &ld.rms_att)) ||
             (rc = upload_f32(m, lw.rms_ffn_weight, d, &cur, &ld.rms_ffn)))
             return cleanup(rc);
     }
-    int rc;
-    if ((rc = upload_qmat(m, {{w->token_embd, V}}, d, &cur, &m->embd)) ||
-        (rc = upload_qmat(m, {{w->lm_head ? w->lm_head : w->token_embd, V}}, d, &cur,
+    if ((rc = upload_qmat(m, up, {{w->token_embd, V}}, d, &cur, &m->embd)) ||
+        (rc = upload_qmat(m, up, {{w->lm_head ? w->lm_head : w->token_embd, V}}, d, &cur,
                           &m->lm_head)) ||
+        (rc = up.finish()) ||
         (rc = upload_f32(m, w->output_norm, d, &cur, &m->out_norm)))
         return cleanup(rc);
 
@@ -1456,7 +1509,6 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     const uint64_t kvm = cfg->num_heads / cfg->num_kv_heads;
     const uint64_t fd_floats = R * cfg->num_kv_heads * (uint64_t)m->fd_nch * kvm * (m->hd + 2);
     add_f(fd_floats);                          // flash-decode partials
-    add_f(R * cfg->num_kv_heads);              // flash-decode counters (int32)
     for (int i = 0; i < 5; i++) add_f(R);      // tok, pos, slot, next, err (int32)
     add_f(S * m->slot_stride);                 // KV
     rc = slm_arena_create(device, cap + a16, &m->arena);
@@ -1479,8 +1531,6 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
         m->q8b[i] = p;
     }
     if ((rc = alloc_view(m, fd_floats, &m->fd_part))) return cleanup(rc);
-    if ((rc = alloc_view(m, R * cfg->num_kv_heads, &p))) return cleanup(rc);
-    m->fd_cnt = (int32_t *)p;  // the arena starts zeroed
     int32_t **ints[] = {&m->d_tok, &m->d_pos, &m->d_slot, &m->d_next, &m->d_err};
     for (auto ip : ints) {
         if ((rc = alloc_view(m, R, &p))) return cleanup(rc);
@@ -1513,6 +1563,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     // K plane (slot, layer) at z = slot*2L + 2*layer from the cache start
     m->have_kmap = encode_k_map(&m->kmap, m->kv, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd);
+    m->have_kmap64 = encode_k_map(&m->kmap64, m->kv, m->kvd, (int)cfg->max_seq_len,
+                                (uint64_t)S * 2 * m->L - 1, m->hd, FD_ITEM_KEYS);
     m->have_amap = encode_att_map(&m->amap, m->att, (int)cfg->max_seq_len, (int)cfg->num_heads,
                                   (uint64_t)R, (int)(cfg->num_heads / cfg->num_kv_heads));
     *out = m;
