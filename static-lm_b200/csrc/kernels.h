@@ -36,7 +36,7 @@ inline void launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 // result into Q8X (n must be a multiple of 32 when q8 is requested).
 // y (optional) receives the f32 normalized rows.
 void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float eps,
-                       float *y, size_t ldy, Q8X q8, int rows, cudaStream_t s);
+                       float *y, size_t ldy, Q8X q8, int rows, cudaStream_t s, bool pdl = false);
 void set_rmsnorm_smem_limit(int bytes);
 // Q8_0 quantization of f32 rows into Q8X (blocks.rs:102-123).
 void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s);
@@ -178,8 +178,9 @@ struct AttnArgs {
     // ~1e-6 relative to the exact path instead of bit-exact)
     int prefill_tc;
     // fused path, softmax + PV: 0 = one CTA per (row, KV head) running its
-    // kv_mul heads; 1 = one CTA per (row, query head), a thread per dim;
-    // 2 = the same with a thread per dim pair.  Same results.
+    // kv_mul heads, a thread per (head, dim pair); 1 = one CTA per (row,
+    // query head), a thread per dim; 2 = the same with a thread per dim pair;
+    // 3 = one CTA per (row, KV head), a thread per (head, dim).  Same results.
     int pv_per_head;
     // decode (opt-in split-K flash-decode, kernels_attn_flash.cu): partial
     // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)]

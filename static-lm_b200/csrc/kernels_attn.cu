@@ -215,6 +215,10 @@ __host__ __device__ inline FusedShape fused_shape(int hpc, int hd, int max_len, 
     return f;
 }
 constexpr int PV_MAX_STAGES = 16;
+#ifndef SLM_PV_MIN_STAGES
+#define SLM_PV_MIN_STAGES 2
+#endif
+constexpr int PV_MIN_STAGES = SLM_PV_MIN_STAGES;
 
 // (A) scores: one CTA per (128 keys, KV head, row).  The 128 K rows go
 // global -> shared through the TMA engine, one bulk copy per row (rows padded
@@ -382,7 +386,10 @@ __global__ void __launch_bounds__(TILE_KEYS)
 // kv_mul chains), so copy latency and the per-item set-up overlap compute
 // instead of being paid once per CTA.  FULL/EMPTY mbarriers per stage, all
 // waits bounded; an item with info.r < 0 ends the consumers' loop.
-constexpr int SCORE_STAGES = 2;
+#ifndef SLM_SCORE_STAGES
+#define SLM_SCORE_STAGES 2
+#endif
+constexpr int SCORE_STAGES = SLM_SCORE_STAGES;
 constexpr int SCORE_CONS_WARPS = TILE_KEYS / 32;
 
 struct ScoreItem {
@@ -415,20 +422,6 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
         s_issued = 0;
         mbar_fence_init();
     }
-    if (warp == SCORE_CONS_WARPS && lane == 0) {
-        // ask L2 for every K box this CTA's items will load, all at once, so
-        // that the HBM stream runs at full width while the pipeline below
-        // walks the items (L2 is where the QKV kernel's newest row lands, so
-        // prefetching before the wait reads nothing stale)
-        for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
-            const int k = (int)(it % ntile_max);
-            const long long rg = it / ntile_max;
-            const int g = (int)(rg % a.num_kv_heads), r = (int)(rg / a.num_kv_heads);
-            if (!unit_owned(a, r, g) || k * TILE_KEYS >= row_len(a, r)) continue;
-            const int kz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
-            for (int b = 0; b < nbox; b++) tma_prefetch_3d(&kmap, g * hd + 32 * b, k * TILE_KEYS, kz);
-        }
-    }
     __syncthreads();
     pdl_wait();  // q and the K row at pos come from the QKV kernel
     pdl_release();
@@ -439,10 +432,14 @@ __global__ void __launch_bounds__(TILE_KEYS + 32)
         for (long long it = blockIdx.x; ; it += gridDim.x) {
             ScoreItem item{-1, 0, 0, 0};
             if (it < n_items) {
-                const int k = (int)(it % ntile_max);
-                const long long rg = it / ntile_max;
-                item.g = (int)(rg % a.num_kv_heads);
-                item.r = (int)(rg / a.num_kv_heads);
+                // KV head fastest: CTAs next to each other in the grid read
+                // the kv_heads slices of the same K rows at about the same
+                // time, so each row of the position-major cache is fetched
+                // from HBM whole
+                item.g = (int)(it % a.num_kv_heads);
+                const long long rk = it / a.num_kv_heads;
+                const int k = (int)(rk % ntile_max);
+                item.r = (int)(rk / ntile_max);
                 if (!unit_owned(a, item.r, item.g)) continue;  // another rank's unit
                 const int L = row_len(a, item.r);
                 item.t0 = k * TILE_KEYS;
@@ -1047,11 +1044,6 @@ __global__ void __launch_bounds__(512)
             tma_load_3d(s_ring + (size_t)k * tt * hd, &vmap, vx, k * tt, vz, &bar_full[k]);
         }
         s_issued = k;
-        // the rest of the KV head's V stream into L2 at once (one CTA of the
-        // kv_mul that share it), so that the ring's loads above mostly wait
-        // for L2, not HBM
-        if (h0 % (a.num_heads / a.num_kv_heads) == 0)
-            for (int kk = k; kk < ntiles; kk++) tma_prefetch_3d(&vmap, vx, kk * tt, vz);
     }
     // V rows were written two kernels back (QKV), the scores by the previous one
     pdl_wait();
@@ -1331,19 +1323,69 @@ int sm_count() {
     return sms;
 }
 
-// Depth of the per-head V ring: the shared memory an SM has, shared by the
-// CTAs it holds when the grid is spread evenly, in whole stages (2 to 16).
-// Few CTAs per SM (small batches) get deep rings, so that each CTA keeps
-// enough bytes in flight to stream its V rows at a useful rate on its own.
-FusedShape per_head_shape(const AttnArgs &a) {
-    const long long ctas = (long long)a.rows * a.num_heads;
+#define KVM_GROUP_OK(k) ((k) >= 1 && (k) <= 4)
+
+// Depth of the V ring of a softmax + PV CTA over `hpc` query heads: the
+// shared memory an SM has, shared by the CTAs it holds when the grid is
+// spread evenly, in whole stages (2 to 16).  Few CTAs per SM (small batches)
+// get deep rings, so that each CTA keeps enough bytes in flight to stream its
+// V rows at a useful rate on its own.
+FusedShape pv_shape(const AttnArgs &a, int hpc) {
+    const long long ctas = (long long)a.rows * (a.num_heads / hpc);
     const long long per_sm = (ctas + sm_count() - 1) / sm_count();
     const size_t budget = (size_t)(FUSED_SMEM_MAX / (per_sm < 1 ? 1 : per_sm));
-    const size_t fixed = fused_shape(1, a.head_dim, a.max_len, 0).smem;
+    const size_t fixed = fused_shape(hpc, a.head_dim, a.max_len, 0).smem;
     const size_t stage = (size_t)TT_V * a.head_dim * sizeof(float);
     long long nst = budget > fixed ? (long long)((budget - fixed) / stage) : 0;
-    nst = nst < 2 ? 2 : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
-    return fused_shape(1, a.head_dim, a.max_len, (int)nst);
+    nst = nst < PV_MIN_STAGES ? PV_MIN_STAGES : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
+    return fused_shape(hpc, a.head_dim, a.max_len, (int)nst);
+}
+FusedShape per_head_shape(const AttnArgs &a) { return pv_shape(a, 1); }
+
+// The (row, KV head) form with a thread per (head, dim), head_dim fixed at
+// compile time where it is 64 or 128 and a ring sized like the per-head one:
+// each V tile is staged once for all kv_mul heads.
+// Thread shape (NH heads x ND dims of chains per thread) for head_dim 64/128.
+template <int KVM, int NH, int ND>
+void launch_pv_group_shape(const AttnArgs &a, const FusedShape &f, const CUtensorMap &vmap, cudaStream_t s) {
+    const int cons = (KVM * a.head_dim / (NH * ND) + 31) / 32 * 32;
+    const dim3 grid(a.num_kv_heads, a.rows), block(cons + 32);
+    if (a.head_dim == 64)
+        launch_kernel(attn_softmax_pv_kernel<KVM, NH, ND, 64>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+    else if (a.head_dim == 128)
+        launch_kernel(attn_softmax_pv_kernel<KVM, NH, ND, 128>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+    else
+        launch_kernel(attn_softmax_pv_kernel<KVM, NH, ND>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+}
+
+// mode 3: a thread per (head, dim); 4: a thread per dim running every head
+// of the group; 5: a thread per (head, dim pair)
+template <int KVM>
+void launch_softmax_pv_group(const AttnArgs &args, const CUtensorMap &vmap, cudaStream_t s) {
+    AttnArgs a = args;
+    const FusedShape f = pv_shape(a, KVM);
+    const bool q8_after = a.q8_out.qs && (KVM * a.head_dim) % 32 != 0;
+    if (q8_after) a.q8_out.qs = nullptr;
+    if (a.pv_per_head == 4)
+        launch_pv_group_shape<KVM, KVM, 1>(a, f, vmap, s);
+    else if (a.pv_per_head == 5 && a.head_dim % 2 == 0)
+        launch_pv_group_shape<KVM, 1, 2>(a, f, vmap, s);
+    else
+        launch_pv_group_shape<KVM, 1, 1>(a, f, vmap, s);
+    if (q8_after) launch_quantize_q8x(a.out, a.ldo, a.dim, args.q8_out, a.rows, s);
+}
+
+template <int KVM, int NH, int ND>
+void set_pv_shape_smem(int bytes) {
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, NH, ND, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, NH, ND, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, NH, ND>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+template <int KVM>
+void set_softmax_pv_group_smem(int bytes) {
+    set_pv_shape_smem<KVM, 1, 1>(bytes);
+    set_pv_shape_smem<KVM, KVM, 1>(bytes);
+    set_pv_shape_smem<KVM, 1, 2>(bytes);
 }
 
 // The (row, query head) form: one head per CTA, a thread per dim (ND = 1) or
@@ -1545,6 +1587,15 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
         return;
     }
+    if (a.pv_per_head >= 3 && KVM_GROUP_OK(kv_mul) && kv_mul * a.head_dim <= 480) {
+        switch (kv_mul) {
+            case 1: launch_softmax_pv_group<1>(a, vmap, s); break;
+            case 2: launch_softmax_pv_group<2>(a, vmap, s); break;
+            case 3: launch_softmax_pv_group<3>(a, vmap, s); break;
+            default: launch_softmax_pv_group<4>(a, vmap, s); break;
+        }
+        return;
+    }
     if (a.pv_per_head) {
         if (a.pv_per_head == 2)
             launch_softmax_pv_per_head<2>(a, vmap, s);
@@ -1575,7 +1626,10 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<6>(bytes);
     set_softmax_pv_smem<7>(bytes);
     set_softmax_pv_smem<8>(bytes);
-    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    set_softmax_pv_group_smem<1>(bytes);
+    set_softmax_pv_group_smem<2>(bytes);
+    set_softmax_pv_group_smem<3>(bytes);
+    set_softmax_pv_group_smem<4>(bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

@@ -40,42 +40,56 @@ __device__ __forceinline__ float fmax_nan(float x, float y) {
     return r;
 }
 
-constexpr int FD_KEYS = FD_ITEM_KEYS;  // keys per item (= V box positions)
-constexpr int FD_CONS = 64;            // consumer threads: one per key of the item
+constexpr int FD_KEYS = FD_ITEM_KEYS;  // keys per chunk (= V box positions)
+constexpr int FD_CONS = 64;            // consumer threads: one per key of a chunk
 constexpr int FD_THREADS = FD_CONS + 32;
-constexpr int FD_STAGES = 3;
+#ifndef SLM_FD_STAGES
+#define SLM_FD_STAGES 2
+#endif
+constexpr int FD_STAGES = SLM_FD_STAGES;
 constexpr int FD_BAR_CONS = 1;         // named barrier of the consumer warps
-
-struct FdItem {
-    int r, g, c, nk;  // row, KV head, chunk, keys in the chunk; r < 0: end
-};
 
 template <int KVM, int HD>
 struct FdSmem {
     static constexpr size_t k = (size_t)(HD / 32) * FD_KEYS * 128;  // swizzled K boxes
     static constexpr size_t v = (size_t)FD_KEYS * HD * 4;           // [key][dim]
+    static constexpr size_t stage = (k + v + 1023) / 1024 * 1024;   // K boxes 1024-aligned
     static constexpr size_t q = (size_t)KVM * HD * 4;
-    static constexpr size_t stage = (k + v + q + 1023) / 1024 * 1024;  // K boxes 1024-aligned
     static constexpr size_t e = (size_t)KVM * FD_KEYS * 4;
+    static constexpr size_t o = (size_t)KVM * HD * 4;
     static constexpr size_t red = (size_t)KVM * 4 * 4;
-    static constexpr size_t total = 1024 + FD_STAGES * stage + e + red;
+    static constexpr size_t total = 1024 + FD_STAGES * stage + q + e + o + red;
 };
 
+// One CTA per (split s, KV head g, row r): chunks [c0, c1) of the row's keys,
+// one after another through the ring, with the running maximum m, sum l and
+// output o of every query head kept across chunks (online softmax: when a
+// chunk raises m, l and o are scaled by exp(m_old - m_new)).  With one split
+// the CTA writes the row's output and its Q8_0 directly; otherwise (o, m, l)
+// goes to the partial buffer for the combine kernel.
 template <int KVM, int HD>
 __global__ void __launch_bounds__(FD_THREADS)
-    attn_flash_decode_kernel(AttnArgs a, int nchm, const __grid_constant__ CUtensorMap kmap,
+    attn_flash_decode_kernel(AttnArgs a, int nsplit, const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap) {
     using SM = FdSmem<KVM, HD>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t bar_full[FD_STAGES], bar_empty[FD_STAGES];
-    __shared__ FdItem s_item[FD_STAGES];
     __shared__ int s_abort, s_issued;
     unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    float *s_e = reinterpret_cast<float *>(base + FD_STAGES * SM::stage);  // [KVM][FD_KEYS]
-    float *s_red = s_e + KVM * FD_KEYS;                                    // [KVM][2] max, [KVM][2] sum
+    float *s_q = reinterpret_cast<float *>(base + FD_STAGES * SM::stage);  // [KVM][HD]
+    float *s_e = s_q + KVM * HD;                                            // [KVM][FD_KEYS]
+    float *s_o = s_e + KVM * FD_KEYS;                                       // [KVM*HD]
+    float *s_red = s_o + KVM * HD;                                          // [KVM][2] max, [KVM][2] sum
+    const int sp = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const long long n_items = (long long)a.rows * a.num_kv_heads * nchm;
-    constexpr unsigned stage_tx = (unsigned)(SM::k + SM::v + SM::q);
+    const int L = row_len(a, r);
+    const int nch = (L + FD_KEYS - 1) / FD_KEYS;
+    const int cps = (nch + nsplit - 1) / nsplit;  // chunks per split
+    const int c0 = sp * cps, c1 = c0 + cps < nch ? c0 + cps : nch;
+    if (c0 >= c1) return;  // CTA-uniform: an empty split (the combine skips it)
+    const int nc = c1 - c0;
+    const int z = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
+    constexpr unsigned stage_tx = (unsigned)(SM::k + SM::v);
     constexpr size_t stride = (size_t)KVM * (HD + 2);  // one partial: o[KVM][HD], m[KVM], l[KVM]
 
     if (tid == 0) {
@@ -87,79 +101,61 @@ __global__ void __launch_bounds__(FD_THREADS)
         s_issued = 0;
         mbar_fence_init();
     }
-    if (warp == FD_CONS / 32 && lane == 0) {
-        // every K and V box of this CTA's items into L2 at once (before the
-        // wait: L2 is where the QKV kernel's newest rows land)
-        for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
-            const int c = (int)(it % nchm);
-            const long long u = it / nchm;
-            const int g = (int)(u % a.num_kv_heads), r = (int)(u / a.num_kv_heads);
-            if (c * FD_KEYS >= row_len(a, r)) continue;
-            const int z = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
-            for (int b = 0; b < HD / 32; b++) tma_prefetch_3d(&kmap, g * HD + 32 * b, c * FD_KEYS, z);
-            tma_prefetch_3d(&vmap, g * HD, c * FD_KEYS, z);
-        }
-    }
     __syncthreads();
-    pdl_wait();  // q and each row's newest K/V come from the QKV kernel
-    pdl_release();
-
+    auto issue = [&](int i) {  // chunk c0 + i into stage i % FD_STAGES
+        unsigned char *dst = base + (size_t)(i % FD_STAGES) * SM::stage;
+        const int t0 = (c0 + i) * FD_KEYS;
+        mbar_arrive_expect_tx(&bar_full[i % FD_STAGES], stage_tx);
+#pragma unroll
+        for (int b = 0; b < HD / 32; b++)
+            tma_load_3d(dst + (size_t)b * FD_KEYS * 128, &kmap, g * HD + 32 * b, t0, z, &bar_full[i % FD_STAGES]);
+        tma_load_3d(dst + SM::k, &vmap, g * HD, t0, z, &bar_full[i % FD_STAGES]);
+    };
+    if (warp == FD_CONS / 32 && lane == 0) {
+        // chunks before the row's last were written by earlier steps: their
+        // copies may start before the wait; the last one holds the row at pos
+        int i = 0;
+        for (; i < FD_STAGES && i < nc && c0 + i < nch - 1; i++) issue(i);
+        s_issued = i;
+    }
+    pdl_wait();  // q and the row at pos come from the QKV kernel
     if (warp == FD_CONS / 32) {
         // ---- producer
         if (lane == 0) {
-            int n = 0;
-            for (long long it = blockIdx.x;; it += gridDim.x) {
-                FdItem item{-1, 0, 0, 0};
-                if (it < n_items) {
-                    const int c = (int)(it % nchm);
-                    const long long u = it / nchm;
-                    item.g = (int)(u % a.num_kv_heads);
-                    item.r = (int)(u / a.num_kv_heads);
-                    const int L = row_len(a, item.r);
-                    if (c * FD_KEYS >= L) continue;  // past this row's keys
-                    item.c = c;
-                    item.nk = L - c * FD_KEYS < FD_KEYS ? L - c * FD_KEYS : FD_KEYS;
-                }
-                const int st = n % FD_STAGES;
-                if (n >= FD_STAGES &&
-                    !mbar_wait(&bar_empty[st], (unsigned)((n / FD_STAGES) - 1) & 1u, &s_abort, a.err))
+            int i = s_issued;
+            for (; i < FD_STAGES && i < nc; i++) issue(i);
+            for (; i < nc; i++) {
+                if (!mbar_wait(&bar_empty[i % FD_STAGES], (unsigned)((i / FD_STAGES) - 1) & 1u, &s_abort, a.err))
                     break;
-                s_item[st] = item;
-                if (item.r < 0) {
-                    mbar_arrive(&bar_full[st]);  // end marker, no bytes
-                    s_issued = n + 1;
-                    break;
-                }
-                unsigned char *dst = base + (size_t)st * SM::stage;
-                const int z = (int)((long long)row_slot(a, item.r) * a.z_slot + a.z_layer);
-                const int t0 = item.c * FD_KEYS;
-                mbar_arrive_expect_tx(&bar_full[st], stage_tx);
-#pragma unroll
-                for (int b = 0; b < HD / 32; b++)
-                    tma_load_3d(dst + (size_t)b * FD_KEYS * 128, &kmap, item.g * HD + 32 * b, t0, z, &bar_full[st]);
-                tma_load_3d(dst + SM::k, &vmap, item.g * HD, t0, z, &bar_full[st]);
-                bulk_copy(dst + SM::k + SM::v, a.q + (size_t)item.r * a.ldq + (size_t)item.g * KVM * HD,
-                          (unsigned)SM::q, &bar_full[st]);
-                n++;
-                s_issued = n;
+                issue(i);
             }
+            s_issued = i;
         }
         __syncwarp();
     } else {
         // ---- consumers
-        for (int n = 0;; n++) {
-            const int st = n % FD_STAGES;
-            if (!mbar_wait(&bar_full[st], (unsigned)(n / FD_STAGES) & 1u, &s_abort, a.err)) break;
-            const FdItem item = s_item[st];
-            if (item.r < 0) break;
+        const float *qg = a.q + (size_t)r * a.ldq + (size_t)g * KVM * HD;
+        for (int i = tid; i < KVM * HD; i += FD_CONS) s_q[i] = qg[i];
+        named_bar_or(FD_BAR_CONS, FD_CONS, false);
+        const float4 *q4 = reinterpret_cast<const float4 *>(s_q);
+        constexpr int DPT = HD / FD_CONS;  // output dims per thread: tid, tid + 64, ...
+        float mrun[KVM], lrun[KVM], o[KVM][DPT];
+#pragma unroll
+        for (int h = 0; h < KVM; h++) {
+            mrun[h] = -INFINITY;
+            lrun[h] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < DPT; j++) o[h][j] = 0.0f;
+        }
+        for (int i = 0; i < nc; i++) {
+            const int st = i % FD_STAGES;
+            if (!mbar_wait(&bar_full[st], (unsigned)(i / FD_STAGES) & 1u, &s_abort, a.err)) break;
             const unsigned char *s_k = base + (size_t)st * SM::stage;
             const float *s_v = reinterpret_cast<const float *>(s_k + SM::k);
-            const float4 *q4 = reinterpret_cast<const float4 *>(s_k + SM::k + SM::v);
-            // scores of key tid for the KVM heads
+            const int nk = L - (c0 + i) * FD_KEYS < FD_KEYS ? L - (c0 + i) * FD_KEYS : FD_KEYS;
+            // scores of key tid (four partial sums per head: 4*KVM FMA chains)
             float s[KVM];
             {
-                // four partial sums per head (x, y, z, w lanes of the float4s):
-                // 4*KVM independent FMA chains
                 float acc[KVM][4];
 #pragma unroll
                 for (int h = 0; h < KVM; h++)
@@ -185,39 +181,42 @@ __global__ void __launch_bounds__(FD_THREADS)
 #pragma unroll
                 for (int h = 0; h < KVM; h++) {
                     const float d = (acc[h][0] + acc[h][1]) + (acc[h][2] + acc[h][3]);
-                    s[h] = tid < item.nk ? d * a.scale : -INFINITY;
+                    s[h] = tid < nk ? d * a.scale : -INFINITY;
                 }
             }
-            // chunk maximum and exp sums (NaN scores propagate as in the exact path)
+            // chunk maximum -> new running maximum (NaN scores propagate)
 #pragma unroll
             for (int h = 0; h < KVM; h++) {
                 const float wm = warp_max_nan(s[h]);
                 if (lane == 0) s_red[h * 2 + warp] = wm;
             }
             named_bar_or(FD_BAR_CONS, FD_CONS, false);
-            float m[KVM], l[KVM];
+            float scale[KVM];
 #pragma unroll
             for (int h = 0; h < KVM; h++) {
-                m[h] = fmax_nan(s_red[h * 2], s_red[h * 2 + 1]);
-                const float e = tid < item.nk ? __expf(s[h] - m[h]) : 0.0f;
+                const float mn = fmax_nan(mrun[h], fmax_nan(s_red[h * 2], s_red[h * 2 + 1]));
+                scale[h] = i == 0 ? 0.0f : __expf(mrun[h] - mn);
+                mrun[h] = mn;
+                const float e = tid < nk ? __expf(s[h] - mn) : 0.0f;
                 s_e[h * FD_KEYS + tid] = e;
                 float sum = e;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                for (int o2 = 16; o2 > 0; o2 >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
                 if (lane == 0) s_red[KVM * 2 + h * 2 + warp] = sum;
             }
             named_bar_or(FD_BAR_CONS, FD_CONS, false);
+            // o = o * scale + sum_t e_t v_t (two partial sums: even / odd keys)
+            float o2[KVM][DPT];
 #pragma unroll
-            for (int h = 0; h < KVM; h++) l[h] = s_red[KVM * 2 + h * 2] + s_red[KVM * 2 + h * 2 + 1];
-            // partial PV of dims tid, tid + 64, ...
-            constexpr int DPT = HD / FD_CONS;  // dims per thread
-            // two partial sums per output (even and odd keys)
-            float o[KVM][DPT], o2[KVM][DPT];
+            for (int h = 0; h < KVM; h++) {
+                lrun[h] = __fmaf_rn(lrun[h], scale[h], s_red[KVM * 2 + h * 2] + s_red[KVM * 2 + h * 2 + 1]);
 #pragma unroll
-            for (int h = 0; h < KVM; h++)
-#pragma unroll
-                for (int j = 0; j < DPT; j++) o[h][j] = o2[h][j] = 0.0f;
-            const int nk4 = item.nk & ~3;
+                for (int j = 0; j < DPT; j++) {
+                    o[h][j] *= scale[h];
+                    o2[h][j] = 0.0f;
+                }
+            }
+            const int nk4 = nk & ~3;
             for (int t = 0; t < nk4; t += 4) {
                 float v[4][DPT];
 #pragma unroll
@@ -236,7 +235,7 @@ __global__ void __launch_bounds__(FD_THREADS)
                     }
                 }
             }
-            for (int t = nk4; t < item.nk; t++) {
+            for (int t = nk4; t < nk; t++) {
 #pragma unroll
                 for (int h = 0; h < KVM; h++) {
                     const float e = s_e[h * FD_KEYS + t];
@@ -252,24 +251,46 @@ __global__ void __launch_bounds__(FD_THREADS)
             // the stage is no longer read: hand it back to the producer
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_empty[st]);
-            // write the partial, then count the chunk in
-            const size_t unit = (size_t)item.r * a.num_kv_heads + item.g;
-            float *part = a.fd_part + (unit * a.fd_nch + item.c) * stride;
-#pragma unroll
-            for (int h = 0; h < KVM; h++)
-#pragma unroll
-                for (int j = 0; j < DPT; j++) part[h * HD + tid + FD_CONS * j] = o[h][j];
-            if (tid < KVM) {
-                part[KVM * HD + tid] = m[tid];
-                part[KVM * HD + KVM + tid] = l[tid];
-            }
-            // s_e and s_red are read again only after the next item's first barrier
+            // s_e and s_red are written again only after the next chunk's first barrier
             named_bar_or(FD_BAR_CONS, FD_CONS, false);
         }
+        if (!s_abort) {
+            if (nsplit == 1) {
+                float *orow = a.out + (size_t)r * a.ldo + (size_t)g * KVM * HD;
+#pragma unroll
+                for (int h = 0; h < KVM; h++)
+#pragma unroll
+                    for (int j = 0; j < DPT; j++) {
+                        const int idx = h * HD + tid + FD_CONS * j;
+                        const float res = o[h][j] / lrun[h];
+                        s_o[idx] = res;
+                        orow[idx] = res;
+                    }
+                if (a.q8_out.qs) {
+                    named_bar_or(FD_BAR_CONS, FD_CONS, false);
+                    const int nbr = a.dim / 32;
+                    for (int blk = warp; blk < (KVM * HD) / 32; blk += FD_CONS / 32)
+                        q8x_store_block(s_o[blk * 32 + lane], a.q8_out,
+                                        (size_t)r * nbr + (size_t)(g * KVM * HD) / 32 + blk, lane);
+                }
+            } else {
+                float *part = a.fd_part + (((size_t)r * a.num_kv_heads + g) * a.fd_nch + sp) * stride;
+#pragma unroll
+                for (int h = 0; h < KVM; h++)
+#pragma unroll
+                    for (int j = 0; j < DPT; j++) part[h * HD + tid + FD_CONS * j] = o[h][j];
+                if (tid < KVM) {
+                    part[KVM * HD + tid] = mrun[tid];
+                    part[KVM * HD + KVM + tid] = lrun[tid];
+                }
+            }
+        }
     }
+    pdl_release();
     __syncthreads();
     if (s_abort && tid == 0) {
-        // a wait gave up: let the copies already issued land (bounded)
+        // a wait gave up: let the copies already issued land (bounded); the
+        // error flag is set and this row's output is left as it was
         const int n_iss = s_issued;
         for (int k = n_iss - FD_STAGES < 0 ? 0 : n_iss - FD_STAGES; k < n_iss; k++) {
             const long long t0 = clock64();
@@ -280,47 +301,29 @@ __global__ void __launch_bounds__(FD_THREADS)
     }
 }
 
-// Combine of the chunk partials of one (row, KV head): thread (head h, dim d)
-//   M = max_c m_c[h],  out = sum_c exp(m_c - M) o_c[h][d] / sum_c exp(m_c - M) l_c[h]
+// Combine of the splits of one (row, KV head): thread (head h, dim d)
+//   M = max_s m_s[h],  out = sum_s exp(m_s - M) o_s[h][d] / sum_s exp(m_s - M) l_s[h]
 // then the Q8_0 of the KVM*HD output block (one 32-element block per warp).
 template <int KVM, int HD>
 __global__ void __launch_bounds__(KVM * HD)
-    attn_flash_combine_kernel(AttnArgs a) {
+    attn_flash_combine_kernel(AttnArgs a, int nsplit) {
     __shared__ float s_out[KVM * HD];
     constexpr size_t stride = (size_t)KVM * (HD + 2);
     const int g = blockIdx.x, r = blockIdx.y;
     const int tid = threadIdx.x, h = tid / HD, warp = tid >> 5, lane = tid & 31;
     const int nch = (row_len(a, r) + FD_KEYS - 1) / FD_KEYS;
+    const int cps = (nch + nsplit - 1) / nsplit;
+    const int ns = (nch + cps - 1) / cps;  // splits that hold chunks
     const float *p0 = a.fd_part + ((size_t)r * a.num_kv_heads + g) * a.fd_nch * stride;
     const float *pm = p0 + KVM * HD + h, *pl = pm + KVM;
-    pdl_wait();  // the partials come from the chunk kernel
-    // one pass over the chunks, eight at a time (their 24 loads in flight
-    // together), rescaling the running sums when the maximum moves
-    constexpr int CB = 8;
-    float M = -INFINITY, num = 0.0f, den = 0.0f;
-    for (int c = 0; c < nch; c += CB) {
-        float m[CB], l[CB], o[CB];
-#pragma unroll
-        for (int u = 0; u < CB; u++) {
-            const bool in = c + u < nch;
-            m[u] = in ? pm[(c + u) * stride] : -INFINITY;
-            l[u] = in ? pl[(c + u) * stride] : 0.0f;
-            o[u] = in ? p0[(c + u) * stride + tid] : 0.0f;
-        }
-        float bm = m[0];
-#pragma unroll
-        for (int u = 1; u < CB; u++) bm = fmax_nan(bm, m[u]);
-        const float Mn = fmax_nan(M, bm);
-        const float sc = c == 0 ? 0.0f : __expf(M - Mn);
-        num *= sc;
-        den *= sc;
-#pragma unroll
-        for (int u = 0; u < CB; u++) {
-            const float w = __expf(m[u] - Mn);
-            num = __fmaf_rn(w, o[u], num);
-            den = __fmaf_rn(w, l[u], den);
-        }
-        M = Mn;
+    pdl_wait();  // the partials come from the split kernel
+    float M = -INFINITY;
+    for (int c = 0; c < ns; c++) M = fmax_nan(M, pm[c * stride]);
+    float num = 0.0f, den = 0.0f;
+    for (int c = 0; c < ns; c++) {
+        const float w = __expf(pm[c * stride] - M);
+        num = __fmaf_rn(w, p0[c * stride + tid], num);
+        den = __fmaf_rn(w, pl[c * stride], den);
     }
     const float res = num / den;
     pdl_release();
@@ -346,15 +349,21 @@ int sm_count_flash() {
 template <int KVM, int HD>
 void launch_fd(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vmap, cudaStream_t s) {
     using SM = FdSmem<KVM, HD>;
+    // splits per (row, KV head): as many as the resident CTA slots allow
+    // (one CTA per (row, KV head) when those alone fill the GPU)
     const int nchm = (a.max_len + FD_KEYS - 1) / FD_KEYS;
-    const long long items = (long long)a.rows * a.num_kv_heads * nchm;
-    const int per_sm = (int)((220 * 1024) / SM::total) > 0 ? (int)((220 * 1024) / SM::total) : 1;
-    long long grid = (long long)sm_count_flash() * per_sm;
-    if (grid > items) grid = items;
-    launch_kernel(attn_flash_decode_kernel<KVM, HD>, dim3((unsigned)grid), dim3(FD_THREADS), SM::total, s, a.pdl,
-                  a, nchm, kmap, vmap);
-    launch_kernel(attn_flash_combine_kernel<KVM, HD>, dim3((unsigned)a.num_kv_heads, (unsigned)a.rows),
-                  dim3(KVM * HD), 0, s, a.pdl, a);
+    const long long units = (long long)a.rows * a.num_kv_heads;
+    const int fit = (int)((228 * 1024) / (SM::total + 1024));
+    const long long slots = (long long)sm_count_flash() * (fit > 0 ? fit : 1);
+    long long ns = slots / units;
+    ns = ns < 1 ? 1 : ns > nchm ? nchm : ns;
+    if (ns > a.fd_nch) ns = a.fd_nch;
+    const dim3 grid((unsigned)ns, (unsigned)a.num_kv_heads, (unsigned)a.rows);
+    launch_kernel(attn_flash_decode_kernel<KVM, HD>, grid, dim3(FD_THREADS), SM::total, s, a.pdl, a, (int)ns,
+                  kmap, vmap);
+    if (ns > 1)
+        launch_kernel(attn_flash_combine_kernel<KVM, HD>, dim3((unsigned)a.num_kv_heads, (unsigned)a.rows),
+                      dim3(KVM * HD), 0, s, a.pdl, a, (int)ns);
 }
 
 template <int HD>

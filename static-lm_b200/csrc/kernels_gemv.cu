@@ -22,6 +22,8 @@
 // the activation bytes, seeded with c_k = 0x4B400000 - 8*sum(a): the result
 // is the bit pattern of 12582912 + isum_k, so isum_k as f32 costs one exact
 // subtraction instead of an int->float conversion.
+#include <cstdlib>
+
 #include "async.cuh"
 #include "kernels.h"
 
@@ -494,6 +496,16 @@ inline int gemm_nw(int rpt, int nb) {
                                                                                : STAGED_MAX_WARPS / 2;
 }
 
+// SLM_DECODE_GEMM=1: decode batches of 16+ rows take the GEMM shape whatever
+// the CTA count (the RMSNorm of QKV and gate/up then runs as its own launch)
+inline bool decode_gemm_forced() {
+    static const bool on = [] {
+        const char *e = getenv("SLM_DECODE_GEMM");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 // The GEMM shape also serves decode-sized batches (32+) of matrices with
 // many row tiles, such as lm_head, when its CTAs still cover every SM twice:
 // four activation rows per warp cut the weight unpacking per row by four and
@@ -504,6 +516,7 @@ inline bool gemm_shape(int rpt, int nb, int batch, int units) {
     const bool fits = staged_smem(rpt, gemm_nw(rpt, nb) * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
     if (!fits) return false;
     if (batch >= GEMM_MIN_BATCH) return true;
+    if (decode_gemm_forced() && batch >= 16) return true;
     const long groups = (batch + gemm_nw(rpt, nb) * GEMM_BT - 1) / (gemm_nw(rpt, nb) * GEMM_BT);
     return batch >= GEMM_MIN_BATCH_WIDE && (long)units * groups >= 2L * 148;
 }
@@ -515,7 +528,9 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
     if (!norm && gemm_shape(RPT, a.nb, a.batch, units)) {
-        launch_staged<GEMM_BT, EPI, false>(a, gemm_nw(RPT, a.nb), total_tiles, units, s);
+        // decode batches: four warps per CTA, for twice the CTAs
+        const int nw = a.batch < GEMM_MIN_BATCH ? STAGED_MAX_WARPS / 2 : gemm_nw(RPT, a.nb);
+        launch_staged<GEMM_BT, EPI, false>(a, nw, total_tiles, units, s);
         return;
     }
     const int nw = pick_nw(units, a.batch);

@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_q8_kernel(
     const int r = blockIdx.x;
     if (r >= rows) return;
     const float *xr = x + (size_t)r * ldx;
+    pdl_wait();  // x is the previous kernel's output (no-op without programmatic launch)
     if ((n & 3) == 0 && (((uintptr_t)xr | (uintptr_t)w) & 15) == 0) {
         for (int i = tid; i < n / 4; i += NORM_THREADS) {
             reinterpret_cast<float4 *>(s_x)[i] = __ldg(reinterpret_cast<const float4 *>(xr) + i);
@@ -357,12 +358,12 @@ void set_rmsnorm_smem_limit(int bytes) {
 }
 
 void launch_rmsnorm_q8(const float *x, size_t ldx, const float *w, int n, float eps, float *y,
-                       size_t ldy, Q8X q8, int rows, cudaStream_t s) {
+                       size_t ldy, Q8X q8, int rows, cudaStream_t s, bool pdl) {
     if (rows <= 0) return;
     float inv_n = 1.0f / (float)n;
     size_t smem = sizeof(float) * (2 * (size_t)((n + 3) & ~3));
-    rmsnorm_q8_kernel<<<rows, NORM_THREADS, smem, s>>>(x, ldx, w, n, eps, inv_n, y, ldy, q8, rows,
-                                                       q8.qs != nullptr);
+    launch_kernel(rmsnorm_q8_kernel, dim3(rows), dim3(NORM_THREADS), smem, s, pdl, x, ldx, w, n, eps, inv_n, y,
+                  ldy, q8, rows, (int)(q8.qs != nullptr));
 }
 
 void launch_quantize_q8x(const float *x, size_t ldx, int n, Q8X q8, int rows, cudaStream_t s) {

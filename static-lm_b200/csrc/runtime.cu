@@ -642,7 +642,7 @@ int check_config(const slm_config *c) {
 // every form gives the same results.
 int env_pv_per_head() {
     const char *env = getenv("SLM_PV_PER_HEAD");
-    return env && env[0] >= '0' && env[0] <= '2' ? env[0] - '0' : 1;
+    return env && env[0] >= '0' && env[0] <= '5' ? env[0] - '0' : 1;
 }
 
 AttnArgs attn_args_for(const slm_config *c) {
@@ -1023,12 +1023,16 @@ inline void mark(Profiler *p, int ph) {
 // themselves (staged weight tiles fit in shared memory); otherwise a separate
 // RMSNorm + Q8 launch precedes them.  Activation rows are 16-byte aligned in
 // the arena (dim is a multiple of 32), as the prologue's cp.async requires.
+// From NORM_FUSE_MAX_ROWS rows up the prologue, which every weight-tile CTA
+// repeats for its rows, costs more than one RMSNorm + Q8 launch over the rows
+// (measured at 64 rows: 2.82 against 2.90 ms per config-3 decode step).
+constexpr int NORM_FUSE_MAX_ROWS = 31;
 bool qkv_norm_fused(const slm_model *m, int n) {
-    return m->fuse_norm && gemv_fuses_norm((int)m->layers[0].wqkv.rows, (int)(m->cfg.dim / QK),
-                                           EPI_QKV, n);
+    return m->fuse_norm && n <= NORM_FUSE_MAX_ROWS &&
+           gemv_fuses_norm((int)m->layers[0].wqkv.rows, (int)(m->cfg.dim / QK), EPI_QKV, n);
 }
 bool gate_up_norm_fused(const slm_model *m, int n) {
-    return m->fuse_norm &&
+    return m->fuse_norm && n <= NORM_FUSE_MAX_ROWS &&
            gemv_fuses_norm(2 * (int)m->cfg.hidden_dim, (int)(m->cfg.dim / QK), EPI_SWIGLU_Q8, n);
 }
 
@@ -1125,7 +1129,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             g.eps = c.rms_eps;
             g.inv_n = inv_d;
         } else {
-            launch_rmsnorm_q8(x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st);
+            launch_rmsnorm_q8(x, d, ld.rms_att, d, c.rms_eps, nullptr, 0, qa8, n, st, m->use_pdl);
             mark(prof, SLM_PHASE_RMSNORM);
         }
         // Wq/Wk/Wv + RoPE + KV append (transformer.rs:413-428)
@@ -1210,7 +1214,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             g.eps = c.rms_eps;
             g.inv_n = inv_d;
         } else {
-            launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st);
+            launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st, m->use_pdl);
             mark(prof, SLM_PHASE_RMSNORM);
         }
         g.w = ld.wgu.tiles;
@@ -1292,6 +1296,8 @@ uint32_t decode_launches(const slm_model *m, int n) {
     if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
         if (m->decode_mode == SLM_DECODE_FLASH && m->have_kmap64 && flash_decode_ok(pa))
             attn = 2;  // flash-decode chunks, then the combine (with the Q8_0 of the output)
+        else if (m->pv_per_head >= 3 && kv_mul <= 4 && kv_mul * m->hd <= 480)
+            attn = ((kv_mul * m->hd) % 32 == 0) ? 2 : 3;
         else if (m->pv_per_head)
             attn = (m->hd % 32 == 0) ? 2 : 3;
         else
