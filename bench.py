@@ -461,11 +461,12 @@ def run_ours(args):
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
         threads = O.lib.orc_default_pool_threads()
-        sample_seqs = [0, 1]
+        # sequences one after another, each decoding up to the W+K steps the
+        # GPU made, until about cpu_seconds of CPU work
+        sample_seqs = [0, 1, 2, 3]
         kv_of = [gather_kv(model, s, layers, kvd) for s in sample_seqs]
         toks0 = first_tokens([seqs_global[s] for s in sample_seqs], vocab)
-        done, secs, outs = cpu_decode_sample(cfg, w, kv_of, toks0, min(W + K, 6),
-                                             args.cpu_seconds, threads)
+        done, secs, outs = cpu_decode_sample(cfg, w, kv_of, toks0, W + K, args.cpu_seconds, threads)
         cpu = {"value": done / secs, "unit": "tok/s", "cores": threads,
                "host_logical_cores": os.cpu_count(), "kind": "port",
                "sample": f"{done} decode tokens of {len(outs)} sequence(s) at context {CTX}+ "

@@ -140,6 +140,16 @@ int slm_gemm_q4_0(const slm_qmatrix *w, const void *inputs_q8_dev, float *output
                   uint64_t batch, uint64_t rows, uint64_t cols, void *scratch_dev,
                   uint64_t scratch_bytes, void *stream);
 uint64_t slm_gemm_q4_0_scratch_bytes(uint64_t batch, uint64_t cols);
+/* No reference counterpart (opt-in arithmetic).  slm_gemm_q4_0 with the int8
+ * products on the tcgen05 tensor cores (kind::i8) for batch >= 128: per
+ * 32-element block the exact int32 sum of (w - 8) * a, then
+ * out += (dw * da) * isum in f32 block by block, where the reference adds eight
+ * four-element lane sums per block in its AVX2 order.  Results agree with
+ * slm_gemm_q4_0 to f32 rounding (~1e-7 relative), not bit for bit; batches
+ * below 128 run the exact kernels.  Same arguments as slm_gemm_q4_0. */
+int slm_gemm_q4_0_tensor_cores(const slm_qmatrix *w, const void *inputs_q8_dev, float *output_dev,
+                               uint64_t batch, uint64_t rows, uint64_t cols, void *scratch_dev,
+                               uint64_t scratch_bytes, void *stream);
 /* No counterpart in the reference.  The same product as slm_gemm_q4_0_arena
  * (output[b*rows + r] = dot(W[r], q8(inputs[b]))) for callers that must not
  * allocate device memory on this path: a host running under a device-memory
@@ -296,9 +306,12 @@ int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
  * SLM_PREFILL_EXACT (default) reproduces causal_multi_head_attention_jit
  * (transformer.rs:273-321) bit for bit on the CUDA cores;
  * SLM_PREFILL_TENSOR_CORES runs QK^T and PV on the tcgen05 tensor cores with
- * a 3xTF32 split (about 1e-6 relative to the exact path, not bit-exact), for
- * callers that accept the tolerance.  Decode is always exact.  No reference
- * counterpart (the reference has one CPU path). */
+ * a 3xTF32 split (about 1e-6 relative to the exact path, not bit-exact) and
+ * the int8 products of the Wq/Wk/Wv, Wo, gate/up and down projections on
+ * tcgen05 kind::i8 (as slm_gemm_q4_0_tensor_cores), for callers that accept
+ * the tolerance.  Decode attention has its own mode
+ * (slm_model_set_decode_mode).  No reference counterpart (the reference has
+ * one CPU path). */
 int slm_model_set_prefill_mode(slm_model *m, int mode);
 /* Attention arithmetic of decode steps (decode_batch, forward_token,
  * generate, decode_steps_device, embed excluded): SLM_DECODE_EXACT (default,

@@ -125,6 +125,10 @@ struct GemvArgs {
     float eps, inv_n;
     int32_t *err;            // set to 3 when a bounded copy wait gave up (may be null)
     bool pdl;                // launch with programmatic dependent launch (staged path)
+    // opt-in: the int8 products on the tcgen05 tensor cores (kind::i8) for
+    // batches of 128+ rows without the fused RMSNorm prologue; ~1e-7
+    // relative to the exact result instead of bit for bit
+    bool tc;
 };
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
 // Whether launch_gemv stages whole weight tiles for this shape (and can then
@@ -196,6 +200,8 @@ void launch_attention(const AttnArgs &a, const CUtensorMap *vmap, const CUtensor
 // KV head); about 1e-6 relative to the exact path.
 bool flash_decode_ok(const AttnArgs &a);
 int flash_decode_chunks(int max_seq);
+// kernel launches of one flash-decode attention (1, or 2 with the combine)
+int flash_decode_launches(const AttnArgs &a);
 // kmap64: K tensor map with FD_ITEM_KEYS-key boxes (encode_k_map)
 void launch_flash_decode(const AttnArgs &a, const CUtensorMap &kmap64, const CUtensorMap &vmap, cudaStream_t s);
 void set_flash_decode_smem();

@@ -1489,7 +1489,13 @@ bool attention_fused_ok(const AttnArgs &a) {
     if (!a.att) return false;  // the scores go through att
     if ((a.slot_stride | a.layer_off) & 3) return false;
     const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
-    return fused_shape(kv_mul, a.head_dim, a.max_len).smem <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
+    // the softmax + PV form that will run: per query head (modes 1, 2) with
+    // its smallest ring, or the (row, KV head) forms
+    const size_t spv = (a.pv_per_head == 1 || a.pv_per_head == 2)
+                           ? fused_shape(1, a.head_dim, a.max_len, PV_MIN_STAGES).smem
+                       : a.pv_per_head >= 3 ? fused_shape(kv_mul, a.head_dim, a.max_len, PV_MIN_STAGES).smem
+                                            : fused_shape(kv_mul, a.head_dim, a.max_len).smem;
+    return spv <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
 }
 
 void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,

@@ -346,18 +346,25 @@ int sm_count_flash() {
     return sms;
 }
 
+// Splits per (row, KV head): as many as the resident CTA slots allow (one CTA
+// per (row, KV head) when those alone fill the GPU).
 template <int KVM, int HD>
-void launch_fd(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vmap, cudaStream_t s) {
+int fd_splits(const AttnArgs &a) {
     using SM = FdSmem<KVM, HD>;
-    // splits per (row, KV head): as many as the resident CTA slots allow
-    // (one CTA per (row, KV head) when those alone fill the GPU)
     const int nchm = (a.max_len + FD_KEYS - 1) / FD_KEYS;
     const long long units = (long long)a.rows * a.num_kv_heads;
     const int fit = (int)((228 * 1024) / (SM::total + 1024));
     const long long slots = (long long)sm_count_flash() * (fit > 0 ? fit : 1);
-    long long ns = slots / units;
+    long long ns = units > 0 ? slots / units : 1;
     ns = ns < 1 ? 1 : ns > nchm ? nchm : ns;
     if (ns > a.fd_nch) ns = a.fd_nch;
+    return (int)ns;
+}
+
+template <int KVM, int HD>
+void launch_fd(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vmap, cudaStream_t s) {
+    using SM = FdSmem<KVM, HD>;
+    const int ns = fd_splits<KVM, HD>(a);
     const dim3 grid((unsigned)ns, (unsigned)a.num_kv_heads, (unsigned)a.rows);
     launch_kernel(attn_flash_decode_kernel<KVM, HD>, grid, dim3(FD_THREADS), SM::total, s, a.pdl, a, (int)ns,
                   kmap, vmap);
@@ -397,6 +404,23 @@ void set_fd_smem_hd() {
 }  // namespace
 
 int flash_decode_chunks(int max_seq) { return (max_seq + FD_KEYS - 1) / FD_KEYS; }
+
+template <int HD>
+int fd_splits_hd(const AttnArgs &a) {
+    switch (a.num_heads / a.num_kv_heads) {
+        case 1: return fd_splits<1, HD>(a);
+        case 2: return fd_splits<2, HD>(a);
+        case 3: return fd_splits<3, HD>(a);
+        case 4: return fd_splits<4, HD>(a);
+        case 6: return fd_splits<6, HD>(a);
+        default: return fd_splits<8, HD>(a);
+    }
+}
+
+int flash_decode_launches(const AttnArgs &a) {
+    const int ns = a.head_dim == 64 ? fd_splits_hd<64>(a) : fd_splits_hd<128>(a);
+    return ns > 1 ? 2 : 1;  // the split kernel, and the combine when there are splits
+}
 
 bool flash_decode_ok(const AttnArgs &a) {
     const int kvm = a.num_heads / a.num_kv_heads;

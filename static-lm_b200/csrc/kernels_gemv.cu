@@ -26,6 +26,7 @@
 
 #include "async.cuh"
 #include "kernels.h"
+#include "tc.cuh"
 
 namespace slm {
 
@@ -442,6 +443,242 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS, BT > 1 ? 2 : 1)
     gemv_epilogue<RPT, BT, EPI>(a, acc, tile, total_tiles, b0, lane);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM (opt-in, prefill-sized batches; not bit-exact).  The int8
+// part of the product runs on tcgen05 kind::i8: per 32-element block j the
+// MMA gives isum[r][b] = sum_e (w_e - 8) * a_e exactly (s32 in TMEM); the CUDA
+// cores then form out[b][r] = sum_j (dw_j * da_j) * isum_j in f32, block by
+// block.  The reference accumulates eight 4-element lane sums per block in its
+// AVX2 order instead, so results differ by f32 rounding (~1e-7 relative).
+//
+// CTA tile: 128 weight rows (four 32-row tiles; for SwiGLU the gate tiles and
+// the matching up tiles, two MMAs) x N activation rows.  Operands go to shared
+// memory in groups of TG_KB blocks (128 bytes of K per row = one 128-byte
+// swizzle atom): the activations' int8 bytes by cp.async from Q8X, the
+// weights expanded from nibbles to int8 (w - 8) by the threads; two stages.
+// One thread issues the group's TG_KB*RPT MMAs (each block into its own TMEM
+// columns, not accumulated) with a commit per block; eight warps drain them:
+// warp w reads TMEM lanes 32*(w%4).. (weight rows) and half w/4 of the N
+// columns.  The f32 results end in the GEMV epilogues (lane = weight row).
+constexpr int TG_M = 128;
+constexpr int TG_KB = 4;
+constexpr int TG_THREADS = 256;
+
+template <int RPT>
+struct TgShape {
+    static constexpr int N = RPT == 1 ? 64 : 32;  // activation rows per CTA (MMA N)
+    static constexpr int CPT = N / 2;             // columns per thread
+    static constexpr size_t a = (size_t)RPT * TG_M * 128;
+    static constexpr size_t b = (size_t)N * 128;
+    static constexpr size_t dw = (size_t)RPT * TG_M * TG_KB * 4;
+    static constexpr size_t da = (size_t)TG_KB * N * 4;
+    static constexpr size_t stage = (a + b + dw + da + 1023) / 1024 * 1024;
+    // at least 80 KB, so that two CTAs share an SM: two x 256 TMEM columns
+    static constexpr size_t smem = 1024 + 2 * stage > 80 * 1024 ? 1024 + 2 * stage : 80 * 1024;
+    static constexpr unsigned tcols = (unsigned)(TG_KB * RPT * N);  // 256
+};
+
+// eight signed 4-bit weights (w - 8) per 32-bit word from unsigned nibbles:
+// v ^ 8 is w - 8 as a 4-bit two's complement value, widened to 8 bits
+__device__ __forceinline__ unsigned nib_to_s8(unsigned v) {
+    const unsigned t = v ^ 0x08080808u;
+    return t | ((t & 0x08080808u) * 0x1Eu);
+}
+
+template <int RPT, int EPI>
+__global__ void __launch_bounds__(TG_THREADS) gemm_tc_kernel(GemvArgs a, int total_tiles) {
+    using SH = TgShape<RPT>;
+    constexpr int N = SH::N, CPT = SH::CPT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar_mma[TG_KB];
+    __shared__ unsigned s_tmem;
+    __shared__ int s_abort;
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quad = warp & 3, hf = warp >> 2;
+    const int mt = blockIdx.x, n0 = blockIdx.y * N;
+    const int nb = a.nb, ng = (nb + TG_KB - 1) / TG_KB;
+    const int mtiles = RPT == 2 ? total_tiles / 2 : total_tiles;  // row tiles of one matrix
+    auto tile_of = [&](int t, int q) { return 4 * mt + q + (t ? total_tiles / 2 : 0); };
+    auto sA = [&](int s, int t) { return base + (size_t)s * SH::stage + (size_t)t * TG_M * 128; };
+    auto sB = [&](int s) { return base + (size_t)s * SH::stage + SH::a; };
+    auto sDW = [&](int s) { return reinterpret_cast<float *>(base + (size_t)s * SH::stage + SH::a + SH::b); };
+    auto sDA = [&](int s) {
+        return reinterpret_cast<float *>(base + (size_t)s * SH::stage + SH::a + SH::b + SH::dw);
+    };
+
+    if (tid == 0) {
+        for (int k = 0; k < TG_KB; k++) mbar_init(&bar_mma[k], 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) tc_alloc(&s_tmem, SH::tcols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const unsigned tbase = s_tmem;
+
+    // ---- staging of group g into stage s: activations by cp.async, weights
+    // loaded into registers first (their latency overlaps the drain) and
+    // expanded into shared memory after it
+    constexpr int AI = RPT * TG_M * TG_KB / TG_THREADS;  // (matrix, row, block) items per thread
+    uint4 wq[AI];
+    float wd[AI];
+    auto stage_b = [&](int g, int s) {
+        const int j0 = g * TG_KB, nbg = nb - j0 < TG_KB ? nb - j0 : TG_KB;
+        unsigned char *dst0 = sB(s);
+        for (int i = tid; i < N * 8; i += TG_THREADS) {
+            const int b = i >> 3, c = i & 7;
+            unsigned char *dst = dst0 + b * 128 + ((c ^ (b & 7)) << 4);
+            if ((c >> 1) < nbg && n0 + b < a.batch)
+                cp_async16(dst, a.x.qs + ((size_t)(n0 + b) * nb + j0) * 32 + c * 16);
+            else
+                *reinterpret_cast<int4 *>(dst) = make_int4(0, 0, 0, 0);
+        }
+        cp_async_commit();
+        float *da = sDA(s);
+        for (int i = tid; i < TG_KB * N; i += TG_THREADS) {
+            const int k = i / N, b = i - k * N;
+            da[i] = (k < nbg && n0 + b < a.batch) ? a.x.d[(size_t)(n0 + b) * nb + j0 + k] : 0.0f;
+        }
+    };
+    auto load_a = [&](int g) {
+        const int j0 = g * TG_KB, nbg = nb - j0 < TG_KB ? nb - j0 : TG_KB;
+#pragma unroll
+        for (int u = 0; u < AI; u++) {
+            const int i = tid + u * TG_THREADS;
+            const int t = i / (TG_M * TG_KB), r = (i / TG_KB) % TG_M, k = i % TG_KB;
+            const int T = tile_of(t, r >> 5);
+            const bool ok = k < nbg && (T - (t ? total_tiles / 2 : 0)) < mtiles;
+            if (ok) {
+                const uint8_t *src = a.w + tile_offset((size_t)T, (size_t)nb, (size_t)(j0 + k));
+                wq[u] = *reinterpret_cast<const uint4 *>(src + (r & 31) * 16);
+                wd[u] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(src + 512 + (r & 31) * 2)));
+            } else {
+                wq[u] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // w - 8 = 0
+                wd[u] = 0.0f;
+            }
+        }
+    };
+    auto store_a = [&](int s) {
+#pragma unroll
+        for (int u = 0; u < AI; u++) {
+            const int i = tid + u * TG_THREADS;
+            const int t = i / (TG_M * TG_KB), r = (i / TG_KB) % TG_M, k = i % TG_KB;
+            const uint4 q = wq[u];
+            const uint4 lo = make_uint4(nib_to_s8(q.x & 0x0F0F0F0Fu), nib_to_s8(q.y & 0x0F0F0F0Fu),
+                                        nib_to_s8(q.z & 0x0F0F0F0Fu), nib_to_s8(q.w & 0x0F0F0F0Fu));
+            const uint4 hi = make_uint4(nib_to_s8((q.x >> 4) & 0x0F0F0F0Fu), nib_to_s8((q.y >> 4) & 0x0F0F0F0Fu),
+                                        nib_to_s8((q.z >> 4) & 0x0F0F0F0Fu), nib_to_s8((q.w >> 4) & 0x0F0F0F0Fu));
+            unsigned char *row = sA(s, t) + r * 128;
+            *reinterpret_cast<uint4 *>(row + (((2 * k) ^ (r & 7)) << 4)) = lo;      // elements 0..15
+            *reinterpret_cast<uint4 *>(row + (((2 * k + 1) ^ (r & 7)) << 4)) = hi;  // elements 16..31
+            sDW(s)[(t * TG_M + r) * TG_KB + k] = wd[u];
+        }
+    };
+    auto issue = [&](int g, int s) {  // thread 0
+        const int j0 = g * TG_KB, nbg = nb - j0 < TG_KB ? nb - j0 : TG_KB;
+        constexpr unsigned idesc = umma_idesc_s8(TG_M, N);
+        for (int k = 0; k < nbg; k++) {
+#pragma unroll
+            for (int t = 0; t < RPT; t++)
+                tc_mma_s8(tbase + (unsigned)((k * RPT + t) * N), umma_desc_sw128(smem_addr(sA(s, t)) + 32u * k),
+                          umma_desc_sw128(smem_addr(sB(s)) + 32u * k), idesc, false);
+            tc_commit(&bar_mma[k]);
+        }
+    };
+
+    float acc[RPT][CPT];
+#pragma unroll
+    for (int t = 0; t < RPT; t++)
+#pragma unroll
+        for (int c = 0; c < CPT; c++) acc[t][c] = 0.0f;
+
+    load_a(0);   // constant weights: before the wait
+    pdl_wait();  // the activation rows are the previous kernel's output
+    stage_b(0, 0);
+    store_a(0);
+    cp_async_wait<0>();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        tc_fence_after();
+        issue(0, 0);
+    }
+    int issued = 1;  // groups whose MMAs are in flight or done
+    for (int g = 0; g < ng && !s_abort; g++) {
+        const int s = g & 1;
+        const bool more = g + 1 < ng;
+        if (more) {
+            stage_b(g + 1, s ^ 1);
+            load_a(g + 1);
+        }
+        // drain the blocks of group g
+        const int nbg = nb - g * TG_KB < TG_KB ? nb - g * TG_KB : TG_KB;
+        for (int k = 0; k < nbg; k++) {
+            if (!mbar_wait(&bar_mma[k], (unsigned)g & 1u, &s_abort, a.err)) break;
+            tc_fence_after();
+            const float *da = sDA(s) + k * N + hf * CPT;
+#pragma unroll
+            for (int t = 0; t < RPT; t++) {
+                unsigned raw[CPT];
+                const unsigned ta = tbase + ((unsigned)(quad * 32) << 16) + (unsigned)((k * RPT + t) * N + hf * CPT);
+                if constexpr (CPT == 32)
+                    tc_ld32_u32(ta, raw);
+                else
+                    tc_ld16_u32(ta, raw);
+                const float dw = sDW(s)[(t * TG_M + quad * 32 + lane) * TG_KB + k];
+#pragma unroll
+                for (int c = 0; c < CPT; c++)
+                    acc[t][c] = __fmaf_rn(__fmul_rn(dw, da[c]), (float)(int)raw[c], acc[t][c]);
+            }
+        }
+        if (more) store_a(s ^ 1);
+        cp_async_wait<0>();
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();  // TMEM columns drained, stage s^1 complete
+        if (more && !s_abort && tid == 0) {
+            tc_fence_after();
+            issue(g + 1, s ^ 1);
+        }
+        if (more) issued = g + 2;
+    }
+    const bool failed = s_abort != 0;
+    if (failed && tid == 0) {
+        // a wait gave up: let the committed MMAs finish (bounded) before the
+        // TMEM they write is freed
+        const int g = issued - 1;
+        const long long tw = clock64();
+        for (int k = 0; k < TG_KB; k++)
+            while (!mbar_test(&bar_mma[k], (unsigned)g & 1u) && clock64() - tw < WAIT_LIMIT) {
+            }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tc_dealloc(tbase, SH::tcols);
+    pdl_release();
+    if (failed) return;
+    // ---- epilogue: column by column through the GEMV epilogue (lane = row)
+    if (tile_of(0, quad) >= mtiles) return;  // warp-uniform: rows past the matrix
+    int tile[RPT];
+#pragma unroll
+    for (int t = 0; t < RPT; t++) tile[t] = tile_of(t, quad);
+#pragma unroll 1
+    for (int c = 0; c < CPT; c++) {
+        const int b = n0 + hf * CPT + c;
+        if (b >= a.batch) break;  // warp-uniform
+        float one[RPT][1][8];
+#pragma unroll
+        for (int t = 0; t < RPT; t++) {
+            one[t][0][0] = acc[t][c];
+#pragma unroll
+            for (int k = 1; k < 8; k++) one[t][0][k] = 0.0f;
+        }
+        gemv_epilogue<RPT, 1, EPI>(a, one, tile, total_tiles, b, lane);
+    }
+}
+
 constexpr int TARGET_WARPS = 148 * 4;
 
 template <int BT, int EPI>
@@ -511,6 +748,8 @@ inline bool decode_gemm_forced() {
 // four activation rows per warp cut the weight unpacking per row by four and
 // the CTA count by four against one row per warp.
 constexpr int GEMM_MIN_BATCH_WIDE = 32;
+// the tensor-core GEMM (opt-in) from this many activation rows up
+constexpr int TC_MIN_BATCH = 128;
 
 inline bool gemm_shape(int rpt, int nb, int batch, int units) {
     const bool fits = staged_smem(rpt, gemm_nw(rpt, nb) * GEMM_BT, nb, false) <= STAGED_SMEM_MAX;
@@ -522,11 +761,24 @@ inline bool gemm_shape(int rpt, int nb, int batch, int units) {
 }
 
 template <int EPI>
+void launch_tc(const GemvArgs &a, int total_tiles, cudaStream_t s) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    using SH = TgShape<RPT>;
+    const int mtiles = RPT == 2 ? total_tiles / 2 : total_tiles;
+    const dim3 grid((unsigned)((mtiles + 3) / 4), (unsigned)((a.batch + SH::N - 1) / SH::N));
+    launch_kernel(gemm_tc_kernel<RPT, EPI>, grid, dim3(TG_THREADS), SH::smem, s, a.pdl, a, total_tiles);
+}
+
+template <int EPI>
 void launch_epi(const GemvArgs &a, cudaStream_t s) {
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
     const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
+    if (a.tc && !norm && a.batch >= TC_MIN_BATCH) {
+        launch_tc<EPI>(a, total_tiles, s);
+        return;
+    }
     if (!norm && gemm_shape(RPT, a.nb, a.batch, units)) {
         // decode batches: four warps per CTA, for twice the CTAs
         const int nw = a.batch < GEMM_MIN_BATCH ? STAGED_MAX_WARPS / 2 : gemm_nw(RPT, a.nb);
@@ -554,6 +806,9 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
 
 template <int EPI>
 void set_limits(int bytes) {
+    cudaFuncSetAttribute(gemm_tc_kernel<(EPI == EPI_SWIGLU_Q8) ? 2 : 1, EPI>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)TgShape<(EPI == EPI_SWIGLU_Q8) ? 2 : 1>::smem);
     cudaFuncSetAttribute(gemv_kernel<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(gemv_kernel<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(gemv_kernel<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

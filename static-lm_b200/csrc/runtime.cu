@@ -319,9 +319,10 @@ SLM_EXPORT void slm_qmatrix_destroy(slm_qmatrix *w) {
 namespace {
 
 int gemm_into(const slm_qmatrix *w, Q8X x, float *out, uint64_t batch, uint64_t rows,
-              uint64_t cols, cudaStream_t st) {
+              uint64_t cols, cudaStream_t st, bool tc = false) {
     ensure_kernel_attributes();
     GemvArgs g{};
+    g.tc = tc;
     g.w = w->tiles;
     g.rows = (int)rows;
     g.nb = (int)(cols / QK);
@@ -395,6 +396,23 @@ SLM_EXPORT int slm_gemm_q4_0(const slm_qmatrix *w, const void *xq, float *out, u
     launch_q8_ref_to_q8x(xq, x, blocks, st);
     TRY(launch_check("q8 conversion kernel"));
     return gemm_into(w, x, out, batch, rows, cols, st);
+}
+
+SLM_EXPORT int slm_gemm_q4_0_tensor_cores(const slm_qmatrix *w, const void *xq, float *out, uint64_t batch,
+                                          uint64_t rows, uint64_t cols, void *scratch, uint64_t scratch_bytes,
+                                          void *stream) {
+    TRY(check_gemm_shape(w, batch, rows, cols));
+    if (batch == 0 || rows == 0) return SLM_OK;
+    if (!xq || !out || !scratch) return fail(SLM_ERR_INVALID_ARG, "null device pointer");
+    uint64_t blocks = batch * (cols / QK);
+    if (scratch_bytes < q8x_bytes(blocks)) return fail(SLM_ERR_CAPACITY, "scratch too small");
+    if ((uintptr_t)scratch % 16) return fail(SLM_ERR_INVALID_ARG, "scratch must be 16-byte aligned");
+    DeviceScope ds(w->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    Q8X x = q8x_view(scratch, blocks);
+    launch_q8_ref_to_q8x(xq, x, blocks, st);
+    TRY(launch_check("q8 conversion kernel"));
+    return gemm_into(w, x, out, batch, rows, cols, st, true);
 }
 
 // ---- the allocation-free GEMM: Q8 activations in a static device buffer
@@ -862,6 +880,7 @@ struct slm_model {
     bool use_pdl = true;     // programmatic dependent launch between decode kernels
     bool no_prefill_tiles = false;  // SLM_PREFILL_ROWWISE=1: prefill through the per-row kernels
     int prefill_mode = SLM_PREFILL_EXACT;  // slm_model_set_prefill_mode
+    bool gemm_tc = true;     // SLM_PREFILL_GEMM_EXACT=1: tensor-core prefill mode keeps exact projections
     int parts = 1;           // decode parts (streams) for batches of 16+ rows
     int pv_per_head = 1;     // softmax + PV per (row, query head): AttnArgs::pv_per_head
     int decode_mode = SLM_DECODE_EXACT;  // slm_model_set_decode_mode
@@ -1100,6 +1119,9 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     aa.prefill_run = kind == STEP_PREFILL ? n : kind == STEP_PREFILL_BATCH ? seq_rows : 0;
     if (m->no_prefill_tiles) aa.prefill_run = 0;
     aa.prefill_tc = aa.prefill_run > 0 && m->prefill_mode == SLM_PREFILL_TENSOR_CORES;
+    // the tensor-core prefill mode also runs the projections' int8 products on
+    // the tensor cores (batches of 128+ rows)
+    const bool gemm_tc = aa.prefill_tc && m->gemm_tc;
     if (kind == STEP_PREFILL_BATCH) {
         aa.rows_per_seq = seq_rows;
         aa.shard_n = sharded ? m->shard_n : 1;
@@ -1111,8 +1133,8 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     }
     // decode rows in the opt-in split-K flash-decode mode (the Q8_0 of the
     // output inside the kernel)
-    const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && fused && m->have_kmap64 &&
-                       flash_decode_ok(aa);
+    const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && m->use_fused_attention &&
+                       m->have_vmap && m->have_kmap64 && flash_decode_ok(aa);
     const int n_units = kind == STEP_PREFILL_BATCH && seq_rows > 0 ? (n / seq_rows) * (int)c.num_kv_heads : 0;
     const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
     const bool norm_gu = m->L > 0 && gate_up_norm_fused(m, n);
@@ -1143,6 +1165,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.qkv = qa;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
+        g.tc = gemm_tc;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_QKV);
         // attention (transformer.rs:430-443)
@@ -1203,6 +1226,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.ld_res = d;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
+        g.tc = gemm_tc;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_WO);
         // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
@@ -1226,6 +1250,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.q8_out = qb8;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
+        g.tc = gemm_tc;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_GATE_UP);
         // down + residual (transformer.rs:477-486)
@@ -1242,6 +1267,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.ld_res = d;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
+        g.tc = gemm_tc;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_DOWN);
     }
@@ -1293,10 +1319,13 @@ uint32_t decode_launches(const slm_model *m, int n) {
     const AttnArgs pa = decode_probe(m, (int)m->cfg.max_seq_len);
     const int kv_mul = (int)(m->cfg.num_heads / m->cfg.num_kv_heads);
     uint32_t attn = 4;  // scores, softmax, pv, quantize
-    if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
-        if (m->decode_mode == SLM_DECODE_FLASH && m->have_kmap64 && flash_decode_ok(pa))
-            attn = 2;  // flash-decode chunks, then the combine (with the Q8_0 of the output)
-        else if (m->pv_per_head >= 3 && kv_mul <= 4 && kv_mul * m->hd <= 480)
+    if (m->use_fused_attention && m->have_vmap && m->decode_mode == SLM_DECODE_FLASH && m->have_kmap64 &&
+        flash_decode_ok(pa)) {
+        AttnArgs pr = pa;
+        pr.rows = n;
+        attn = (uint32_t)flash_decode_launches(pr);  // splits (+ the combine, with the Q8_0 of the output)
+    } else if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
+        if (m->pv_per_head >= 3 && kv_mul <= 4 && kv_mul * m->hd <= 480)
             attn = ((kv_mul * m->hd) % 32 == 0) ? 2 : 3;
         else if (m->pv_per_head)
             attn = (m->hd % 32 == 0) ? 2 : 3;
@@ -1556,6 +1585,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->pv_per_head = env_pv_per_head();
     env = getenv("SLM_DECODE_PARTS");
     if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
+    env = getenv("SLM_PREFILL_GEMM_EXACT");
+    m->gemm_tc = !(env && env[0] == '1');
     env = getenv("SLM_PREFILL_ROWWISE");
     m->no_prefill_tiles = env && env[0] == '1';
     env = getenv("SLM_NO_PDL");

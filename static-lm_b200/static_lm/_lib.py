@@ -81,6 +81,7 @@ SIGNATURES = {
     "slm_gemm_q4_0_arena": (C.c_int, [_V, _V, Slice, Slice, Slice, _U64, _U64, _U64, _V], True),
     "slm_gemm_q4_0": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V, _U64, _V], True),
     "slm_gemm_q4_0_scratch_bytes": (_U64, [_U64, _U64], False),
+    "slm_gemm_q4_0_tensor_cores": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V, _U64, _V], True),
     "slm_gemm_q4_0_f32_noalloc": (C.c_int, [_V, _V, _V, _U64, _U64, _U64, _V], True),
     "slm_quantize_row_q8_0": (C.c_int, [_V, _V, _U64, _V], True),
     "slm_selftest_bounded_wait": (C.c_int, [C.c_int, _U64], False),
