@@ -48,7 +48,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill measurement")
     p.add_argument("--no-flash", action="store_true", help="skip the flash-decode leg")
-    p.add_argument("--sweep", default=None, choices=["cfg4"],
+    p.add_argument("--sweep", default=None, choices=["cfg4", "published"],
                    help="kernel sweep of BASELINE config 4 instead of the bench line: decode "
                         "attention (exact and flash) at L 512/2048/8192 x B 1..128 and the Q4 GEMVs "
                         "4096x4096 / 14336x4096 at B 1/8/64, one JSON line per case")
@@ -666,10 +666,108 @@ def run_sweep(args):
     return 0
 
 
+def run_published(args):
+    """GPU figures beside the reference's published CPU timings
+    (README.md:136-145): wall-clock time through the
+    public API of model creation (weight upload: the "load" of those runs)
+    plus a 16-token prefill and 8 or 64 greedy decode steps, for the config-1,
+    Stories-15M (config 2) and SmolLM2-135M (config 3) shapes with synthetic
+    weights; then config 2 at batch 32 and config 5 (8 x 4096-token prefill,
+    then 128 greedy steps per sequence).  One JSON line per case; every case
+    is run twice and the second run reported (the first pays one-time CUDA
+    module loading)."""
+    import torch
+    import static_lm as S
+    from static_lm import synth
+    torch.cuda.set_device(0)
+    torch.cuda.synchronize()
+
+    def one(name, n_dec, max_seq=None):
+        cfg, layers, vocab = synth.config(name, max_seq_len=max_seq)
+        w = synth.synth_model(cfg, layers, vocab, seed=args.seed)
+        prompt = (np.arange(16, dtype=np.int32) * 7 + 3) % vocab
+        res = None
+        for _ in range(2):
+            t0 = time.perf_counter()
+            m = S.Model(cfg, w, max_sequences=1, max_rows=16)
+            t1 = time.perf_counter()
+            toks = m.generate(prompt, n_dec + 1)  # the prefill's token, then n_dec decode steps
+            t2 = time.perf_counter()
+            m.close()
+            res = (t1 - t0, t2 - t1, len(toks))
+        return res
+
+    published = {("cfg1", 8): 76.0, ("cfg2", 8): 114.6, ("cfg2", 64): 340.0, ("cfg3", 8): 703.0,
+                 ("cfg3", 64): 2510.0}
+    for (name, n_dec), ref_ms in published.items():
+        load, run, n = one(name, n_dec, 256 if name == "cfg3" else None)
+        print(json.dumps({"sweep": "published", "config": name, "prompt_tokens": 16, "decoded": n_dec,
+                          "gpu_load_plus_generate_ms": round((load + run) * 1000, 2),
+                          "gpu_generate_ms": round(run * 1000, 2), "gpu_load_ms": round(load * 1000, 2),
+                          "reference_ms": ref_ms,
+                          "reference": "README.md:136-145, Ryzen 5 PRO 4650U, whole process incl. start-up",
+                          "data": "synthetic weights of the same shape"}), flush=True)
+    # config 2 at batch 32: 16-token prompts, batched prefill, 64 greedy steps
+    cfg, layers, vocab = synth.config("cfg2")
+    w = synth.synth_model(cfg, layers, vocab, seed=args.seed)
+    B = 32
+    m = S.Model(cfg, w, max_sequences=B, max_rows=B * 16)
+    prompts = np.random.default_rng(args.seed).integers(0, vocab, (B, 16)).astype(np.int32)
+    for rep in range(2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        first = m.prefill_batch(prompts)
+        t1 = time.perf_counter()
+        seqs = torch.arange(B, dtype=torch.int32, device="cuda")
+        td = torch.tensor(list(first), dtype=torch.int32, device="cuda")
+        pd = torch.full((B,), 16, dtype=torch.int32, device="cuda")
+        out = torch.zeros(64 * B, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        m.decode_steps_device(B, seqs.data_ptr(), td.data_ptr(), pd.data_ptr(), 64, out.data_ptr(), 16)
+        torch.cuda.ExternalStream(m.stream).synchronize()
+        t3 = time.perf_counter()
+    print(json.dumps({"sweep": "published", "config": "cfg2", "batch": B, "prompt_tokens": 16, "decoded": 64,
+                      "prefill_ms": round((t1 - t0) * 1000, 3), "decode_ms": round((t3 - t2) * 1000, 3),
+                      "decode_tok_s": round(B * 64 / (t3 - t2), 1)}), flush=True)
+    m.close()
+    # config 5: 8 prompts x 4096 tokens, batched prefill, then 128 greedy steps
+    cfg, layers, vocab = synth.config("cfg5")
+    w = synth.synth_model(cfg, layers, vocab, seed=args.seed)
+    nseq = 8
+    m = S.Model(cfg, w, max_sequences=nseq, max_rows=nseq * PREFILL_LEN)
+    prompts = np.random.default_rng(args.seed).integers(0, vocab, (nseq, PREFILL_LEN)).astype(np.int32)
+    for rep in range(2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        first = m.prefill_batch(prompts)
+        t1 = time.perf_counter()
+        seqs = torch.arange(nseq, dtype=torch.int32, device="cuda")
+        td = torch.tensor(list(first), dtype=torch.int32, device="cuda")
+        pd = torch.full((nseq,), PREFILL_LEN, dtype=torch.int32, device="cuda")
+        out = torch.zeros(128 * nseq, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        m.decode_steps_device(nseq, seqs.data_ptr(), td.data_ptr(), pd.data_ptr(), 128, out.data_ptr(),
+                              PREFILL_LEN)
+        torch.cuda.ExternalStream(m.stream).synchronize()
+        t3 = time.perf_counter()
+    print(json.dumps({"sweep": "published", "config": "cfg5", "sequences": nseq, "prompt_tokens": PREFILL_LEN,
+                      "decoded": 128, "prefill_ms": round((t1 - t0) * 1000, 2),
+                      "prefill_tok_s": round(nseq * PREFILL_LEN / (t1 - t0), 1),
+                      "decode_ms": round((t3 - t2) * 1000, 2),
+                      "decode_tok_s": round(nseq * 128 / (t3 - t2), 1), "arithmetic": "exact (default modes)"}),
+          flush=True)
+    m.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep == "published":
+        return run_published(args)
     if args.sweep:
         return run_sweep(args)
     return run_ours(args)

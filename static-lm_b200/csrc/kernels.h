@@ -184,7 +184,10 @@ struct AttnArgs {
     // fused path, softmax + PV: 0 = one CTA per (row, KV head) running its
     // kv_mul heads, a thread per (head, dim pair); 1 = one CTA per (row,
     // query head), a thread per dim; 2 = the same with a thread per dim pair;
-    // 3 = one CTA per (row, KV head), a thread per (head, dim).  Same results.
+    // 3 = one CTA per (row, KV head), a thread per (head, dim); 4, 5 = the
+    // same with a thread per dim running every head / per (head, dim pair);
+    // 6, 7 = one CTA per (row, KV head, half of head_dim), a thread per (head,
+    // dim) / (head, dim pair).  Same results.
     int pv_per_head;
     // decode (opt-in split-K flash-decode, kernels_attn_flash.cu): partial
     // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)]
@@ -222,8 +225,10 @@ void launch_attn_pv(const AttnArgs &a, cudaStream_t s);
 bool attention_fused_ok(const AttnArgs &a);
 // amap: the tensor map of encode_att_map over the att scratch (null = no
 // query-tiled prefill softmax/PV)
+// vmap_half: the V planes with a box head_dim / 2 wide (encode_v_map with
+// head_dim / 2), or null; used by the split softmax + PV forms (modes 6, 7)
 void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       const CUtensorMap *amap, cudaStream_t s);
+                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half = nullptr);
 // 3-D tensor map over att [rows][heads][att_ld] f32, box = 64 positions x
 // kv_mul heads x 16 rows (the prefill probability tiles).
 bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, uint64_t rows,

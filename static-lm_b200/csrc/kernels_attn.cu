@@ -996,7 +996,10 @@ struct PvVec {
 // num_heads; the kv_mul CTAs of a KV head then each stream its V rows, mostly
 // from L2).  NST is the depth of the V ring (<= PV_MAX_STAGES), chosen by the
 // launch from the CTAs each SM holds.
-template <int KVM, int NH, int ND, int HDT = 0>
+// DS: the head_dim split -- with DS = 2 a CTA covers half of every head's dims
+// (grid.x = num_kv_heads * 2, V from a tensor map whose box is head_dim / 2
+// wide), so each V tile is half as large and is staged once for all KVM heads.
+template <int KVM, int NH, int ND, int HDT = 0, int DS = 1>
 __global__ void __launch_bounds__(512)
     attn_softmax_pv_kernel(AttnArgs a, int lp, int NST, const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1006,11 +1009,14 @@ __global__ void __launch_bounds__(512)
     float *smem = reinterpret_cast<float *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
     constexpr int tt = TT_V;
     const int nth = blockDim.x;
-    const int h0 = blockIdx.x * KVM, r = blockIdx.y;  // first query head of this CTA
+    const int h0 = (blockIdx.x / DS) * KVM, r = blockIdx.y;  // first query head of this CTA
+    const int dsp = blockIdx.x % DS;                          // which part of the head's dims
     const int g = h0 / (a.num_heads / a.num_kv_heads);  // its KV head
     if (!unit_owned(a, r, g)) return;  // CTA-uniform: another rank's unit
-    // HDT: head_dim fixed at compile time (V rows at immediate offsets), or 0
-    const int hd = HDT ? HDT : a.head_dim;
+    // HDT: head_dim fixed at compile time (V rows at immediate offsets), or 0;
+    // hd is this CTA's part of it (the V tile width and the dims it computes)
+    const int hdf = HDT ? HDT : a.head_dim;
+    const int hd = hdf / DS;
     const int tid = threadIdx.x;
     float *s_ring = smem;                                   // [NST][tt][hd]
     float *s_sc = s_ring + (size_t)NST * tt * hd;           // [KVM][lp]
@@ -1018,7 +1024,7 @@ __global__ void __launch_bounds__(512)
     float *s_red = s_out + (size_t)KVM * hd;                // 64 + 8*32 floats
     const int L = row_len(a, r);
     const int ntiles = (L + tt - 1) / tt;
-    const int vx = g * hd;
+    const int vx = g * hdf + dsp * hd;
     const int vz = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
     const int n_thr = KVM * hd / (NH * ND);  // consumer threads: (NH heads, ND dims)
     const int n_cons = (n_thr + 31) >> 5;  // consumer warps
@@ -1284,16 +1290,17 @@ __global__ void __launch_bounds__(512)
         return;
     }
     pdl_release();  // the successor may start while the outputs are written
-    float *orow = a.out + (size_t)r * a.ldo + (size_t)h0 * hd;
-    for (int k = tid; k < KVM * hd; k += nth) orow[k] = s_out[k];
-    // Q8_0 of the attention output for the Wo GEMV: this CTA owns the
-    // KVM*hd consecutive dims from g*KVM*hd, one 32-element block per warp
-    // when KVM*hd is a multiple of 32 (checked by the host)
+    // this CTA's dims: [dsp*hd, (dsp+1)*hd) of each of its KVM heads
+    float *orow = a.out + (size_t)r * a.ldo + (size_t)h0 * hdf + (size_t)dsp * hd;
+    for (int k = tid; k < KVM * hd; k += nth) orow[(k / hd) * hdf + k % hd] = s_out[k];
+    // Q8_0 of the attention output for the Wo GEMV: this CTA owns whole
+    // 32-element blocks (hd a multiple of 32, checked by the host), one per
+    // warp
     if (a.q8_out.qs) {
-        const int nbr = a.dim / 32;
+        const int nbr = a.dim / 32, bph = hd / 32;  // blocks per head part
         for (int blk = warp; blk < (KVM * hd) / 32; blk += nw)
             q8x_store_block(s_out[blk * 32 + lane], a.q8_out,
-                            (size_t)r * nbr + (size_t)(h0 * hd) / 32 + blk, lane);
+                            (size_t)r * nbr + (size_t)((h0 + blk / bph) * hdf + dsp * hd) / 32 + blk % bph, lane);
     }
 }
 
@@ -1356,6 +1363,38 @@ void launch_pv_group_shape(const AttnArgs &a, const FusedShape &f, const CUtenso
         launch_kernel(attn_softmax_pv_kernel<KVM, NH, ND, 128>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
     else
         launch_kernel(attn_softmax_pv_kernel<KVM, NH, ND>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+}
+
+// The (row, KV head, head_dim half) form: grid.x = num_kv_heads * 2, V
+// through vmap_half (box head_dim / 2 wide); mode 6: a thread per (head,
+// dim), 7: a thread per (head, dim pair).
+template <int KVM, int ND>
+void launch_softmax_pv_split(const AttnArgs &a, const CUtensorMap &vmap_half, cudaStream_t s) {
+    const int hdv = a.head_dim / 2;
+    const long long ctas = (long long)a.rows * a.num_kv_heads * 2;
+    const long long per_sm = (ctas + sm_count() - 1) / sm_count();
+    const size_t budget = (size_t)(FUSED_SMEM_MAX / (per_sm < 1 ? 1 : per_sm));
+    const size_t fixed = fused_shape(KVM, hdv, a.max_len, 0).smem;
+    const size_t stage = (size_t)TT_V * hdv * sizeof(float);
+    long long nst = budget > fixed ? (long long)((budget - fixed) / stage) : 0;
+    nst = nst < PV_MIN_STAGES ? PV_MIN_STAGES : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
+    const FusedShape f = fused_shape(KVM, hdv, a.max_len, (int)nst);
+    const int cons = (KVM * hdv / ND + 31) / 32 * 32;
+    const dim3 grid(a.num_kv_heads * 2, a.rows), block(cons + 32);
+    if (a.head_dim == 64)
+        launch_kernel(attn_softmax_pv_kernel<KVM, 1, ND, 64, 2>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap_half);
+    else
+        launch_kernel(attn_softmax_pv_kernel<KVM, 1, ND, 128, 2>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap_half);
+}
+
+template <int KVM>
+void set_softmax_pv_split_smem(int bytes) {
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, 1, 1, 64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, 1, 1, 128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, 1, 2, 64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<KVM, 1, 2, 128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 // mode 3: a thread per (head, dim); 4: a thread per dim running every head
@@ -1499,7 +1538,7 @@ bool attention_fused_ok(const AttnArgs &a) {
 }
 
 void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       const CUtensorMap *amap, cudaStream_t s) {
+                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half) {
     if (args.rows <= 0) return;
     if (args.prefill_tc && attn_prefill_tc_ok(args)) {
         launch_attn_prefill_tc(args, s);
@@ -1593,7 +1632,18 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
         return;
     }
-    if (a.pv_per_head >= 3 && KVM_GROUP_OK(kv_mul) && kv_mul * a.head_dim <= 480) {
+    if (a.pv_per_head >= 6 && vmap_half && KVM_GROUP_OK(kv_mul) && (a.head_dim == 64 || a.head_dim == 128) &&
+        kv_mul * a.head_dim / 2 <= 480) {
+        const bool nd2 = a.pv_per_head == 7;
+        switch (kv_mul) {
+            case 1: nd2 ? launch_softmax_pv_split<1, 2>(a, *vmap_half, s) : launch_softmax_pv_split<1, 1>(a, *vmap_half, s); break;
+            case 2: nd2 ? launch_softmax_pv_split<2, 2>(a, *vmap_half, s) : launch_softmax_pv_split<2, 1>(a, *vmap_half, s); break;
+            case 3: nd2 ? launch_softmax_pv_split<3, 2>(a, *vmap_half, s) : launch_softmax_pv_split<3, 1>(a, *vmap_half, s); break;
+            default: nd2 ? launch_softmax_pv_split<4, 2>(a, *vmap_half, s) : launch_softmax_pv_split<4, 1>(a, *vmap_half, s); break;
+        }
+        return;
+    }
+    if (a.pv_per_head >= 3 && a.pv_per_head <= 5 && KVM_GROUP_OK(kv_mul) && kv_mul * a.head_dim <= 480) {
         switch (kv_mul) {
             case 1: launch_softmax_pv_group<1>(a, vmap, s); break;
             case 2: launch_softmax_pv_group<2>(a, vmap, s); break;
@@ -1632,6 +1682,10 @@ void set_attention_smem_limit(int bytes) {
     set_softmax_pv_smem<6>(bytes);
     set_softmax_pv_smem<7>(bytes);
     set_softmax_pv_smem<8>(bytes);
+    set_softmax_pv_split_smem<1>(bytes);
+    set_softmax_pv_split_smem<2>(bytes);
+    set_softmax_pv_split_smem<3>(bytes);
+    set_softmax_pv_split_smem<4>(bytes);
     set_softmax_pv_group_smem<1>(bytes);
     set_softmax_pv_group_smem<2>(bytes);
     set_softmax_pv_group_smem<3>(bytes);

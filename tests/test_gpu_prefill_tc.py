@@ -22,10 +22,20 @@ from static_lm.synth import Config
 pytestmark = pytest.mark.gpu
 
 
-def _close(got, want, rel=5e-2):
-    tol = rel * float(np.abs(want).max()) + 1e-4
+# Model-level logit bound, relative to max |logit|.  Each flipped Q8_0 value
+# moves its row by one step (amax/127 of its block, ~0.8 % of the block's
+# largest value); the 2-layer seeded cases below measured at most
+# MEASURED_LOGIT_REL, and the bound keeps a factor ~2 over that.
+LOGIT_REL = 2e-2
+MEASURED_LOGIT_REL = {}
+
+
+def _close(got, want, key, rel=LOGIT_REL):
+    scale = float(np.abs(want).max())
     err = float(np.abs(got - want).max())
-    assert err <= tol, (err, tol)
+    MEASURED_LOGIT_REL[key] = err / scale
+    print(f"tc-prefill logits {key}: max|diff|/max|logit| = {err / scale:.3e}")
+    assert err <= rel * scale + 1e-4, (key, err, scale)
     return err
 
 
@@ -80,7 +90,7 @@ def test_tensor_core_prefill_within_tolerance(cuda, name, nseq, n):
     got = list(tc.prefill_batch(prompts))
     assert got == want
     for s in range(nseq):
-        _close(tc.logits(s), exact.logits(s))
+        _close(tc.logits(s), exact.logits(s), f"{name}-{nseq}x{n}-seq{s}")
     # decoding continues from the tensor-core prefill's KV cache (decode is exact)
     nxt_e = exact.decode_batch(list(range(nseq)), want, [n] * nseq)
     nxt_t = tc.decode_batch(list(range(nseq)), got, [n] * nseq)
@@ -94,7 +104,7 @@ def test_tensor_core_prefill_head_dim_32_and_single_prompt(cuda):
     exact, tc = _pair(cfg, 2, 1024, 1, 200)
     toks = np.random.default_rng(9).integers(0, 1024, 200).astype(np.int32)
     assert tc.prefill_tokens(toks) == exact.prefill_tokens(toks)
-    _close(tc.logits(0), exact.logits(0))
+    _close(tc.logits(0), exact.logits(0), "hd32-1x200")
 
 
 def test_tensor_core_mode_falls_back_to_exact_for_other_head_dims(cuda):
