@@ -440,10 +440,11 @@ def run_ours(args):
         f_achieved = kv_bytes_layer / (f_attn_launch_ms / 1000.0) / 1e9
         flash = {
             "value": GLOBAL_BATCH * K / (fms / 1000.0), "unit": "tok/s", "ms_per_step": fms / K,
-            "arithmetic": "split-K flash-decode (128-key chunks, per-chunk max / exp sums / PV, "
-                          "combined by the last CTA); ~1e-6 relative to the exact path; opt-in via "
-                          "slm_model_set_decode_mode",
-            "roofline": {"bound": "hbm", "kernel": "attn_flash_decode_kernel (one layer, all rows)",
+            "arithmetic": "split-K flash-decode (64-key chunks, online max / exp sums / PV across a "
+                          "CTA's chunks, splits merged by a combine kernel); ~1e-6 relative to the exact "
+                          "path; opt-in via slm_model_set_decode_mode",
+            "roofline": {"bound": "hbm", "kernel": "attn_flash_decode_kernel + attn_flash_combine_kernel "
+                                                   "(one layer, all rows)",
                          "achieved": f_achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": f_achieved / hbm_peak, "peak_source": peak_note,
                          "algorithmic_bytes_per_launch": kv_bytes_layer},

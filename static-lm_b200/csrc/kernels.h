@@ -142,6 +142,8 @@ void set_gemv_smem_limit(int bytes);
 // (128-byte swizzle), V = head_dim floats x V_BOX_POSITIONS positions.
 constexpr int K_BOX_KEYS = 128;
 constexpr int V_BOX_POSITIONS = 64;
+// the box of the fine V map (softmax + PV forms with 16/32-position stages)
+constexpr int V_FINE_POSITIONS = 16;
 // keys of one flash-decode work item (one V box)
 constexpr int FD_ITEM_KEYS = V_BOX_POSITIONS;
 
@@ -187,7 +189,9 @@ struct AttnArgs {
     // 3 = one CTA per (row, KV head), a thread per (head, dim); 4, 5 = the
     // same with a thread per dim running every head / per (head, dim pair);
     // 6, 7 = one CTA per (row, KV head, half of head_dim), a thread per (head,
-    // dim) / (head, dim pair).  Same results.
+    // dim) / (head, dim pair); 8, 9 = as 1 with 32- / 16-position V stages
+    // (a deeper ring in the same shared memory); 10 = one CTA per (row, query
+    // head, half of head_dim), a thread per dim.  Same results.
     int pv_per_head;
     // decode (opt-in split-K flash-decode, kernels_attn_flash.cu): partial
     // results [rows][num_kv_heads][fd_nch][kv_mul*(head_dim+2)]
@@ -227,18 +231,21 @@ bool attention_fused_ok(const AttnArgs &a);
 // query-tiled prefill softmax/PV)
 // vmap_half: the V planes with a box head_dim / 2 wide (encode_v_map with
 // head_dim / 2), or null; used by the split softmax + PV forms (modes 6, 7)
+// vmap_fine: the V planes with a V_FINE_POSITIONS-position box, or null; used
+// by the per-head forms with 32- and 16-position stages (modes 8, 9)
 void launch_attn_fused(const AttnArgs &a, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half = nullptr);
+                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half = nullptr,
+                       const CUtensorMap *vmap_fine = nullptr);
 // 3-D tensor map over att [rows][heads][att_ld] f32, box = 64 positions x
 // kv_mul heads x 16 rows (the prefill probability tiles).
 bool encode_att_map(CUtensorMap *map, const float *att, int att_ld, int heads, uint64_t rows,
                     int kv_mul);
 // 3-D tensor map over `planes` consecutive [max_seq][kv_dim] f32 planes from
-// `base`, box = head_dim floats x 64 positions x 1 plane.  False when the
-// driver entry point is missing or the shape is not expressible (the caller
-// then uses the three-phase path).
+// `base`, box = head_dim floats x box_pos positions x 1 plane.  False when
+// the driver entry point is missing or the shape is not expressible (the
+// caller then uses the three-phase path).
 bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
-                  uint64_t planes, int head_dim);
+                  uint64_t planes, int head_dim, int box_pos = V_BOX_POSITIONS);
 // The same planes for K, box = 32 floats x box_keys positions with the
 // 128-byte swizzle (head_dim % 32 == 0 only): K_BOX_KEYS for the exact
 // scores kernels, FD_ITEM_KEYS for the flash-decode kernel.

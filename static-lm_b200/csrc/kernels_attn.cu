@@ -204,17 +204,18 @@ struct FusedShape {
 
 // Shared memory of a softmax + PV CTA over `hpc` query heads with an
 // `nst`-stage V ring.
-__host__ __device__ inline FusedShape fused_shape(int hpc, int hd, int max_len, int nst = FUSED_STAGES) {
+__host__ __device__ inline FusedShape fused_shape(int hpc, int hd, int max_len, int nst = FUSED_STAGES,
+                                                  int tt = TT_V) {
     FusedShape f;
-    f.tt = TT_V;
+    f.tt = tt;
     f.lp = (max_len + 31) / 32 * 32 + 4;
     f.nst = nst;
-    f.smem = sizeof(float) * ((size_t)nst * TT_V * hd + (size_t)hpc * f.lp +
+    f.smem = sizeof(float) * ((size_t)nst * tt * hd + (size_t)hpc * f.lp +
                               (size_t)hpc * hd + 64 + 8 * 32) +
              128;
     return f;
 }
-constexpr int PV_MAX_STAGES = 16;
+constexpr int PV_MAX_STAGES = 32;
 #ifndef SLM_PV_MIN_STAGES
 #define SLM_PV_MIN_STAGES 2
 #endif
@@ -999,7 +1000,11 @@ struct PvVec {
 // DS: the head_dim split -- with DS = 2 a CTA covers half of every head's dims
 // (grid.x = num_kv_heads * 2, V from a tensor map whose box is head_dim / 2
 // wide), so each V tile is half as large and is staged once for all KVM heads.
-template <int KVM, int NH, int ND, int HDT = 0, int DS = 1>
+// TTV: V positions per stage.  TT_V is one box of the standard map; other
+// sizes (16, 32) come from a map whose box is V_FINE_POSITIONS positions, as
+// TTV / V_FINE_POSITIONS boxes per stage: smaller stages give a deeper ring
+// in the same shared memory, so more of each CTA's V stream is in flight.
+template <int KVM, int NH, int ND, int HDT = 0, int DS = 1, int TTV = TT_V>
 __global__ void __launch_bounds__(512)
     attn_softmax_pv_kernel(AttnArgs a, int lp, int NST, const __grid_constant__ CUtensorMap vmap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1007,7 +1012,10 @@ __global__ void __launch_bounds__(512)
     __shared__ int s_abort, s_issued;
     // TMA destinations 128-byte aligned (the launch adds 128 B of slack)
     float *smem = reinterpret_cast<float *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
-    constexpr int tt = TT_V;
+    constexpr int tt = TTV;
+    constexpr int box_pos = TTV == TT_V ? TT_V : V_FINE_POSITIONS;  // positions per TMA box
+    static_assert(TTV % box_pos == 0, "a stage is whole boxes");
+    constexpr int nld = TTV / box_pos;
     const int nth = blockDim.x;
     const int h0 = (blockIdx.x / DS) * KVM, r = blockIdx.y;  // first query head of this CTA
     const int dsp = blockIdx.x % DS;                          // which part of the head's dims
@@ -1047,7 +1055,10 @@ __global__ void __launch_bounds__(512)
         int k = 0;
         for (; k < NST && k < ntiles; k++) {
             mbar_arrive_expect_tx(&bar_full[k], tile_bytes);
-            tma_load_3d(s_ring + (size_t)k * tt * hd, &vmap, vx, k * tt, vz, &bar_full[k]);
+#pragma unroll
+            for (int j = 0; j < nld; j++)
+                tma_load_3d(s_ring + ((size_t)k * tt + j * box_pos) * hd, &vmap, vx, k * tt + j * box_pos, vz,
+                            &bar_full[k]);
         }
         s_issued = k;
     }
@@ -1092,50 +1103,54 @@ __global__ void __launch_bounds__(512)
         }
         __syncthreads();
     }
-    // exp(s - max) and the four lane sums of each head (graph.rs:168-179
-    // order), pipelined by segments of SEG positions: warp 0's lanes 4h..4h+3
-    // add segment k-1 while the other warps exponentiate segment k.  The lane
-    // chains cover [0, L & ~3) in order; the tail [L & ~3, L) is added after.
+    // exp(s - max) of every position by all threads, then the four lane sums
+    // of each head (graph.rs:168-179 order): lane 4h + l of warp 0 adds
+    // e[l], e[l+4], ... over [0, L & ~3) in order, its loads one group of 16
+    // ahead of the adds; the tail [L & ~3, L) is added after.
     const int vl = L & ~3;
-    constexpr int SEG = 256;
-    const int nseg = (L + SEG - 1) / SEG;
+#pragma unroll
+    for (int h = 0; h < KVM; h++) {
+        const float mx = s_red[32 + h];
+        float *row = s_sc + h * lp;
+        int t = tid;
+        for (; t + nth < L; t += 2 * nth) {
+            const float x0 = row[t], x1 = row[t + nth];
+            const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
+            row[t] = e0;
+            row[t + nth] = e1;
+        }
+        if (t < L) row[t] = exp_poly(__fsub_rn(row[t], mx));
+    }
+    __syncthreads();
     float chain = 0.0f;
-    // exp workers: warps w >= 1 with w % 4 != 0, so that no exp work shares
-    // warp 0's scheduler with the dependent chains
-    const bool worker = warp > 0 && (warp & 3) != 0;
-    const int wid = (warp - 1 - (warp >> 2)) * 32 + lane;
-    const int nwk = ((nw - 1) - (nw - 1) / 4) * 32;
-    for (int k = 0; k <= nseg; k++) {
-        if (worker && k < nseg) {
-            const int t0 = k * SEG, t1 = L - t0 < SEG ? L : t0 + SEG;
-            for (int h = 0; h < KVM; h++) {
-                const float mx = s_red[32 + h];
-                float *row = s_sc + h * lp;
-                int t = t0 + wid;
-                for (; t + nwk < t1; t += 2 * nwk) {
-                    const float x0 = row[t], x1 = row[t + nwk];
-                    const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
-                    row[t] = e0;
-                    row[t + nwk] = e1;
-                }
-                for (; t < t1; t += nwk) row[t] = exp_poly(__fsub_rn(row[t], mx));
-            }
-        }
-        if (warp == 0 && k > 0 && tid < 4 * KVM) {
-            const int h = tid >> 2, l = tid & 3;
-            const float *e = s_sc + h * lp;
-            const int t1 = (k * SEG < vl) ? k * SEG : vl;
-            int i = (k - 1) * SEG + l;
-            for (; i + 28 < t1; i += 32) {
-                float v[8];
+    if (warp == 0 && tid < 4 * KVM) {
+        const int h = tid >> 2, l = tid & 3;
+        const unsigned e0 = smem_addr(s_sc + h * lp + l);
+        const int n4 = vl >> 2;  // this lane's positions l, l+4, ... below vl
+        constexpr int G = 16;
+        float cur[G], nxt[G];
+        auto load = [&](int i, float (&v)[G]) {
 #pragma unroll
-                for (int u = 0; u < 8; u++) v[u] = e[i + 4 * u];
+            for (int u = 0; u < G; u++)
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v[u]) : "r"(e0 + 16u * (unsigned)(i + u)) : "memory");
+        };
+        int i = 0;
+        if (n4 >= G) load(0, cur);
+        for (; i + 2 * G <= n4; i += 2 * G) {
+            load(i + G, nxt);
 #pragma unroll
-                for (int u = 0; u < 8; u++) chain = __fadd_rn(chain, v[u]);
-            }
-            for (; i < t1; i += 4) chain = __fadd_rn(chain, e[i]);
+            for (int u = 0; u < G; u++) chain = __fadd_rn(chain, cur[u]);
+            if (i + 3 * G <= n4) load(i + 2 * G, cur);
+#pragma unroll
+            for (int u = 0; u < G; u++) chain = __fadd_rn(chain, nxt[u]);
         }
-        __syncthreads();
+        if (i + G <= n4) {
+#pragma unroll
+            for (int u = 0; u < G; u++) chain = __fadd_rn(chain, cur[u]);
+            i += G;
+        }
+        const float *e = s_sc + h * lp + l;
+        for (; i < n4; i++) chain = __fadd_rn(chain, e[4 * i]);
     }
     if (tid < 4 * KVM) s_red[tid] = chain;  // [0, 4*KVM) with KVM <= 8 stays below 32
     __syncthreads();
@@ -1187,7 +1202,10 @@ __global__ void __launch_bounds__(512)
             if (lane == 0) {
                 const int st = k % NST;
                 mbar_arrive_expect_tx(&bar_full[st], tile_bytes);
-                tma_load_3d(s_ring + (size_t)st * tt * hd, &vmap, vx, k * tt, vz, &bar_full[st]);
+#pragma unroll
+                for (int j = 0; j < nld; j++)
+                    tma_load_3d(s_ring + ((size_t)st * tt + j * box_pos) * hd, &vmap, vx, k * tt + j * box_pos, vz,
+                                &bar_full[st]);
                 s_issued = k + 1;
             }
             __syncwarp();
@@ -1201,70 +1219,94 @@ __global__ void __launch_bounds__(512)
         for (int h = 0; h < NH; h++)
 #pragma unroll
             for (int c = 0; c < ND; c++) acc[h][c] = 0.0f;
+        // Full tiles: a register pipeline of CH-position chunks, one chunk
+        // ahead, that runs across stage boundaries -- a stage is released
+        // as soon as its last chunk is in registers and the next stage's
+        // first chunk is loaded before the current chunk is added, so the
+        // only serial work per position is the add of each chain.  The
+        // loads are volatile so that they stay ahead of the adds.
+        constexpr int CH0 = NH > 1 ? 8 : 16, CH = CH0 < tt / 2 ? CH0 : tt / 2, NCH = tt / CH;
+        static_assert(tt % CH == 0 && NCH % 2 == 0 && CH % 4 == 0, "an even number of whole chunks per stage");
+        const int nfull = L / tt;
+        const unsigned ring0 = smem_addr(s_ring) + 4u * (unsigned)jc;
+        const unsigned prob0 = smem_addr(s_sc) + 4u * (unsigned)(hl * lp);
+        float va[CH][ND], vb[CH][ND], pa[NH][CH], pb[NH][CH];
+        // chunk ch of tile k into (v, p)
+        auto load = [&](int k, int ch, float (&v)[CH][ND], float (&pr)[NH][CH]) {
+            const unsigned vs = ring0 + 4u * (unsigned)(((k % NST) * tt + ch * CH) * hd);
+            const unsigned ps = prob0 + 4u * (unsigned)(k * tt + ch * CH);
+#pragma unroll
+            for (int u = 0; u < CH; u++) {
+                if constexpr (ND == 2)
+                    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v[u][0]), "=f"(v[u][1])
+                                 : "r"(vs + 4u * (unsigned)(u * hd)));
+                else
+                    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v[u][0]) : "r"(vs + 4u * (unsigned)(u * hd)));
+            }
+#pragma unroll
+            for (int h = 0; h < NH; h++)
+#pragma unroll
+                for (int u = 0; u < CH; u += 4)
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(pr[h][u]), "=f"(pr[h][u + 1]), "=f"(pr[h][u + 2]), "=f"(pr[h][u + 3])
+                                 : "r"(ps + 4u * (unsigned)(h * lp + u)));
+        };
+        auto add = [&](const float (&v)[CH][ND], const float (&pr)[NH][CH]) {
+#pragma unroll
+            for (int u = 0; u < CH; u++)
+#pragma unroll
+                for (int h = 0; h < NH; h++)
+#pragma unroll
+                    for (int c = 0; c < ND; c++) acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr[h][u], v[u][c]));
+        };
+        auto release = [&](int k) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_empty[k % NST]);
+        };
+        bool ok = true;
+        if (nfull > 0) {
+            ok = mbar_wait(&bar_full[0], 0u, &s_abort, a.err);
+            if (ok && active) load(0, 0, va, pa);
+        }
 #pragma unroll 1
-        for (int k = 0; k < ntiles; k++) {
-            if (!mbar_wait(&bar_full[k % NST], (unsigned)(k / NST) & 1u, &s_abort,
-                           a.err))
-                break;
-            if (active) {
-                const float *vt = s_ring + (size_t)(k % NST) * tt * hd + jc;  // row stride hd
-                const float *pp = s_sc + hl * lp + k * tt;                               // head stride lp
-                const int nrows = L - k * tt < tt ? L - k * tt : tt;
-                if (nrows == tt) {
-                    // full tile in chunks of PV_CH positions, double-buffered in
-                    // two register sets (no copies): the shared-memory loads of
-                    // chunk c+1 are in flight while chunk c is added
-                    constexpr int PV_CH = NH > 1 ? 8 : 16, NCH = TT_V / PV_CH;
-                    float4 pa[NH][PV_CH / 4], pb[NH][PV_CH / 4];
-                    PvVec<ND> va[PV_CH], vb[PV_CH];
-                    auto load = [&](int ch, float4 (&pc)[NH][PV_CH / 4], PvVec<ND> (&vc)[PV_CH]) {
+        for (int k = 0; ok && k < nfull; k++) {
 #pragma unroll
-                        for (int h = 0; h < NH; h++)
-#pragma unroll
-                            for (int u = 0; u < PV_CH / 4; u++)
-                                pc[h][u] = reinterpret_cast<const float4 *>(pp + (size_t)h * lp + ch * PV_CH)[u];
-#pragma unroll
-                        for (int u = 0; u < PV_CH; u++) vc[u] = PvVec<ND>::load(vt + (size_t)(ch * PV_CH + u) * hd);
-                    };
-                    auto add = [&](const float4 (&pc)[NH][PV_CH / 4], const PvVec<ND> (&vc)[PV_CH]) {
-#pragma unroll
-                        for (int u = 0; u < PV_CH / 4; u++) {
-#pragma unroll
-                            for (int e = 0; e < 4; e++)
-#pragma unroll
-                                for (int h = 0; h < NH; h++) {
-                                    const float pr = e == 0 ? pc[h][u].x
-                                                   : e == 1 ? pc[h][u].y
-                                                   : e == 2 ? pc[h][u].z
-                                                            : pc[h][u].w;
-#pragma unroll
-                                    for (int c = 0; c < ND; c++)
-                                        acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vc[4 * u + e].v[c]));
-                                }
-                        }
-                    };
-                    load(0, pa, va);
-#pragma unroll
-                    for (int ch = 0; ch < NCH; ch += 2) {
-                        if (ch + 1 < NCH) load(ch + 1, pb, vb);
-                        add(pa, va);
-                        if (ch + 2 < NCH) load(ch + 2, pa, va);
-                        if (ch + 1 < NCH) add(pb, vb);
-                    }
+            for (int ch = 0; ch < NCH; ch += 2) {
+                // chunk ch is in (va, pa); bring chunk ch + 1 into (vb, pb)
+                if (active) load(k, ch + 1, vb, pb);
+                if (active) add(va, pa);
+                // chunk ch + 2, or the next tile's chunk 0, into (va, pa)
+                if (ch + 2 < NCH) {
+                    if (active) load(k, ch + 2, va, pa);
                 } else {
-                    for (int tl = 0; tl < nrows; tl++) {
-                        const PvVec<ND> vv = PvVec<ND>::load(vt + (size_t)tl * hd);
+                    release(k);  // every chunk of tile k is in registers
+                    if (k + 1 < nfull) {
+                        ok = mbar_wait(&bar_full[(k + 1) % NST], (unsigned)((k + 1) / NST) & 1u, &s_abort, a.err);
+                        if (ok && active) load(k + 1, 0, va, pa);
+                    }
+                }
+                if (active) add(vb, pb);
+            }
+        }
+        // the ragged last tile, position by position
+        if (ok && nfull < ntiles) {
+            const int k = nfull;
+            ok = mbar_wait(&bar_full[k % NST], (unsigned)(k / NST) & 1u, &s_abort, a.err);
+            if (ok && active) {
+                const float *vt = s_ring + (size_t)(k % NST) * tt * hd + jc;  // row stride hd
+                const float *pp = s_sc + hl * lp + k * tt;                    // head stride lp
+                const int nrows = L - k * tt;
+                for (int tl = 0; tl < nrows; tl++) {
+                    const PvVec<ND> vv = PvVec<ND>::load(vt + (size_t)tl * hd);
 #pragma unroll
-                        for (int h = 0; h < NH; h++) {
-                            const float pr = pp[(size_t)h * lp + tl];
+                    for (int h = 0; h < NH; h++) {
+                        const float pr = pp[(size_t)h * lp + tl];
 #pragma unroll
-                            for (int c = 0; c < ND; c++) acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vv.v[c]));
-                        }
+                        for (int c = 0; c < ND; c++) acc[h][c] = __fadd_rn(acc[h][c], __fmul_rn(pr, vv.v[c]));
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_empty[k % NST]);
+            if (ok) release(k);
         }
         if (active)
 #pragma unroll
@@ -1334,20 +1376,20 @@ int sm_count() {
 
 // Depth of the V ring of a softmax + PV CTA over `hpc` query heads: the
 // shared memory an SM has, shared by the CTAs it holds when the grid is
-// spread evenly, in whole stages (2 to 16).  Few CTAs per SM (small batches)
+// spread evenly, in whole stages (2 to PV_MAX_STAGES).  Few CTAs per SM (small batches)
 // get deep rings, so that each CTA keeps enough bytes in flight to stream its
 // V rows at a useful rate on its own.
-FusedShape pv_shape(const AttnArgs &a, int hpc) {
+FusedShape pv_shape(const AttnArgs &a, int hpc, int tt = TT_V) {
     const long long ctas = (long long)a.rows * (a.num_heads / hpc);
     const long long per_sm = (ctas + sm_count() - 1) / sm_count();
     const size_t budget = (size_t)(FUSED_SMEM_MAX / (per_sm < 1 ? 1 : per_sm));
-    const size_t fixed = fused_shape(hpc, a.head_dim, a.max_len, 0).smem;
-    const size_t stage = (size_t)TT_V * a.head_dim * sizeof(float);
+    const size_t fixed = fused_shape(hpc, a.head_dim, a.max_len, 0, tt).smem;
+    const size_t stage = (size_t)tt * a.head_dim * sizeof(float);
     long long nst = budget > fixed ? (long long)((budget - fixed) / stage) : 0;
     nst = nst < PV_MIN_STAGES ? PV_MIN_STAGES : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
-    return fused_shape(hpc, a.head_dim, a.max_len, (int)nst);
+    return fused_shape(hpc, a.head_dim, a.max_len, (int)nst, tt);
 }
-FusedShape per_head_shape(const AttnArgs &a) { return pv_shape(a, 1); }
+FusedShape per_head_shape(const AttnArgs &a, int tt = TT_V) { return pv_shape(a, 1, tt); }
 
 // The (row, KV head) form with a thread per (head, dim), head_dim fixed at
 // compile time where it is 64 or 128 and a ring sized like the per-head one:
@@ -1386,6 +1428,29 @@ void launch_softmax_pv_split(const AttnArgs &a, const CUtensorMap &vmap_half, cu
                       vmap_half);
     else
         launch_kernel(attn_softmax_pv_kernel<KVM, 1, ND, 128, 2>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap_half);
+}
+
+// The (row, query head, half of head_dim) form (mode 10): grid.x =
+// num_heads * 2, V through vmap_half, a thread per dim of the half; twice
+// the CTAs of the per-head form, each streaming half of its head's V rows.
+void launch_softmax_pv_per_head_split(const AttnArgs &a, const CUtensorMap &vmap_half, cudaStream_t s) {
+    const int hdv = a.head_dim / 2;
+    const long long ctas = (long long)a.rows * a.num_heads * 2;
+    const long long per_sm = (ctas + sm_count() - 1) / sm_count();
+    const size_t budget = (size_t)(FUSED_SMEM_MAX / (per_sm < 1 ? 1 : per_sm));
+    const size_t fixed = fused_shape(1, hdv, a.max_len, 0).smem;
+    const size_t stage = (size_t)TT_V * hdv * sizeof(float);
+    long long nst = budget > fixed ? (long long)((budget - fixed) / stage) : 0;
+    nst = nst < PV_MIN_STAGES ? PV_MIN_STAGES : nst > PV_MAX_STAGES ? PV_MAX_STAGES : nst;
+    const FusedShape f = fused_shape(1, hdv, a.max_len, (int)nst);
+    const int cons = (hdv + 31) / 32 * 32;
+    const dim3 grid(a.num_heads * 2, a.rows), block(cons + 32);
+    if (a.head_dim == 64)
+        launch_kernel(attn_softmax_pv_kernel<1, 1, 1, 64, 2>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap_half);
+    else
+        launch_kernel(attn_softmax_pv_kernel<1, 1, 1, 128, 2>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
                       vmap_half);
 }
 
@@ -1429,21 +1494,24 @@ void set_softmax_pv_group_smem(int bytes) {
 
 // The (row, query head) form: one head per CTA, a thread per dim (ND = 1) or
 // per dim pair (ND = 2); kv_mul times the CTAs of the (row, KV head) form.
-template <int ND>
+template <int ND, int TTV = TT_V>
 void launch_softmax_pv_per_head(const AttnArgs &args, const CUtensorMap &vmap, cudaStream_t s) {
     AttnArgs a = args;
-    const FusedShape f = per_head_shape(a);
+    const FusedShape f = per_head_shape(a, TTV);
     // the in-kernel Q8_0 of the output needs whole 32-element blocks per CTA
     const bool q8_after = a.q8_out.qs && a.head_dim % 32 != 0;
     if (q8_after) a.q8_out.qs = nullptr;
     const int cons = (a.head_dim / ND + 31) / 32 * 32;
     const dim3 grid(a.num_heads, a.rows), block(cons + 32);
     if (a.head_dim == 64)
-        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 64>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 64, 1, TTV>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap);
     else if (a.head_dim == 128)
-        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 128>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 128, 1, TTV>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap);
     else
-        launch_kernel(attn_softmax_pv_kernel<1, 1, ND>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst, vmap);
+        launch_kernel(attn_softmax_pv_kernel<1, 1, ND, 0, 1, TTV>, grid, block, f.smem, s, a.pdl, a, f.lp, f.nst,
+                      vmap);
     if (q8_after) launch_quantize_q8x(a.out, a.ldo, a.dim, args.q8_out, a.rows, s);
 }
 
@@ -1474,15 +1542,15 @@ EncodeTiledFn encode_tiled_fn() {
 }  // namespace
 
 bool encode_v_map(CUtensorMap *map, const float *base, int kv_dim, int max_seq,
-                  uint64_t planes, int head_dim) {
+                  uint64_t planes, int head_dim, int box_pos) {
     const EncodeTiledFn fn = encode_tiled_fn();
     if (!fn || !base || ((uintptr_t)base & 15) || (kv_dim & 3) || (head_dim & 3) ||
         head_dim > 256 || head_dim > kv_dim || max_seq <= 0 || planes == 0 ||
-        planes > 0x7fffffffULL)
+        planes > 0x7fffffffULL || box_pos < 1 || box_pos > 256)
         return false;
     const cuuint64_t dims[3] = {(cuuint64_t)kv_dim, (cuuint64_t)max_seq, (cuuint64_t)planes};
     const cuuint64_t strides[2] = {(cuuint64_t)kv_dim * 4, (cuuint64_t)kv_dim * 4 * (cuuint64_t)max_seq};
-    const cuuint32_t box[3] = {(cuuint32_t)head_dim, (cuuint32_t)TT_V, 1};
+    const cuuint32_t box[3] = {(cuuint32_t)head_dim, (cuuint32_t)box_pos, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1530,15 +1598,19 @@ bool attention_fused_ok(const AttnArgs &a) {
     const size_t sk = sizeof(float) * ((size_t)TILE_KEYS * (a.head_dim + 4) + (size_t)kv_mul * a.head_dim);
     // the softmax + PV form that will run: per query head (modes 1, 2) with
     // its smallest ring, or the (row, KV head) forms
-    const size_t spv = (a.pv_per_head == 1 || a.pv_per_head == 2)
+    const int pvm = a.pv_per_head;
+    const size_t spv = (pvm == 1 || pvm == 2 || pvm == 10)
                            ? fused_shape(1, a.head_dim, a.max_len, PV_MIN_STAGES).smem
-                       : a.pv_per_head >= 3 ? fused_shape(kv_mul, a.head_dim, a.max_len, PV_MIN_STAGES).smem
-                                            : fused_shape(kv_mul, a.head_dim, a.max_len).smem;
+                       : pvm == 8             ? fused_shape(1, a.head_dim, a.max_len, PV_MIN_STAGES, 32).smem
+                       : pvm == 9             ? fused_shape(1, a.head_dim, a.max_len, PV_MIN_STAGES, 16).smem
+                       : pvm >= 3             ? fused_shape(kv_mul, a.head_dim, a.max_len, PV_MIN_STAGES).smem
+                                              : fused_shape(kv_mul, a.head_dim, a.max_len).smem;
     return spv <= FUSED_SMEM_MAX && sk <= FUSED_SMEM_MAX;
 }
 
 void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUtensorMap *kmap,
-                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half) {
+                       const CUtensorMap *amap, cudaStream_t s, const CUtensorMap *vmap_half,
+                       const CUtensorMap *vmap_fine) {
     if (args.rows <= 0) return;
     if (args.prefill_tc && attn_prefill_tc_ok(args)) {
         launch_attn_prefill_tc(args, s);
@@ -1632,7 +1704,7 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
         if (a.q8_out.qs) launch_quantize_q8x(a.out, a.ldo, a.dim, a.q8_out, a.rows, s);
         return;
     }
-    if (a.pv_per_head >= 6 && vmap_half && KVM_GROUP_OK(kv_mul) && (a.head_dim == 64 || a.head_dim == 128) &&
+    if ((a.pv_per_head == 6 || a.pv_per_head == 7) && vmap_half && KVM_GROUP_OK(kv_mul) && (a.head_dim == 64 || a.head_dim == 128) &&
         kv_mul * a.head_dim / 2 <= 480) {
         const bool nd2 = a.pv_per_head == 7;
         switch (kv_mul) {
@@ -1650,6 +1722,18 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
             case 3: launch_softmax_pv_group<3>(a, vmap, s); break;
             default: launch_softmax_pv_group<4>(a, vmap, s); break;
         }
+        return;
+    }
+    if (a.pv_per_head == 10 && vmap_half && (a.head_dim == 64 || a.head_dim == 128)) {
+        launch_softmax_pv_per_head_split(a, *vmap_half, s);
+        return;
+    }
+    if ((a.pv_per_head == 8 || a.pv_per_head == 9) && vmap_fine) {
+        // per query head, a thread per dim, 32- or 16-position stages
+        if (a.pv_per_head == 8)
+            launch_softmax_pv_per_head<1, 32>(a, *vmap_fine, s);
+        else
+            launch_softmax_pv_per_head<1, 16>(a, *vmap_fine, s);
         return;
     }
     if (a.pv_per_head) {
@@ -1694,6 +1778,12 @@ void set_attention_smem_limit(int bytes) {
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncSetAttribute(attn_softmax_pv_kernel<1, 1, 2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    for (auto fn : {attn_softmax_pv_kernel<1, 1, 1, 64, 1, 32>, attn_softmax_pv_kernel<1, 1, 1, 128, 1, 32>,
+                    attn_softmax_pv_kernel<1, 1, 1, 0, 1, 32>, attn_softmax_pv_kernel<1, 1, 1, 64, 1, 16>,
+                    attn_softmax_pv_kernel<1, 1, 1, 128, 1, 16>, attn_softmax_pv_kernel<1, 1, 1, 0, 1, 16>})
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     cudaFuncSetAttribute(attn_scores_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

@@ -660,7 +660,9 @@ int check_config(const slm_config *c) {
 // every form gives the same results.
 int env_pv_per_head() {
     const char *env = getenv("SLM_PV_PER_HEAD");
-    return env && env[0] >= '0' && env[0] <= '7' ? env[0] - '0' : 1;
+    if (!env || env[0] < '0' || env[0] > '9') return 1;
+    const int v = atoi(env);
+    return v <= 10 ? v : 1;
 }
 
 AttnArgs attn_args_for(const slm_config *c) {
@@ -780,8 +782,11 @@ SLM_EXPORT int slm_causal_attention_rows(const float *q, const float *k, const f
         cudaStreamSynchronize(st);
         return rc;
     }
+    CUtensorMap vmap_fine;
+    const bool have_vf = encode_v_map(&vmap_fine, v, a.kv_dim, a.max_seq, 1, a.head_dim, V_FINE_POSITIONS);
     if (have_v && attention_fused_ok(a))
-        launch_attn_fused(a, vmap, have_k ? &kmap : nullptr, have_a ? &amap : nullptr, st);
+        launch_attn_fused(a, vmap, have_k ? &kmap : nullptr, have_a ? &amap : nullptr, st, nullptr,
+                          have_vf ? &vmap_fine : nullptr);
     else
         launch_attention(a, have_v ? &vmap : nullptr, have_k ? &kmap : nullptr, st);
     cudaFreeAsync(dpos, st);
@@ -892,6 +897,8 @@ struct slm_model {
     CUtensorMap kmap;        // K planes, swizzled boxes for the scores kernel
     CUtensorMap vmap_half;   // V planes, boxes head_dim / 2 wide (split softmax + PV forms)
     bool have_vmap_half = false;
+    CUtensorMap vmap_fine;   // V planes, V_FINE_POSITIONS-position boxes (fine-stage PV forms)
+    bool have_vmap_fine = false;
     CUtensorMap kmap64;      // K planes, FD_ITEM_KEYS-key boxes for the flash-decode kernel
     bool have_kmap64 = false;
     CUtensorMap amap;        // att scratch, probability tiles of the prefill softmax/PV
@@ -1182,7 +1189,8 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             // scores, then softmax + PV + the Q8_0 of the output
             launch_attn_fused(aa, m->vmap, m->have_kmap ? &m->kmap : nullptr,
                               m->have_amap && row0 == 0 ? &m->amap : nullptr, st,
-                              m->have_vmap_half ? &m->vmap_half : nullptr);
+                              m->have_vmap_half ? &m->vmap_half : nullptr,
+                              m->have_vmap_fine ? &m->vmap_fine : nullptr);
             mark(prof, SLM_PHASE_ATTN_FUSED);
             if (sharded) {
                 // this rank's units -> all ranks: one all-gather before Wo
@@ -1328,7 +1336,7 @@ uint32_t decode_launches(const slm_model *m, int n) {
         pr.rows = n;
         attn = (uint32_t)flash_decode_launches(pr);  // splits (+ the combine, with the Q8_0 of the output)
     } else if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
-        if (m->pv_per_head >= 6 && m->have_vmap_half && kv_mul <= 4 && (m->hd == 64 || m->hd == 128) &&
+        if ((m->pv_per_head == 6 || m->pv_per_head == 7) && m->have_vmap_half && kv_mul <= 4 && (m->hd == 64 || m->hd == 128) &&
             kv_mul * m->hd / 2 <= 480)
             attn = 2;
         else if (m->pv_per_head >= 3 && m->pv_per_head <= 5 && kv_mul <= 4 && kv_mul * m->hd <= 480)
@@ -1605,6 +1613,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
                                 (uint64_t)S * 2 * m->L - 1, m->hd);
     m->have_vmap_half = m->hd % 2 == 0 && encode_v_map(&m->vmap_half, m->kv + m->v_off, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd / 2);
+    m->have_vmap_fine = encode_v_map(&m->vmap_fine, m->kv + m->v_off, m->kvd, (int)cfg->max_seq_len,
+                                     (uint64_t)S * 2 * m->L - 1, m->hd, V_FINE_POSITIONS);
     // K plane (slot, layer) at z = slot*2L + 2*layer from the cache start
     m->have_kmap = encode_k_map(&m->kmap, m->kv, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd);

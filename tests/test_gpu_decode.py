@@ -10,8 +10,9 @@ Exact mode (default) against the CPU oracle, bit for bit:
   then 64 greedy decode steps, sampled sequences against the oracle;
 - the softmax + PV forms (per KV head with a thread per (head, dim pair),
   per (head, dim) or per dim running every head, per (row, KV head, half of
-  head_dim), per query head with a thread per dim or per dim pair, one or
-  four decode parts) give identical results.
+  head_dim), per query head with a thread per dim or per dim pair, with
+  64-, 32- or 16-position V stages, one or four decode parts) give identical
+  results.
 Flash-decode mode (opt-in, split-K) within the north star's tolerance:
 - attention rows against the oracle's attention (1e-3 relative, 1e-4
   absolute), at the config-3 shape near position 4095 and at the Llama-3-8B
@@ -121,7 +122,8 @@ def test_cfg2_32_prompts_prefill16_decode64_match_oracle(cuda):
 
 
 @pytest.mark.parametrize("per_head,parts", [("0", "1"), ("0", "4"), ("1", "4"), ("2", "1"), ("3", "1"),
-                                             ("4", "1"), ("5", "1"), ("6", "1"), ("7", "1")])
+                                             ("4", "1"), ("5", "1"), ("6", "1"), ("7", "1"), ("8", "1"),
+                                             ("9", "1"), ("10", "1")])
 def test_softmax_pv_forms_agree(cuda, per_head, parts):
     """Every form of the exact softmax + PV (and the decode split into parts
     on parallel streams) gives the default form's results bit for bit."""
