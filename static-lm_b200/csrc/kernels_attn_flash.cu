@@ -25,6 +25,8 @@
 // dims t, t+64, .. for the PV).  Every mbarrier wait is bounded.  The two
 // kernels are ordered by the stream (programmatic dependent launch), so the
 // chunk kernel needs no counters or fences of its own.
+#include <cstdlib>
+
 #include "async.cuh"
 #include "attn_rows.cuh"
 #include "kernels.h"
@@ -48,6 +50,29 @@ constexpr int FD_THREADS = FD_CONS + 32;
 #endif
 constexpr int FD_STAGES = SLM_FD_STAGES;
 constexpr int FD_BAR_CONS = 1;         // named barrier of the consumer warps
+constexpr int FD_CLUSTER_MAX = 8;      // splits merged inside a cluster (portable cluster size)
+
+// thread-block cluster helpers: this CTA's rank, the address of a shared
+// variable in CTA `rank` of the cluster, a load from it, and the cluster-wide
+// barrier (every CTA of the cluster arrives once, then all wait)
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned cluster_map(unsigned saddr, unsigned rank) {
+    unsigned r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float cluster_ld(unsigned addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
 
 template <int KVM, int HD>
 struct FdSmem {
@@ -66,8 +91,12 @@ struct FdSmem {
 // output o of every query head kept across chunks (online softmax: when a
 // chunk raises m, l and o are scaled by exp(m_old - m_new)).  With one split
 // the CTA writes the row's output and its Q8_0 directly; otherwise (o, m, l)
-// goes to the partial buffer for the combine kernel.
-template <int KVM, int HD>
+// goes to the partial buffer for the combine kernel -- or, with CL, the
+// splits of a (row, KV head) are one thread-block cluster: each leaves its
+// (o, m, l) in its own shared memory and rank 0 merges them through
+// distributed shared memory (the combine kernel's arithmetic, in the same
+// order) and writes the output and its Q8_0, so no second kernel runs.
+template <int KVM, int HD, bool CL = false>
 __global__ void __launch_bounds__(FD_THREADS)
     attn_flash_decode_kernel(AttnArgs a, int nsplit, const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap) {
@@ -86,8 +115,10 @@ __global__ void __launch_bounds__(FD_THREADS)
     const int nch = (L + FD_KEYS - 1) / FD_KEYS;
     const int cps = (nch + nsplit - 1) / nsplit;  // chunks per split
     const int c0 = sp * cps, c1 = c0 + cps < nch ? c0 + cps : nch;
-    if (c0 >= c1) return;  // CTA-uniform: an empty split (the combine skips it)
-    const int nc = c1 - c0;
+    // CTA-uniform: an empty split (the combine skips it; in a cluster it
+    // takes part with an empty partial)
+    if (!CL && c0 >= c1) return;
+    const int nc = c1 > c0 ? c1 - c0 : 0;
     const int z = (int)((long long)row_slot(a, r) * a.z_slot + a.z_layer);
     constexpr unsigned stage_tx = (unsigned)(SM::k + SM::v);
     constexpr size_t stride = (size_t)KVM * (HD + 2);  // one partial: o[KVM][HD], m[KVM], l[KVM]
@@ -254,7 +285,19 @@ __global__ void __launch_bounds__(FD_THREADS)
             // s_e and s_red are written again only after the next chunk's first barrier
             named_bar_or(FD_BAR_CONS, FD_CONS, false);
         }
-        if (!s_abort) {
+        if constexpr (CL) {
+            // this split's partial, left in this CTA's shared memory
+#pragma unroll
+            for (int h = 0; h < KVM; h++)
+#pragma unroll
+                for (int j = 0; j < DPT; j++) s_o[h * HD + tid + FD_CONS * j] = o[h][j];
+#pragma unroll
+            for (int h = 0; h < KVM; h++)
+                if (tid == h) {
+                    s_red[h] = mrun[h];
+                    s_red[KVM + h] = lrun[h];
+                }
+        } else if (!s_abort) {
             if (nsplit == 1) {
                 float *orow = a.out + (size_t)r * a.ldo + (size_t)g * KVM * HD;
 #pragma unroll
@@ -279,12 +322,44 @@ __global__ void __launch_bounds__(FD_THREADS)
                 for (int h = 0; h < KVM; h++)
 #pragma unroll
                     for (int j = 0; j < DPT; j++) part[h * HD + tid + FD_CONS * j] = o[h][j];
-                if (tid < KVM) {
-                    part[KVM * HD + tid] = mrun[tid];
-                    part[KVM * HD + KVM + tid] = lrun[tid];
-                }
+#pragma unroll
+                for (int h = 0; h < KVM; h++)
+                    if (tid == h) {
+                        part[KVM * HD + h] = mrun[h];
+                        part[KVM * HD + KVM + h] = lrun[h];
+                    }
             }
         }
+    }
+    if constexpr (CL) {
+        __syncthreads();
+        cluster_sync_all();  // every split's partial is in place
+        if (cluster_rank() == 0) {
+            const unsigned o_addr = smem_addr(s_o), r_addr = smem_addr(s_red);
+            float *s_res = reinterpret_cast<float *>(base);  // the ring is no longer read
+            for (int idx = tid; idx < KVM * HD; idx += FD_THREADS) {
+                const int h = idx / HD;
+                float M = -INFINITY;
+                for (int c = 0; c < nsplit; c++) M = fmax_nan(M, cluster_ld(cluster_map(r_addr + 4u * h, c)));
+                float num = 0.0f, den = 0.0f;
+                for (int c = 0; c < nsplit; c++) {
+                    const float w = __expf(cluster_ld(cluster_map(r_addr + 4u * h, c)) - M);
+                    num = __fmaf_rn(w, cluster_ld(cluster_map(o_addr + 4u * idx, c)), num);
+                    den = __fmaf_rn(w, cluster_ld(cluster_map(r_addr + 4u * (KVM + h), c)), den);
+                }
+                const float res = num / den;
+                s_res[idx] = res;
+                if (!s_abort) a.out[(size_t)r * a.ldo + (size_t)g * KVM * HD + idx] = res;
+            }
+            __syncthreads();
+            if (a.q8_out.qs && !s_abort) {
+                const int nbr = a.dim / 32;
+                for (int blk = warp; blk < (KVM * HD) / 32; blk += FD_THREADS / 32)
+                    q8x_store_block(s_res[blk * 32 + lane], a.q8_out,
+                                    (size_t)r * nbr + (size_t)(g * KVM * HD) / 32 + blk, lane);
+            }
+        }
+        cluster_sync_all();  // rank 0 has read every split's shared memory
     }
     pdl_release();
     __syncthreads();
@@ -346,6 +421,14 @@ int sm_count_flash() {
     return sms;
 }
 
+// SLM_FD_CLUSTER: 1 (default) merges 2..8 splits inside a cluster, 2 also caps
+// the splits at 8 to do so, 0 always uses the combine kernel
+int fd_cluster_mode() {
+    const char *e = getenv("SLM_FD_CLUSTER");
+    return e && e[0] >= '0' && e[0] <= '2' ? e[0] - '0' : 1;
+}
+bool fd_cluster(int ns) { return fd_cluster_mode() > 0 && ns > 1 && ns <= FD_CLUSTER_MAX; }
+
 // Splits per (row, KV head): as many as the resident CTA slots allow (one CTA
 // per (row, KV head) when those alone fill the GPU).
 template <int KVM, int HD>
@@ -358,6 +441,7 @@ int fd_splits(const AttnArgs &a) {
     long long ns = units > 0 ? slots / units : 1;
     ns = ns < 1 ? 1 : ns > nchm ? nchm : ns;
     if (ns > a.fd_nch) ns = a.fd_nch;
+    if (fd_cluster_mode() == 2 && ns > FD_CLUSTER_MAX) ns = FD_CLUSTER_MAX;
     return (int)ns;
 }
 
@@ -366,6 +450,11 @@ void launch_fd(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap &vm
     using SM = FdSmem<KVM, HD>;
     const int ns = fd_splits<KVM, HD>(a);
     const dim3 grid((unsigned)ns, (unsigned)a.num_kv_heads, (unsigned)a.rows);
+    if (fd_cluster(ns)) {
+        launch_kernel_cluster(attn_flash_decode_kernel<KVM, HD, true>, grid, dim3(FD_THREADS), SM::total, s, a.pdl,
+                              (unsigned)ns, a, (int)ns, kmap, vmap);
+        return;
+    }
     launch_kernel(attn_flash_decode_kernel<KVM, HD>, grid, dim3(FD_THREADS), SM::total, s, a.pdl, a, (int)ns,
                   kmap, vmap);
     if (ns > 1)
@@ -388,6 +477,8 @@ void launch_fd_hd(const AttnArgs &a, const CUtensorMap &kmap, const CUtensorMap 
 template <int KVM, int HD>
 void set_fd_smem_one() {
     cudaFuncSetAttribute(attn_flash_decode_kernel<KVM, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)FdSmem<KVM, HD>::total);
+    cudaFuncSetAttribute(attn_flash_decode_kernel<KVM, HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)FdSmem<KVM, HD>::total);
 }
 
@@ -419,7 +510,8 @@ int fd_splits_hd(const AttnArgs &a) {
 
 int flash_decode_launches(const AttnArgs &a) {
     const int ns = a.head_dim == 64 ? fd_splits_hd<64>(a) : fd_splits_hd<128>(a);
-    return ns > 1 ? 2 : 1;  // the split kernel, and the combine when there are splits
+    // the split kernel, and the combine when splits are not merged in a cluster
+    return ns > 1 && !fd_cluster(ns) ? 2 : 1;
 }
 
 bool flash_decode_ok(const AttnArgs &a) {

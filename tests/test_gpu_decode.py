@@ -167,8 +167,13 @@ FLASH_CASES = [(576, 9, 3, 4224, 40, 4056), (4096, 32, 8, 8256, 3, 8189), (256, 
                (1024, 8, 8, 1100, 6, 1000)]
 
 
+# SLM_FD_CLUSTER: "1" merges 2..8 splits inside a thread-block cluster (the
+# default), "2" also caps the splits at 8 to do so, "0" always runs the
+# separate combine kernel
+@pytest.mark.parametrize("cluster", ["1", "0", "2"])
 @pytest.mark.parametrize("dim,heads,kvh,T,n,start", FLASH_CASES)
-def test_flash_decode_rows_within_tolerance_of_oracle(cuda, dim, heads, kvh, T, n, start):
+def test_flash_decode_rows_within_tolerance_of_oracle(cuda, dim, heads, kvh, T, n, start, cluster, monkeypatch):
+    monkeypatch.setenv("SLM_FD_CLUSTER", cluster)
     cfg_o = O.Config(dim, 4 * dim, heads, kvh, T, 1e-5)
     cfg_s = Config(dim, 4 * dim, heads, kvh, T, 1e-5)
     kvd = dim // heads * kvh
