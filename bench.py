@@ -1,13 +1,17 @@
 #!/usr/bin/env python3
 """Benchmark of the static-lm hot path on B200: batched greedy decode at the
-SmolLM2-135M shape: 64 independent sequences, KV cache
-pre-filled to 2048 positions from seeded N(0,1), sharded by sequence over N
-GPUs (one process per GPU, no data-path collective, total batch fixed =>
-strong scaling).  One step = one decode step of every sequence: 30 layers of
-RMSNorm+Q8, Wq/Wk/Wv+RoPE+KV append, GQA attention, Wo, SwiGLU FFN, then
-final norm, lm_head and argmax.
+SmolLM2-135M shape: batch 64 of independent sequences,
+KV cache pre-filled to 2048 positions from seeded N(0,1), sharded by sequence
+over N GPUs (one process per GPU, no data-path collective).  By default each
+GPU decodes its own batch of 64 sequences (64*N in the job: weak scaling);
+the same line also times the fixed batch of 64 split over the N GPUs
+(64/N each: strong scaling) under "strong_scaling", and `--scaling strong`
+makes that the headline.  One step = one decode step of every sequence: 30
+layers of RMSNorm+Q8, Wq/Wk/Wv+RoPE+KV append, GQA attention, Wo, SwiGLU
+FFN, then final norm, lm_head and argmax.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--scaling weak|strong]
 
 `--impl reference` times the CPU restatement of the reference's own path
 (oracle/, the reference itself is Rust and cannot be built here) on the
@@ -29,7 +33,7 @@ sys.path.insert(0, os.path.join(ROOT, "static-lm_b200"))
 
 import numpy as np  # noqa: E402
 
-GLOBAL_BATCH = 64
+BATCH = 64  # config 3's batch: per GPU (weak scaling) or for the whole job (strong)
 CTX = 2048
 PREFILL_SEQS, PREFILL_LEN = 8, 4096  # config 5: 8 prompts of 4096 tokens
 DECODE_ROOM = 128  # max_seq_len = 2048 + 128: the steps after the prefilled context
@@ -42,6 +46,8 @@ def parse():
     p.add_argument("--steps", type=int, default=40)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                   help="weak: 64 sequences per GPU (default); strong: 64 sequences over all GPUs")
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU work of the cpu_baseline / reference sample")
@@ -67,13 +73,23 @@ def dist_env():
     return ws, rank, local
 
 
-def workload(n_gpus):
+def global_batch(n_gpus, scaling):
+    return BATCH * n_gpus if scaling == "weak" else BATCH
+
+
+def workload(n_gpus, scaling="weak"):
+    per = BATCH if scaling == "weak" else BATCH // n_gpus
     return {
         "workload": "cfg3: SmolLM2-135M-shaped synthetic Q4_0 model (dim 576, hidden 1536, "
+                    "30 layers, 9/3 heads, vocab 49152), batched greedy decode of independent "
+                    "sequences (batch 64 per GPU: weak scaling)" if scaling == "weak" else
+                    "cfg3: SmolLM2-135M-shaped synthetic Q4_0 model (dim 576, hidden 1536, "
                     "30 layers, 9/3 heads, vocab 49152), batched greedy decode of 64 independent "
-                    "sequences, KV cache pre-filled to 2048 positions from seeded N(0,1)",
-        "global_batch": GLOBAL_BATCH,
+                    "sequences split over the GPUs (strong scaling)",
+        "global_batch": global_batch(n_gpus, scaling),
+        "rows_per_gpu": per,
         "seq_len": CTX,
+        "kv": "KV cache pre-filled to 2048 positions from seeded N(0,1)",
         "max_seq_len": CTX + DECODE_ROOM,
         "parallelism": f"dp{n_gpus} (sequences sharded over GPUs, no collective)",
         "weights": "seeded N(0,0.02) quantized to Q4_0, RMSNorm scales 1.0",
@@ -173,7 +189,8 @@ def first_tokens(seqs_global, vocab):
 
 def shard_sequences(global_batch, world_size, rank):
     """The global sequence ids rank `rank` decodes: contiguous, equal shards
-    (sequences are independent, so no data crosses ranks)."""
+    (sequences are independent, so no data crosses ranks).  Weak scaling
+    passes global_batch = 64 * world_size (64 per rank)."""
     if global_batch % world_size:
         raise SystemExit("global batch must divide by the number of GPUs")
     b = global_batch // world_size
@@ -273,10 +290,10 @@ def run_reference(args):
         # reference decodes its sequences one after another); the 64-sequence
         # step time is that times 64, given apart and marked as scaled
         "ms_per_step": sec_per_tok * 1000.0, "step": "one decode token of one sequence",
-        "ms_per_64_sequence_step_scaled": sec_per_tok * 1000.0 * GLOBAL_BATCH,
+        "ms_per_64_sequence_step_scaled": sec_per_tok * 1000.0 * BATCH,
         "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload(args.gpus),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload(args.gpus, args.scaling),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads,
                          "host_logical_cores": os.cpu_count(), "kind": "port",
                          "sample": f"one sequence decoding at context {CTX}+, "
@@ -306,7 +323,8 @@ def run_ours(args):
                                              device_id=torch.device("cuda", local))
     import static_lm as S
 
-    seqs_global = shard_sequences(GLOBAL_BATCH, ws, rank)
+    GB = global_batch(ws, args.scaling)
+    seqs_global = shard_sequences(GB, ws, rank)
     B = len(seqs_global)
     t_build = time.time()
     cfg, layers, vocab, w = build_weights(args.seed, args.layers)
@@ -359,8 +377,35 @@ def run_ours(args):
     clk = clocks.stop()
     ms = max_ranks(ev0.elapsed_time(ev1))
     ms_per_step = ms / K
-    value = GLOBAL_BATCH * K / (ms / 1000.0)
+    value = GB * K / (ms / 1000.0)
     tokens_dev = out.view(W + K, B).cpu().numpy()
+
+    # ---- strong scaling in the same run: the fixed batch of 64 split over
+    # the N GPUs (64/N rows each: the first of this rank's sequences)
+    strong = None
+    if ws > 1 and args.scaling == "weak" and BATCH % ws == 0:
+        Bs = BATCH // ws
+        seqs, toks, pos = device_state()
+        seqs_s, toks_s, pos_s = seqs[:Bs].clone(), toks[:Bs].clone(), pos[:Bs].clone()
+        outs = torch.zeros((W + K) * Bs, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        model.decode_steps_device(Bs, seqs_s.data_ptr(), toks_s.data_ptr(), pos_s.data_ptr(), W,
+                                  outs.data_ptr(), CTX)
+        stream.synchronize()
+        barrier()
+        sev0, sev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sev0.record(stream)
+        model.decode_steps_device(Bs, seqs_s.data_ptr(), toks_s.data_ptr(), pos_s.data_ptr(), K,
+                                  outs.data_ptr() + W * Bs * 4, CTX + W)
+        sev1.record(stream)
+        stream.synchronize()
+        barrier()
+        sms = max_ranks(sev0.elapsed_time(sev1))
+        strong = {"global_batch": BATCH, "rows_per_gpu": Bs, "value": BATCH * K / (sms / 1000.0),
+                  "unit": "tok/s", "ms_per_step": sms / K, "steps": K, "warmup": W,
+                  "gpu_launches": model.launches_per_decode_step(Bs) * K,
+                  "note": "the fixed batch of 64 sequences split over the GPUs, timed in this run "
+                          "like the headline (device events, max over ranks)"}
 
     # ---- phase profile (same steps, eager launches with events on the model stream)
     seqs, toks, pos = device_state()
@@ -383,7 +428,7 @@ def run_ours(args):
         toks_h = model.decode_batch(seqs_h, toks_h, pos_h)
         pos_h = pos_h + 1
     e2e_s = max_ranks(time.perf_counter() - t0)
-    e2e_value = GLOBAL_BATCH * e2e_steps / e2e_s
+    e2e_value = GB * e2e_steps / e2e_s
 
     # ---- roofline of the dominant kernel(s) (algorithmic bytes / event time)
     Lp = CTX + (prof_steps + 1) / 2.0
@@ -439,7 +484,7 @@ def run_ours(args):
         f_attn_launch_ms = fph["attn_fused"] / prof_steps / layers
         f_achieved = kv_bytes_layer / (f_attn_launch_ms / 1000.0) / 1e9
         flash = {
-            "value": GLOBAL_BATCH * K / (fms / 1000.0), "unit": "tok/s", "ms_per_step": fms / K,
+            "value": GB * K / (fms / 1000.0), "unit": "tok/s", "ms_per_step": fms / K,
             "arithmetic": "split-K flash-decode (64-key chunks, online max / exp sums / PV across a "
                           "CTA's chunks, splits merged by a combine kernel); ~1e-6 relative to the exact "
                           "path; opt-in via slm_model_set_decode_mode",
@@ -535,8 +580,8 @@ def run_ours(args):
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
-        "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload(ws),
+        "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload(ws, args.scaling),
         "roofline": {"bound": "hbm",
                      "kernel": "attention of one layer: attn_scores_pipe_kernel + "
                                "attn_softmax_pv_kernel (+Q8 of the output) over all parts"
@@ -550,12 +595,13 @@ def run_ours(args):
                                "kernel_ms_per_step": attn_ms + gemv_ms},
         "phases_ms_per_step": {k: round(v, 4) for k, v in per_step.items()},
         "dominant_phase": dominant,
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * GLOBAL_BATCH,
-                "d2h_bytes_per_step": 4 * GLOBAL_BATCH,
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12 * GB,
+                "d2h_bytes_per_step": 4 * GB,
                 "api": "slm_model_decode_batch (host token/position arrays in, next tokens out)"},
         "gpu_launches": gpu_launches,
         "clocks": clk,
         "setup_s": round(setup_s, 1),
+        "strong_scaling": strong,
         "flash_decode": flash,
         "prefill": prefill,
     }

@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libslm_b200.so")
 SOURCES = ["kernels_vec.cu", "kernels_gemv.cu", "kernels_attn.cu", "kernels_attn_tc.cu", "kernels_attn_flash.cu",
-           "runtime.cu"]
+           "kernels_attn_cluster.cu", "runtime.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "--fmad=false",
          "-std=c++17", "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden",

@@ -112,6 +112,79 @@ __device__ __forceinline__ void pdl_release() {
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// ---- thread-block clusters -------------------------------------------------
+// This CTA's rank in its cluster, the address of a shared variable in CTA
+// `rank` of the cluster, a load from / a store to such an address, and the
+// cluster-wide barrier.  Every thread of every CTA of the cluster arrives once
+// per barrier phase, then waits; arrive and wait alternate in each thread.
+// The forms without .aligned let the threads of a warp reach them apart.
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned cluster_map(unsigned saddr, unsigned rank) {
+    unsigned r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float cluster_ld(unsigned addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_st(unsigned addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// arrive without ordering (only "this CTA is running"), arrive that publishes
+// this thread's earlier stores, and the wait that sees every arrived thread's
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;\n" ::: "memory"); }
+
+// `count` arrivals on an mbarrier at once.
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Shared-memory loads and stores at 32-bit shared-window addresses
+// (smem_addr): no generic-address conversion per access.  The loads are
+// volatile, so they keep their order with the mbarrier waits (also volatile)
+// that make the data they read ready, while the arithmetic around them is
+// free to move.
+__device__ __forceinline__ float lds_f32(unsigned a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 lds_f32x2(unsigned a) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float4 lds_f32x4(unsigned a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts_f32(unsigned a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void sts_f32x4(unsigned a, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Barrier `id` over `count` threads (whole warps), without a result.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
 // Named barrier `id` over `count` threads (whole warps) that also returns the
 // OR of `pred` over them, so every participant takes the same branch after it.
 __device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {

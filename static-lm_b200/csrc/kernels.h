@@ -233,6 +233,20 @@ int flash_decode_launches(const AttnArgs &a);
 // kmap64: K tensor map with FD_ITEM_KEYS-key boxes (encode_k_map)
 void launch_flash_decode(const AttnArgs &a, const CUtensorMap &kmap64, const CUtensorMap &vmap, cudaStream_t s);
 void set_flash_decode_smem();
+// Exact decode attention in one launch (kernels_attn_cluster.cu): a
+// thread-block cluster of C CTAs per (row, KV head) splits the keys for the
+// scores and the head dims for the PV chains; bit-exact with the two-kernel
+// path.  attn_decode_cluster_size() gives C for these rows (0: the form does
+// not apply -- prefill rows, probabilities asked for, head_dim other than 64
+// or 128, kv_mul above 4, or score rows beyond 96 KB).  kmap32: K tensor map
+// with CL_BOX_KEYS-key boxes; vmap_c: V tensor map with a box of head_dim / C
+// floats x CL_BOX_KEYS * C positions.
+constexpr int CL_BOX_KEYS = 32;
+bool attn_decode_cluster_ok(const AttnArgs &a);
+int attn_decode_cluster_size(const AttnArgs &a);
+void launch_attn_decode_cluster(const AttnArgs &a, const CUtensorMap &kmap32, const CUtensorMap &vmap_c, int C,
+                                cudaStream_t s);
+void set_attn_decode_cluster_smem();
 // Tensor-core causal prefill (kernels_attn_tc.cu): one launch per layer over
 // (128 query rows, query head) tiles, then the Q8_0 of the output when asked.
 bool attn_prefill_tc_ok(const AttnArgs &a);

@@ -1087,9 +1087,22 @@ __global__ void __launch_bounds__(512)
         float m[KVM];
 #pragma unroll
         for (int h = 0; h < KVM; h++) m[h] = -INFINITY;
+        // the maximum of a set does not depend on the order it is taken in:
+        // four independent running maxima per thread
 #pragma unroll
-        for (int h = 0; h < KVM; h++)
-            for (int t = tid; t < L; t += nth) m[h] = cl_fmax(m[h], s_sc[h * lp + t]);
+        for (int h = 0; h < KVM; h++) {
+            const float *row = s_sc + h * lp;
+            float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+            int t = tid;
+            for (; t + 3 * nth < L; t += 4 * nth) {
+                m[h] = cl_fmax(m[h], row[t]);
+                m1 = cl_fmax(m1, row[t + nth]);
+                m2 = cl_fmax(m2, row[t + 2 * nth]);
+                m3 = cl_fmax(m3, row[t + 3 * nth]);
+            }
+            for (; t < L; t += nth) m[h] = cl_fmax(m[h], row[t]);
+            m[h] = cl_fmax(cl_fmax(m[h], m1), cl_fmax(m2, m3));
+        }
 #pragma unroll
         for (int h = 0; h < KVM; h++) {
             for (int o = 16; o > 0; o >>= 1) m[h] = cl_fmax(m[h], __shfl_xor_sync(0xffffffffu, m[h], o));
@@ -1113,13 +1126,16 @@ __global__ void __launch_bounds__(512)
         const float mx = s_red[32 + h];
         float *row = s_sc + h * lp;
         int t = tid;
-        for (; t + nth < L; t += 2 * nth) {
-            const float x0 = row[t], x1 = row[t + nth];
+        for (; t + 3 * nth < L; t += 4 * nth) {
+            const float x0 = row[t], x1 = row[t + nth], x2 = row[t + 2 * nth], x3 = row[t + 3 * nth];
             const float e0 = exp_poly(__fsub_rn(x0, mx)), e1 = exp_poly(__fsub_rn(x1, mx));
+            const float e2 = exp_poly(__fsub_rn(x2, mx)), e3 = exp_poly(__fsub_rn(x3, mx));
             row[t] = e0;
             row[t + nth] = e1;
+            row[t + 2 * nth] = e2;
+            row[t + 3 * nth] = e3;
         }
-        if (t < L) row[t] = exp_poly(__fsub_rn(row[t], mx));
+        for (; t < L; t += nth) row[t] = exp_poly(__fsub_rn(row[t], mx));
     }
     __syncthreads();
     float chain = 0.0f;
@@ -1758,6 +1774,7 @@ void launch_attn_fused(const AttnArgs &args, const CUtensorMap &vmap, const CUte
 void set_attention_smem_limit(int bytes) {
     set_attn_prefill_tc_smem();
     set_flash_decode_smem();
+    set_attn_decode_cluster_smem();
     set_softmax_pv_smem<1>(bytes);
     set_softmax_pv_smem<2>(bytes);
     set_softmax_pv_smem<3>(bytes);

@@ -52,28 +52,6 @@ constexpr int FD_STAGES = SLM_FD_STAGES;
 constexpr int FD_BAR_CONS = 1;         // named barrier of the consumer warps
 constexpr int FD_CLUSTER_MAX = 8;      // splits merged inside a cluster (portable cluster size)
 
-// thread-block cluster helpers: this CTA's rank, the address of a shared
-// variable in CTA `rank` of the cluster, a load from it, and the cluster-wide
-// barrier (every CTA of the cluster arrives once, then all wait)
-__device__ __forceinline__ unsigned cluster_rank() {
-    unsigned r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ unsigned cluster_map(unsigned saddr, unsigned rank) {
-    unsigned r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float cluster_ld(unsigned addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-
 template <int KVM, int HD>
 struct FdSmem {
     static constexpr size_t k = (size_t)(HD / 32) * FD_KEYS * 128;  // swizzled K boxes

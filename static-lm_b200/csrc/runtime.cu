@@ -662,7 +662,7 @@ int env_pv_per_head() {
     const char *env = getenv("SLM_PV_PER_HEAD");
     if (!env || env[0] < '0' || env[0] > '9') return 1;
     const int v = atoi(env);
-    return v <= 10 ? v : 1;
+    return v <= 11 ? v : 1;
 }
 
 AttnArgs attn_args_for(const slm_config *c) {
@@ -901,6 +901,11 @@ struct slm_model {
     bool have_vmap_fine = false;
     CUtensorMap kmap64;      // K planes, FD_ITEM_KEYS-key boxes for the flash-decode kernel
     bool have_kmap64 = false;
+    // exact decode in one cluster launch: K planes with CL_BOX_KEYS-key boxes,
+    // V planes with the box of cluster size 1, 2, 4, 8 (head_dim / C floats x
+    // CL_BOX_KEYS * C positions)
+    CUtensorMap kmap32, vmap_cl[4];
+    bool have_kmap32 = false, have_vmap_cl[4] = {false, false, false, false};
     CUtensorMap amap;        // att scratch, probability tiles of the prefill softmax/PV
     bool have_vmap = false, have_kmap = false, have_amap = false;
     // KV-head-sharded batched prefill (slm_model_attach_shard)
@@ -1064,6 +1069,16 @@ bool gate_up_norm_fused(const slm_model *m, int n) {
            gemv_fuses_norm(2 * (int)m->cfg.hidden_dim, (int)(m->cfg.dim / QK), EPI_SWIGLU_Q8, n);
 }
 
+// Decode attention of the exact mode in one cluster launch (SLM_PV_PER_HEAD
+// 11): the cluster size for these rows, 0 when the form does not apply (the
+// two-kernel forms run then).
+int cl_map_index(int C) { return C == 1 ? 0 : C == 2 ? 1 : C == 4 ? 2 : 3; }
+int decode_cluster(const slm_model *m, const AttnArgs &a) {
+    if (m->pv_per_head != 11 || !m->have_kmap32) return 0;
+    const int C = attn_decode_cluster_size(a);
+    return C > 0 && m->have_vmap_cl[cl_map_index(C)] ? C : 0;
+}
+
 void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, cudaStream_t st,
                      int part, Profiler *prof = nullptr, int seq_rows = 0) {
     const slm_config &c = m->cfg;
@@ -1144,6 +1159,8 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     // output inside the kernel)
     const bool flash = kind == STEP_DECODE && m->decode_mode == SLM_DECODE_FLASH && m->use_fused_attention &&
                        m->have_vmap && m->have_kmap64 && flash_decode_ok(aa);
+    // decode rows of the exact mode: the one-launch cluster form when it applies
+    const int ccl = kind == STEP_DECODE && fused && !flash ? decode_cluster(m, aa) : 0;
     const int n_units = kind == STEP_PREFILL_BATCH && seq_rows > 0 ? (n / seq_rows) * (int)c.num_kv_heads : 0;
     const bool norm_qkv = m->L > 0 && qkv_norm_fused(m, n);
     const bool norm_gu = m->L > 0 && gate_up_norm_fused(m, n);
@@ -1184,6 +1201,10 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             AttnArgs fa = aa;
             fa.q8_out = qb8;
             launch_flash_decode(fa, m->kmap64, m->vmap, st);
+            mark(prof, SLM_PHASE_ATTN_FUSED);
+        } else if (fused && ccl) {
+            // scores, softmax, PV and the Q8_0 of the output in one cluster launch
+            launch_attn_decode_cluster(aa, m->kmap32, m->vmap_cl[cl_map_index(ccl)], ccl, st);
             mark(prof, SLM_PHASE_ATTN_FUSED);
         } else if (fused) {
             // scores, then softmax + PV + the Q8_0 of the output
@@ -1336,7 +1357,11 @@ uint32_t decode_launches(const slm_model *m, int n) {
         pr.rows = n;
         attn = (uint32_t)flash_decode_launches(pr);  // splits (+ the combine, with the Q8_0 of the output)
     } else if (m->use_fused_attention && m->have_vmap && attention_fused_ok(pa)) {
-        if ((m->pv_per_head == 6 || m->pv_per_head == 7) && m->have_vmap_half && kv_mul <= 4 && (m->hd == 64 || m->hd == 128) &&
+        AttnArgs pr = pa;
+        pr.rows = n;
+        if (decode_cluster(m, pr))
+            attn = 1;
+        else if ((m->pv_per_head == 6 || m->pv_per_head == 7) && m->have_vmap_half && kv_mul <= 4 && (m->hd == 64 || m->hd == 128) &&
             kv_mul * m->hd / 2 <= 480)
             attn = 2;
         else if (m->pv_per_head >= 3 && m->pv_per_head <= 5 && kv_mul <= 4 && kv_mul * m->hd <= 480)
@@ -1620,6 +1645,12 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
                                 (uint64_t)S * 2 * m->L - 1, m->hd);
     m->have_kmap64 = encode_k_map(&m->kmap64, m->kv, m->kvd, (int)cfg->max_seq_len,
                                 (uint64_t)S * 2 * m->L - 1, m->hd, FD_ITEM_KEYS);
+    m->have_kmap32 = encode_k_map(&m->kmap32, m->kv, m->kvd, (int)cfg->max_seq_len,
+                                  (uint64_t)S * 2 * m->L - 1, m->hd, CL_BOX_KEYS);
+    for (int i = 0; i < 4; i++)
+        m->have_vmap_cl[i] = m->hd % (4 << i) == 0 &&
+                             encode_v_map(&m->vmap_cl[i], m->kv + m->v_off, m->kvd, (int)cfg->max_seq_len,
+                                          (uint64_t)S * 2 * m->L - 1, m->hd >> i, CL_BOX_KEYS << i);
     m->have_amap = encode_att_map(&m->amap, m->att, (int)cfg->max_seq_len, (int)cfg->num_heads,
                                   (uint64_t)R, (int)(cfg->num_heads / cfg->num_kv_heads));
     *out = m;

@@ -121,12 +121,29 @@ def test_cfg2_32_prompts_prefill16_decode64_match_oracle(cuda):
         o.close()
 
 
-@pytest.mark.parametrize("per_head,parts", [("0", "1"), ("0", "4"), ("1", "4"), ("2", "1"), ("3", "1"),
-                                             ("4", "1"), ("5", "1"), ("6", "1"), ("7", "1"), ("8", "1"),
-                                             ("9", "1"), ("10", "1")])
-def test_softmax_pv_forms_agree(cuda, per_head, parts):
+@pytest.mark.parametrize("per_head,parts,cluster", [
+    ("0", "1", ""), ("0", "4", ""), ("1", "4", ""), ("2", "1", ""), ("3", "1", ""), ("4", "1", ""), ("5", "1", ""),
+    ("6", "1", ""), ("7", "1", ""), ("8", "1", ""), ("9", "1", ""), ("10", "1", ""),
+    ("11", "1", ""), ("11", "4", ""), ("11", "1", "1"), ("11", "1", "2"), ("11", "1", "8"), ("11", "4", "2"),
+    ("11", "1", "1,nd2"), ("11", "1", "2,nh1"), ("11", "4", "8,nha"), ("11", "4", "8,pm1"), ("11", "1", "2,pm1"),
+    ("11", "1", "1,pm1"), ("11", "4", "4,pm0")])
+def test_softmax_pv_forms_agree(cuda, per_head, parts, cluster, monkeypatch):
     """Every form of the exact softmax + PV (and the decode split into parts
-    on parallel streams) gives the default form's results bit for bit."""
+    on parallel streams) gives the default form's results bit for bit.  Form
+    11 is the one-launch cluster kernel: `cluster` forces its cluster size
+    (SLM_CLUSTER_C; "" = the size it picks: 4 at 32 rows, 8 at 8 rows per
+    part), two PV chains per thread (SLM_CLUSTER_ND=2), one or every head
+    per PV thread (SLM_CLUSTER_NH), and the products form on or off
+    (SLM_CLUSTER_PM)."""
+    c, _, opt = cluster.partition(",")
+    if c:
+        monkeypatch.setenv("SLM_CLUSTER_C", c)
+    if opt == "nd2":
+        monkeypatch.setenv("SLM_CLUSTER_ND", "2")
+    elif opt in ("nh1", "nha"):
+        monkeypatch.setenv("SLM_CLUSTER_NH", "1" if opt == "nh1" else "all")
+    elif opt in ("pm0", "pm1"):
+        monkeypatch.setenv("SLM_CLUSTER_PM", opt[2])
     cfg, _, vocab = synth.config("cfg3", max_seq_len=600)
     w = synth.synth_model(cfg, 2, vocab, seed=13)
     B = 32

@@ -72,6 +72,21 @@ def test_shards_partition_the_batch():
         bench.shard_sequences(GLOBAL, 4, 0)
 
 
+def test_weak_and_strong_batches():
+    """Weak scaling (the bench's default) gives every rank its own batch of
+    64 sequences, strong scaling splits the 64 over the ranks; either way the
+    shards are disjoint and cover the job's batch."""
+    for world in (1, 2, 4, 8):
+        for scaling, per in (("weak", 64), ("strong", 64 // world)):
+            gb = bench.global_batch(world, scaling)
+            shards = [bench.shard_sequences(gb, world, r) for r in range(world)]
+            assert all(len(sh) == per for sh in shards)
+            flat = sorted(g for sh in shards for g in sh)
+            assert flat == list(range(gb))
+            cfgd = bench.workload(world, scaling)
+            assert cfgd["global_batch"] == gb and cfgd["rows_per_gpu"] == per
+
+
 def test_two_gloo_ranks_decode_their_shards_like_one_process():
     world = 2
     ctx = mp.get_context("spawn")
