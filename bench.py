@@ -61,6 +61,9 @@ def parse():
     p.add_argument("--layers", type=int, default=None,
                    help="profiling case only: fewer layers (same per-kernel shapes); the "
                         "line is then marked as not a bench value")
+    p.add_argument("--batch", type=int, default=BATCH,
+                   help="profiling case only: sequences per GPU (weak) or in the job (strong); "
+                        "the line is then marked as not a bench value")
     p.add_argument("--prefill-seqs", type=int, default=PREFILL_SEQS,
                    help="profiling case only: prompts of the prefill leg (default 8)")
     return p.parse_args()
@@ -73,8 +76,8 @@ def dist_env():
     return ws, rank, local
 
 
-def global_batch(n_gpus, scaling):
-    return BATCH * n_gpus if scaling == "weak" else BATCH
+def global_batch(n_gpus, scaling, batch=BATCH):
+    return batch * n_gpus if scaling == "weak" else batch
 
 
 def workload(n_gpus, scaling="weak"):
@@ -323,7 +326,7 @@ def run_ours(args):
                                              device_id=torch.device("cuda", local))
     import static_lm as S
 
-    GB = global_batch(ws, args.scaling)
+    GB = global_batch(ws, args.scaling, args.batch)
     seqs_global = shard_sequences(GB, ws, rank)
     B = len(seqs_global)
     t_build = time.time()
@@ -608,10 +611,12 @@ def run_ours(args):
     if cpu:
         line["cpu_baseline"] = cpu
         line["cpu_parity_tokens_equal"] = parity
-    if args.layers or args.prefill_seqs != PREFILL_SEQS:
+    if args.layers or args.prefill_seqs != PREFILL_SEQS or args.batch != BATCH:
         line["config"]["layers"] = layers
         line["config"]["prefill_seqs"] = args.prefill_seqs
-        line["note"] = "profiling case (fewer layers or prompts): not a bench value"
+        line["config"]["global_batch"] = GB
+        line["config"]["rows_per_gpu"] = len(seqs_global)
+        line["note"] = "profiling case (fewer layers, prompts or sequences): not a bench value"
     if rank == 0:
         print(json.dumps(line), flush=True)
     if model is not None:

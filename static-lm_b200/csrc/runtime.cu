@@ -656,13 +656,21 @@ int check_config(const slm_config *c) {
 }
 
 // Softmax + PV form of the exact attention (AttnArgs::pv_per_head): one CTA
-// per (row, query head) unless SLM_PV_PER_HEAD says otherwise (0, 1 or 2);
-// every form gives the same results.
+// per (row, query head) unless SLM_PV_PER_HEAD says otherwise (0 .. 11);
+// every form gives the same results.  Unset, decode steps of at most
+// CLUSTER_AUTO_ROWS rows (per part) use the one-launch cluster form (11),
+// measured faster there (31.4 against 33.7 us per layer at 8 rows of
+// config 3) and slower from 16 rows.
+constexpr int CLUSTER_AUTO_ROWS = 8;
 int env_pv_per_head() {
     const char *env = getenv("SLM_PV_PER_HEAD");
     if (!env || env[0] < '0' || env[0] > '9') return 1;
     const int v = atoi(env);
     return v <= 11 ? v : 1;
+}
+bool env_pv_form_auto() {
+    const char *env = getenv("SLM_PV_PER_HEAD");
+    return !env || env[0] < '0' || env[0] > '9';
 }
 
 AttnArgs attn_args_for(const slm_config *c) {
@@ -888,6 +896,7 @@ struct slm_model {
     bool gemm_tc = true;     // SLM_PREFILL_GEMM_EXACT=1: tensor-core prefill mode keeps exact projections
     int parts = 1;           // decode parts (streams) for batches of 16+ rows
     int pv_per_head = 1;     // softmax + PV per (row, query head): AttnArgs::pv_per_head
+    bool pv_form_auto = true;  // SLM_PV_PER_HEAD unset: small decode steps take the cluster form
     int decode_mode = SLM_DECODE_EXACT;  // slm_model_set_decode_mode
     float *fd_part = nullptr;  // flash-decode partials [R][kvh][fd_nch][kv_mul*(hd+2)]
     int fd_nch = 0;
@@ -1074,7 +1083,8 @@ bool gate_up_norm_fused(const slm_model *m, int n) {
 // two-kernel forms run then).
 int cl_map_index(int C) { return C == 1 ? 0 : C == 2 ? 1 : C == 4 ? 2 : 3; }
 int decode_cluster(const slm_model *m, const AttnArgs &a) {
-    if (m->pv_per_head != 11 || !m->have_kmap32) return 0;
+    const bool want = m->pv_per_head == 11 || (m->pv_form_auto && a.rows <= CLUSTER_AUTO_ROWS);
+    if (!want || !m->have_kmap32) return 0;
     const int C = attn_decode_cluster_size(a);
     return C > 0 && m->have_vmap_cl[cl_map_index(C)] ? C : 0;
 }
@@ -1622,6 +1632,7 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     env = getenv("SLM_DECODE_ONE_STREAM");
     m->split_decode = !(env && env[0] == '1');
     m->pv_per_head = env_pv_per_head();
+    m->pv_form_auto = env_pv_form_auto();
     env = getenv("SLM_DECODE_PARTS");
     if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
     env = getenv("SLM_PREFILL_GEMM_EXACT");
