@@ -556,25 +556,26 @@ def run_ours(args):
             return nxt, max_ranks(pev0.elapsed_time(pev1))
 
         first, pms = timed_prefill()
-        tc = None
-        if ws == 1:
-            # the opt-in tensor-core mode (3xTF32; not bit-exact) on the same prompts
-            exact_logits = pm.logits(0)
-            pm.set_prefill_mode(True)
-            first_tc, pms_tc = timed_prefill()
-            tc = {"value": nps * PREFILL_LEN / (pms_tc / 1000.0), "unit": "tok/s", "ms": pms_tc,
-                  "arithmetic": "QK^T and PV on tcgen05 (kind::tf32, 3xTF32 split), opt-in via "
-                                "slm_model_set_prefill_mode; not bit-exact",
-                  # Q8_0 quantization after every attention can turn the mode's ~1e-6
-                  # differences into one-step int8 changes, so near-ties may flip
-                  "first_tokens_equal_to_exact": sum(int(x) == int(y) for x, y in zip(first_tc, first)),
-                  "of_prompts": len(first),
-                  "max_abs_logit_diff_prompt0": float(np.abs(pm.logits(0) - exact_logits).max())}
+        # the opt-in tensor-core mode (3xTF32; not bit-exact) on the same
+        # prompts, on every rank (the same collectives in the same order)
+        exact_logits = pm.logits(0)
+        pm.set_prefill_mode(True)
+        first_tc, pms_tc = timed_prefill()
+        tc = {"value": nps * PREFILL_LEN / (pms_tc / 1000.0), "unit": "tok/s", "ms": pms_tc,
+              "arithmetic": "QK^T and PV on tcgen05 (kind::tf32, 3xTF32 split), opt-in via "
+                            "slm_model_set_prefill_mode; not bit-exact",
+              # Q8_0 quantization after every attention can turn the mode's ~1e-6
+              # differences into one-step int8 changes, so near-ties may flip
+              "first_tokens_equal_to_exact": sum(int(x) == int(y) for x, y in zip(first_tc, first)),
+              "of_prompts": len(first),
+              "first_tokens": [int(t) for t in first_tc[:4]],
+              "max_abs_logit_diff_prompt0": float(np.abs(pm.logits(0) - exact_logits).max())}
         prefill = {"value": nps * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
                    "ms": pms, "workload": f"{nps} prompts x {PREFILL_LEN} tokens, "
                    "SmolLM2-135M shape, batched causal prefill to the first greedy token",
-                   "sharding": (f"(sequence, KV head) units over {ws} ranks, one NCCL "
-                                "all-gather of attention outputs per layer before Wo")
+                   "sharding": (f"(sequence, KV head) units over {ws} ranks, one NCCL all-gather of "
+                                "attention outputs per layer before Wo; Wo, RMSNorm and FFN row-sharded "
+                                "with one in-place NCCL all-gather of the residual rows per layer")
                    if ws > 1 else "one GPU",
                    "first_tokens": [int(t) for t in first[:4]],
                    "arithmetic": "bit-exact f32 chains on the CUDA cores (default mode)",

@@ -150,6 +150,10 @@ struct GemvArgs {
     // batches of 128+ rows without the fused RMSNorm prologue; ~1e-7
     // relative to the exact result instead of bit for bit
     bool tc;
+    // with tc: also below 128 rows (a row-sharded slice of a step whose
+    // whole batch takes the tensor cores, so that every rank computes its
+    // rows with the arithmetic the unsharded step uses)
+    bool tc_any_batch;
 };
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
 // Whether launch_gemv stages whole weight tiles for this shape (and can then

@@ -775,7 +775,7 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
     const int total_tiles = (a.rows + TILE_ROWS - 1) / TILE_ROWS;
     const int units = units_of(a.rows, EPI);
     const bool norm = a.nx != nullptr;
-    if (a.tc && !norm && a.batch >= TC_MIN_BATCH) {
+    if (a.tc && !norm && (a.batch >= TC_MIN_BATCH || a.tc_any_batch)) {
         launch_tc<EPI>(a, total_tiles, s);
         return;
     }

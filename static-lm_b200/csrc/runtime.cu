@@ -897,6 +897,7 @@ struct slm_model {
     int parts = 1;           // decode parts (streams) for batches of 16+ rows
     int pv_per_head = 1;     // softmax + PV per (row, query head): AttnArgs::pv_per_head
     bool pv_form_auto = true;  // SLM_PV_PER_HEAD unset: small decode steps take the cluster form
+    bool shard_ffn = true;     // sharded prefill: Wo / FFN row-sharded (SLM_SHARD_FFN=0: replicated)
     int decode_mode = SLM_DECODE_EXACT;  // slm_model_set_decode_mode
     float *fd_part = nullptr;  // flash-decode partials [R][kvh][fd_nch][kv_mul*(hd+2)]
     int fd_nch = 0;
@@ -1035,6 +1036,14 @@ int upload_f32(slm_model *m, const float *src, uint64_t n, uint64_t *cursor, flo
 }
 
 Q8X q8view(void *p, uint64_t blocks) { return q8x_view(p, blocks); }
+// The rows from row0 of a Q8X view with nb blocks per row.
+Q8X q8rows(Q8X v, size_t row0, int nb) {
+    const size_t b0 = row0 * (size_t)nb;
+    v.qs += b0 * 32;
+    v.c += b0 * 8;
+    v.d += b0;
+    return v;
+}
 
 // Records an event on the model stream at every phase boundary; the interval
 // since the previous mark is attributed to the phase passed to mark().
@@ -1149,6 +1158,12 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
     // a batched prefill on a sharded model computes only this rank's
     // (sequence, KV head) units, then all-gathers the outputs before Wo
     const bool sharded = kind == STEP_PREFILL_BATCH && m->shard_n > 1 && fused;
+    // ... and its Wo, RMSNorm and FFN row-sharded: this rank computes rows
+    // [rs0, rs0 + ns) and one in-place all-gather of x per layer gives every
+    // rank all rows for the next layer's QKV (rows are independent, so the
+    // values are those of the unsharded step)
+    const bool row_shard = sharded && m->shard_ffn && n % m->shard_n == 0;
+    const int ns = row_shard ? n / m->shard_n : n, rs0 = row_shard ? m->shard_r * ns : 0;
     // prefill rows are runs of consecutive positions of one sequence
     aa.prefill_run = kind == STEP_PREFILL ? n : kind == STEP_PREFILL_BATCH ? seq_rows : 0;
     if (m->no_prefill_tiles) aa.prefill_run = 0;
@@ -1241,7 +1256,7 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
                                     seq_rows, st);
             }
             if (!aa.q8_out.qs) {
-                launch_quantize_q8x(xb, d, d, qb8, n, st);
+                launch_quantize_q8x(xb + (size_t)rs0 * d, d, d, q8rows(qb8, rs0, d / QK), ns, st);
                 mark(prof, SLM_PHASE_QUANTIZE);
             }
         } else {
@@ -1254,45 +1269,50 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
             launch_quantize_q8x(xb, d, d, qb8, n, st);
             mark(prof, SLM_PHASE_QUANTIZE);
         }
-        // Wo + residual (transformer.rs:445-446)
+        // Wo + residual (transformer.rs:445-446), this rank's rows when
+        // row-sharded (rs0 = 0, ns = n otherwise)
+        const size_t ro = (size_t)rs0 * d;
         g = GemvArgs{};
         g.w = ld.wo.tiles;
         g.rows = d;
         g.nb = d / QK;
-        g.x = qb8;
-        g.batch = n;
+        g.x = q8rows(qb8, rs0, d / QK);
+        g.batch = ns;
         g.epi = EPI_RESIDUAL;
-        g.out = x_mid;
+        g.out = x_mid + ro;
         g.ld_out = d;
-        g.res = x;
+        g.res = x + ro;
         g.ld_res = d;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
         g.tc = gemm_tc;
+        g.tc_any_batch = row_shard && n >= 128;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_WO);
         // rmsnorm(x_mid) -> gate/up -> SwiGLU -> Q8 (transformer.rs:448-475)
         g = GemvArgs{};
         if (norm_gu) {
-            g.nx = x_mid;
+            g.nx = x_mid + ro;
             g.ld_nx = d;
             g.nw = ld.rms_ffn;
             g.eps = c.rms_eps;
             g.inv_n = inv_d;
         } else {
-            launch_rmsnorm_q8(x_mid, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, qa8, n, st, m->use_pdl);
+            launch_rmsnorm_q8(x_mid + ro, d, ld.rms_ffn, d, c.rms_eps, nullptr, 0, q8rows(qa8, rs0, d / QK), ns, st,
+                              m->use_pdl);
             mark(prof, SLM_PHASE_RMSNORM);
         }
         g.w = ld.wgu.tiles;
         g.rows = 2 * h;
         g.nb = d / QK;
-        g.x = qa8;
-        g.batch = n;
+        g.x = q8rows(qa8, rs0, d / QK);
+        g.batch = ns;
         g.epi = EPI_SWIGLU_Q8;
-        g.q8_out = qb8;
+        g.q8_out = q8rows(qb8, rs0, h / QK);
         g.err = m->d_err;
         g.pdl = m->use_pdl;
         g.tc = gemm_tc;
+        g.tc_any_batch = row_shard && n >= 128;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_GATE_UP);
         // down + residual (transformer.rs:477-486)
@@ -1300,18 +1320,29 @@ void enqueue_forward(slm_model *m, int row0, int n, int max_len, StepKind kind, 
         g.w = ld.wdown.tiles;
         g.rows = d;
         g.nb = h / QK;
-        g.x = qb8;
-        g.batch = n;
+        g.x = q8rows(qb8, rs0, h / QK);
+        g.batch = ns;
         g.epi = EPI_RESIDUAL;
-        g.out = x;
+        g.out = x + ro;
         g.ld_out = d;
-        g.res = x_mid;
+        g.res = x_mid + ro;
         g.ld_res = d;
         g.err = m->d_err;
         g.pdl = m->use_pdl;
         g.tc = gemm_tc;
+        g.tc_any_batch = row_shard && n >= 128;
         launch_gemv(g, st);
         mark(prof, SLM_PHASE_DOWN);
+        if (row_shard && m->comm && m->comm_rc == SLM_OK) {
+            // every rank's rows of x to every rank (in place: this rank's rows
+            // are already at their offset in x)
+            const ncclResult_t r = nccl_api().all_gather(x + ro, x, (size_t)ns * d, ncclFloat32, m->comm, st);
+            const int rc = comm_settle(m, r, "ncclAllGather");
+            if (rc != SLM_OK) {
+                m->comm_rc = rc;
+                m->comm_msg = g_err;
+            }
+        }
     }
     if (kind == STEP_EMBED) return;
     // final RMSNorm + lm_head + argmax (transformer.rs:776-794 / 835-853)
@@ -1633,6 +1664,8 @@ SLM_EXPORT int slm_model_create(int device, const slm_config *cfg, const slm_mod
     m->split_decode = !(env && env[0] == '1');
     m->pv_per_head = env_pv_per_head();
     m->pv_form_auto = env_pv_form_auto();
+    env = getenv("SLM_SHARD_FFN");
+    m->shard_ffn = !(env && env[0] == '0');
     env = getenv("SLM_DECODE_PARTS");
     if (env && env[0] >= '1' && env[0] <= '0' + slm_model::MAX_PARTS) m->parts = env[0] - '0';
     env = getenv("SLM_PREFILL_GEMM_EXACT");
