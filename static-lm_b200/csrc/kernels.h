@@ -248,6 +248,11 @@ void set_flash_decode_smem();
 constexpr int CL_BOX_KEYS = 32;
 bool attn_decode_cluster_ok(const AttnArgs &a);
 int attn_decode_cluster_size(const AttnArgs &a);
+// Whether the cluster form is the faster exact form for these rows: its
+// products PV applies and fits three ring stages within the CTA's share of an
+// SM (measured faster than the two-kernel form at 8 rows of config 3, slower
+// where a second wave or the per-head form's PV would be needed).
+bool attn_decode_cluster_preferred(const AttnArgs &a);
 void launch_attn_decode_cluster(const AttnArgs &a, const CUtensorMap &kmap32, const CUtensorMap &vmap_c, int C,
                                 cudaStream_t s);
 void set_attn_decode_cluster_smem();

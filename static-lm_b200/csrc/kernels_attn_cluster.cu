@@ -662,7 +662,12 @@ bool cl_pm(const AttnArgs &a, int C) {
         want = ctas <= 2LL * sm_count_cached();
     }
     if (!want) return false;
-    return cl_shape(kvm, hd, a.max_len, 3, cl_prod_floats(kvm, hd, C)).smem <= CL_SMEM_CTA;
+    // three ring stages within this CTA's share of the SM (the grid in one wave)
+    const long long ctas = (long long)a.rows * a.num_kv_heads * C;
+    const long long per_sm = (ctas + sm_count_cached() - 1) / sm_count_cached();
+    const size_t share = CL_SMEM_SM / (size_t)(per_sm < 1 ? 1 : per_sm);
+    const size_t need = cl_shape(kvm, hd, a.max_len, 3, cl_prod_floats(kvm, hd, C)).smem;
+    return need <= CL_SMEM_CTA && need <= share;
 }
 
 int cl_env_nd() {
@@ -720,6 +725,11 @@ void cl_set_smem() {
 }
 
 }  // namespace
+
+bool attn_decode_cluster_preferred(const AttnArgs &a) {
+    const int C = attn_decode_cluster_size(a);
+    return C > 0 && cl_pm(a, C);
+}
 
 void launch_attn_decode_cluster(const AttnArgs &a, const CUtensorMap &kmap32, const CUtensorMap &vmap_c, int C,
                                 cudaStream_t s) {

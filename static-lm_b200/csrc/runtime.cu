@@ -658,9 +658,10 @@ int check_config(const slm_config *c) {
 // Softmax + PV form of the exact attention (AttnArgs::pv_per_head): one CTA
 // per (row, query head) unless SLM_PV_PER_HEAD says otherwise (0 .. 11);
 // every form gives the same results.  Unset, decode steps of at most
-// CLUSTER_AUTO_ROWS rows (per part) use the one-launch cluster form (11),
-// measured faster there (31.4 against 33.7 us per layer at 8 rows of
-// config 3) and slower from 16 rows.
+// CLUSTER_AUTO_ROWS rows (per part) use the one-launch cluster form (11)
+// where attn_decode_cluster_preferred() says it fits (measured 30.9 against
+// 34.2 us per layer at 8 rows of config 3; slower from 16 rows, and where its
+// shared memory would leave the grid a second wave).
 constexpr int CLUSTER_AUTO_ROWS = 8;
 int env_pv_per_head() {
     const char *env = getenv("SLM_PV_PER_HEAD");
@@ -1092,7 +1093,8 @@ bool gate_up_norm_fused(const slm_model *m, int n) {
 // two-kernel forms run then).
 int cl_map_index(int C) { return C == 1 ? 0 : C == 2 ? 1 : C == 4 ? 2 : 3; }
 int decode_cluster(const slm_model *m, const AttnArgs &a) {
-    const bool want = m->pv_per_head == 11 || (m->pv_form_auto && a.rows <= CLUSTER_AUTO_ROWS);
+    const bool want = m->pv_per_head == 11 ||
+                      (m->pv_form_auto && a.rows <= CLUSTER_AUTO_ROWS && attn_decode_cluster_preferred(a));
     if (!want || !m->have_kmap32) return 0;
     const int C = attn_decode_cluster_size(a);
     return C > 0 && m->have_vmap_cl[cl_map_index(C)] ? C : 0;
