@@ -555,6 +555,28 @@ def run_ours(args):
             pstream.synchronize()
             return nxt, max_ranks(pev0.elapsed_time(pev1))
 
+        # algorithmic work of the prefill: causal attention (QK^T and PV, a
+        # multiply and an add per element, over keys 0..t of every query t and
+        # head) and the projections (two operations per weight and row)
+        hd_p = pcfg.dim // pcfg.num_heads
+        attn_flop = layers * nps * pcfg.num_heads * 4.0 * hd_p * PREFILL_LEN * (PREFILL_LEN + 1) / 2
+        kvd_p = hd_p * pcfg.num_kv_heads
+        params = pcfg.dim * (pcfg.dim + 2 * kvd_p) + pcfg.dim * pcfg.dim + 3 * pcfg.dim * pcfg.hidden_dim
+        proj_flop = layers * nps * PREFILL_LEN * 2.0 * params
+        bf16_peak = peaks.get("bf16_tflops")
+        tensor_peak = bf16_peak or 1590.0
+
+        def prefill_roofline(ms):
+            achieved = (attn_flop + proj_flop) / (ms / 1000.0) / 1e12
+            return {"bound": "tensor", "achieved": achieved, "peak": tensor_peak, "unit": "TFLOP/s",
+                    "frac": achieved / tensor_peak,
+                    "peak_source": "of measured (dense bf16 burst)" if bf16_peak else "of fallback",
+                    "flop_per_prefill": attn_flop + proj_flop, "attention_flop": attn_flop,
+                    "projection_flop": proj_flop,
+                    "note": "algorithmic operations over the whole prefill time; the exact mode "
+                            "runs on the CUDA cores, the tensor-core mode computes attention as "
+                            "3xTF32 (three tf32 MMAs per product) and the projections as int8 MMAs"}
+
         first, pms = timed_prefill()
         # the opt-in tensor-core mode (3xTF32; not bit-exact) on the same
         # prompts, on every rank (the same collectives in the same order)
@@ -569,6 +591,7 @@ def run_ours(args):
               "first_tokens_equal_to_exact": sum(int(x) == int(y) for x, y in zip(first_tc, first)),
               "of_prompts": len(first),
               "first_tokens": [int(t) for t in first_tc[:4]],
+              "roofline": prefill_roofline(pms_tc),
               "max_abs_logit_diff_prompt0": float(np.abs(pm.logits(0) - exact_logits).max())}
         prefill = {"value": nps * PREFILL_LEN / (pms / 1000.0), "unit": "tok/s",
                    "ms": pms, "workload": f"{nps} prompts x {PREFILL_LEN} tokens, "
@@ -579,6 +602,7 @@ def run_ours(args):
                    if ws > 1 else "one GPU",
                    "first_tokens": [int(t) for t in first[:4]],
                    "arithmetic": "bit-exact f32 chains on the CUDA cores (default mode)",
+                   "roofline": prefill_roofline(pms),
                    "tensor_cores": tc}
         pm.close()
 
