@@ -444,6 +444,128 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS, BT > 1 ? 2 : 1)
 }
 
 // ---------------------------------------------------------------------------
+// Batch-1 GEMV of wide matrices (nb >= SPLIT_MIN_NB blocks per row): one CTA
+// per unit (RPT weight tiles), eight warps.  The reference's order fixes only
+// the eight chains acc_k = fma(dw*da, isum_k, acc_k) over the blocks of a row;
+// the int8 dot sums isum_k and the scale products dw*da of different blocks
+// are independent.  So, in rounds of SPLIT_ROUND / RPT blocks, every warp forms
+// them for eight blocks of the round -- its weight blocks straight from HBM,
+// one 16-byte load per lane (row) and block, all eight in flight at once, the
+// next round's loaded while warp 0 works -- into shared memory as the exact
+// f32 values block_dot uses, and warp 0 then runs its lane's eight FMA chains
+// through the round in block order.  Same values, same order: bit-exact.
+constexpr int SPLIT_MIN_NB = 64;
+constexpr int SPLIT_ROUND = 64;            // blocks per round for one tile: 8 per warp
+constexpr int SPLIT_WB = SPLIT_ROUND / 8;  // blocks a warp forms per round (and tile)
+
+// the activation row (68 B a block) and one round's dot sums and scales
+// (SPLIT_ROUND blocks x 32 rows x 9 floats, whatever the tiles per unit)
+__host__ __device__ inline size_t split_smem(int nb) {
+    return (((size_t)nb * 68 + 15) & ~(size_t)15) + (size_t)SPLIT_ROUND * 32 * 9 * 4 + 16;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(256) gemv_split_kernel(GemvArgs a, int total_tiles) {
+    constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
+    constexpr int R = SPLIT_ROUND / RPT;  // blocks per round
+    constexpr int WB = R / 8;             // blocks per warp and round
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int nb = a.nb;
+    int8_t *s_qs = (int8_t *)smem;                       // [nb][32]
+    int32_t *s_c = (int32_t *)(smem + (size_t)nb * 32);  // [nb][8]
+    float *s_d = (float *)(smem + (size_t)nb * 64);      // [nb]
+    // [RPT][R][8][32]: f32 of isum_k per (tile, block of the round, k, lane)
+    float *s_f = (float *)(smem + (((size_t)nb * 68 + 15) & ~(size_t)15));
+    float *s_s = s_f + (size_t)RPT * R * 8 * 32;         // [RPT][R][32]: dw*da
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int tile[RPT];
+    tile[0] = blockIdx.x;
+    if (RPT == 2) tile[RPT - 1] = blockIdx.x + total_tiles / 2;
+
+    // this warp's weight blocks of a round: nibbles and scale of row `lane`
+    uint4 wq[RPT][WB];
+    unsigned short ws[RPT][WB];
+    auto load_w = [&](int r0) {
+#pragma unroll
+        for (int u = 0; u < WB; u++) {
+            const int j = r0 + warp * WB + u;
+#pragma unroll
+            for (int t = 0; t < RPT; t++) {
+                if (j < nb) {
+                    const uint8_t *tp = a.w + tile_offset((size_t)tile[t], nb, j);
+                    wq[t][u] = __ldg(reinterpret_cast<const uint4 *>(tp + lane * 16));
+                    ws[t][u] = __ldg(reinterpret_cast<const unsigned short *>(tp + 512 + lane * 2));
+                }
+            }
+        }
+    };
+    load_w(0);  // constant data: in flight while the previous kernel finishes
+    pdl_wait();  // the activation row is the previous kernel's output
+    for (int i = threadIdx.x; i < nb * 4; i += blockDim.x) {
+        const int j = i >> 2, part = i & 3;
+        void *dst = part < 2 ? (void *)(s_qs + j * 32 + part * 16) : (void *)(s_c + j * 8 + (part - 2) * 4);
+        const void *src = part < 2 ? (const void *)(a.x.qs + (size_t)j * 32 + part * 16)
+                                   : (const void *)(a.x.c + (size_t)j * 8 + (part - 2) * 4);
+        cp_async16(dst, src);
+    }
+    cp_async_commit();
+    for (int j = threadIdx.x; j < nb; j += blockDim.x) s_d[j] = a.x.d[j];
+    cp_async_wait<0>();
+    __syncthreads();
+
+    float acc[RPT][1][8];
+#pragma unroll
+    for (int t = 0; t < RPT; t++)
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc[t][0][k] = 0.0f;
+    for (int r0 = 0; r0 < nb; r0 += R) {
+        // this warp's blocks of the round: the 8 dot sums and dw*da per row
+#pragma unroll
+        for (int u = 0; u < WB; u++) {
+            const int jr = warp * WB + u, j = r0 + jr;
+            if (j < nb) {
+                const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[0];
+                const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[1];
+                const int4 c0 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[0];
+                const int4 c1 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[1];
+                const float da = s_d[j];
+                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+                for (int t = 0; t < RPT; t++) {
+                    const unsigned qw[4] = {wq[t][u].x, wq[t][u].y, wq[t][u].z, wq[t][u].w};
+                    const float dw = __half2float(__ushort_as_half(ws[t][u]));
+                    float *f = s_f + ((size_t)(t * R + jr) * 8) * 32 + lane;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        f[k * 32] = __fsub_rn(__int_as_float(dp4a_us(qw[k] & 0x0F0F0F0Fu, av[k], cv[k])), MAGIC_F);
+                        f[(4 + k) * 32] =
+                            __fsub_rn(__int_as_float(dp4a_us((qw[k] >> 4) & 0x0F0F0F0Fu, av[4 + k], cv[4 + k])), MAGIC_F);
+                    }
+                    s_s[(size_t)(t * R + jr) * 32 + lane] = __fmul_rn(dw, da);
+                }
+            }
+        }
+        if (r0 + R < nb) load_w(r0 + R);  // the next round's blocks, in flight during the chains
+        __syncthreads();
+        if (warp == 0) {
+            const int rn = nb - r0 < R ? nb - r0 : R;
+            for (int jr = 0; jr < rn; jr++) {
+#pragma unroll
+                for (int t = 0; t < RPT; t++) {
+                    const float *f = s_f + ((size_t)(t * R + jr) * 8) * 32 + lane;
+                    const float dd = s_s[(size_t)(t * R + jr) * 32 + lane];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) acc[t][0][k] = __fmaf_rn(dd, f[k * 32], acc[t][0][k]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    pdl_release();
+    if (warp == 0) gemv_epilogue<RPT, 1, EPI>(a, acc, tile, total_tiles, 0, lane);
+}
+
 // Tensor-core GEMM (opt-in, prefill-sized batches; not bit-exact).  The int8
 // part of the product runs on tcgen05 kind::i8: per 32-element block j the
 // MMA gives isum[r][b] = sum_e (w_e - 8) * a_e exactly (s32 in TMEM); the CUDA
@@ -690,10 +812,23 @@ void launch_bt(const GemvArgs &a, int total_tiles, int units, cudaStream_t s) {
     gemv_kernel<BT, EPI><<<grid, 128, smem, s>>>(a, total_tiles, units);
 }
 
+// SLM_GEMV_SPLIT=0: batch-1 GEMVs of wide matrices take the staged kernel
+inline bool split_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("SLM_GEMV_SPLIT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 // Warps per staged CTA: the most (up to 8) that still gives every SM a CTA
 // (within 5%), so the weight tiles are shared by as many rows as the grid allows.
+// No more warps than activation rows: a warp past the batch has no work and
+// its rows' shared memory would only cut the CTAs an SM holds.
 inline int pick_nw(int units, int batch) {
-    for (int nw = STAGED_MAX_WARPS; nw > 1; nw >>= 1)
+    int cap = 1;
+    while (cap < batch && cap < STAGED_MAX_WARPS) cap <<= 1;
+    for (int nw = cap; nw > 1; nw >>= 1)
         if ((long)units * ((batch + nw - 1) / nw) >= 140) return nw;
     return 1;
 }
@@ -785,6 +920,13 @@ void launch_epi(const GemvArgs &a, cudaStream_t s) {
         launch_staged<GEMM_BT, EPI, false>(a, nw, total_tiles, units, s);
         return;
     }
+    if (!norm && a.batch == 1 && a.nb >= SPLIT_MIN_NB && split_enabled() &&
+        split_smem(a.nb) <= STAGED_SMEM_MAX) {
+        // one activation row of a wide matrix: the blocks of a tile over eight warps
+        launch_kernel(gemv_split_kernel<EPI>, dim3((unsigned)units), dim3(256), split_smem(a.nb), s, a.pdl, a,
+                      total_tiles);
+        return;
+    }
     const int nw = pick_nw(units, a.batch);
     if (staged_smem(RPT, nw, a.nb, norm) <= STAGED_SMEM_MAX) {
         // one activation row per warp
@@ -816,6 +958,7 @@ void set_limits(int bytes) {
     cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
     cudaFuncSetAttribute(gemv_staged_kernel<1, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
     cudaFuncSetAttribute(gemv_staged_kernel<GEMM_BT, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
+    cudaFuncSetAttribute(gemv_split_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, st);
 }
 
 }  // namespace

@@ -268,3 +268,25 @@ def test_model_errors(cuda):
         g.prefill_tokens([])
     # the model still works after rejected calls
     assert g.forward_token(1, 0) == O.Model(cfg, w).forward_token(1, 0)
+
+
+@pytest.mark.parametrize("unfused", [False, True])
+def test_wide_model_batch1_generate_matches_oracle(cuda, unfused):
+    """dim 2048, hidden 2048 (64 blocks a row): batch-1 decode steps take the
+    block-split GEMV for Wo, down and lm_head, and, with the RMSNorm as its own
+    launch (SLM_UNFUSED_NORM=1), also for QKV and gate/up; tokens and logits
+    equal the oracle's."""
+    cfg = Config(2048, 2048, 16, 4, 64, 1e-5)
+    w = synth.synth_model(cfg, 1, 1024, seed=31)
+    if unfused:
+        os.environ["SLM_UNFUSED_NORM"] = "1"
+    try:
+        g = S.Model(cfg, w, max_sequences=1, max_rows=8)
+    finally:
+        os.environ.pop("SLM_UNFUSED_NORM", None)
+    o = O.Model(cfg, w)
+    prompt = [3, 17, 255, 1000]
+    assert g.generate(prompt, 6) == o.generate(prompt, 6)
+    assert np.array_equal(g.logits(0), o.logits())
+    o.close()
+    g.close()

@@ -89,6 +89,9 @@ GEMM_SHAPES = [  # (batch, rows, cols)
     (1, 1, 32), (1, 576, 576), (1, 960, 576), (3, 100, 64), (2, 33, 96), (4, 3072, 576),
     (5, 576, 1536), (64, 1536, 576), (64, 576, 1536), (8, 4096, 4096), (1, 14336, 4096),
     (1, 32000, 288), (7, 49152, 576),
+    # batch 1 of wide matrices: the block-split GEMV (64+ blocks a row), ragged
+    # row tiles and a last round of one block (65 and 129 blocks)
+    (1, 4096, 4096), (1, 100, 2048), (1, 576, 2080), (1, 33, 4128),
     # prefill-sized batches: the GEMM shape (4 activation rows per warp), ragged edges
     (1024, 576, 576), (1037, 300, 64), (1100, 960, 576), (2048, 576, 1536),
 ]
