@@ -298,8 +298,12 @@ int slm_model_prefill_tokens(slm_model *m, uint32_t seq, const int32_t *tokens, 
  * token of prompt i; logits row i = its logits.  After
  * slm_model_attach_shard with nranks > 1, each rank computes the attention
  * of its (sequence, KV head) units only (slm_shard_units) and one NCCL
- * all-gather per layer assembles the outputs before Wo; every rank then holds
- * the full results.  Requires nseq*num_kv_heads to divide by nranks. */
+ * all-gather per layer assembles the outputs before Wo; when nseq*n divides by
+ * nranks, Wo and the FFN then run on this rank's nseq*n/nranks rows and a
+ * second, in-place all-gather per layer hands every rank all rows again.
+ * Every rank holds the full results (and every sequence's KV: the QKV
+ * projection runs on all rows).  Requires nseq*num_kv_heads to divide by
+ * nranks. */
 int slm_model_prefill_batch(slm_model *m, uint32_t nseq, const uint32_t *seqs,
                             const int32_t *tokens, uint32_t n, int32_t *next);
 /* Attention arithmetic of prefill forwards (prefill_tokens, prefill_batch):
