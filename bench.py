@@ -54,10 +54,11 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill measurement")
     p.add_argument("--no-flash", action="store_true", help="skip the flash-decode leg")
-    p.add_argument("--sweep", default=None, choices=["cfg4", "published"],
+    p.add_argument("--sweep", default=None, choices=["cfg4", "cfg4-gemv", "published"],
                    help="kernel sweep of BASELINE config 4 instead of the bench line: decode "
                         "attention (exact and flash) at L 512/2048/8192 x B 1..128 and the Q4 GEMVs "
-                        "4096x4096 / 14336x4096 at B 1/8/64, one JSON line per case")
+                        "4096x4096 / 14336x4096 at B 1/8/64, one JSON line per case (cfg4-gemv: the GEMVs "
+                        "alone)")
     p.add_argument("--layers", type=int, default=None,
                    help="profiling case only: fewer layers (same per-kernel shapes); the "
                         "line is then marked as not a bench value")
@@ -675,10 +676,10 @@ def run_sweep(args):
     hbm = peaks.get("hbm_gbs") or 6650.0
     src = "of measured" if peaks.get("hbm_gbs") else "of fallback"
     cfg0, layers, vocab = synth.config("cfg4")
-    w = synth.synth_model(cfg0, layers, vocab, seed=args.seed)
+    w = synth.synth_model(cfg0, layers, vocab, seed=args.seed) if args.sweep != "cfg4-gemv" else None
     kvd = cfg0.dim // cfg0.num_heads * cfg0.num_kv_heads
     Bmax, steps = 128, 4
-    for L in (512, 2048, 8192):
+    for L in (() if args.sweep == "cfg4-gemv" else (512, 2048, 8192)):
         cfg, _, _ = synth.config("cfg4", max_seq_len=L + 16)
         m = S.Model(cfg, w, max_sequences=Bmax, max_rows=Bmax)
         g = torch.Generator(device="cuda")
