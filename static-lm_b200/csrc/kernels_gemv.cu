@@ -448,50 +448,63 @@ __global__ void __launch_bounds__(32 * STAGED_MAX_WARPS, BT > 1 ? 2 : 1)
 // per unit (RPT weight tiles), eight warps.  The reference's order fixes only
 // the eight chains acc_k = fma(dw*da, isum_k, acc_k) over the blocks of a row;
 // the int8 dot sums isum_k and the scale products dw*da of different blocks
-// are independent.  So, in rounds of SPLIT_ROUND / RPT blocks, every warp forms
-// them for eight blocks of the round -- its weight blocks straight from HBM,
-// one 16-byte load per lane (row) and block, all eight in flight at once, the
-// next round's loaded while warp 0 works -- into shared memory as the exact
-// f32 values block_dot uses, and warp 0 then runs its lane's eight FMA chains
-// through the round in block order.  Same values, same order: bit-exact.
+// are independent.  So the blocks go in rounds of SPLIT_ROUND / RPT: warps
+// 1..7 form a round's dot sums (as the exact f32 values block_dot uses) and
+// dw*da from 16-byte weight loads straight from HBM -- the next round's loads
+// in flight while they store -- into one of two buffers, and warp 0 runs its
+// lane's eight FMA chains through the previous round in block order.  Same
+// values, same order: bit-exact.  Every mbarrier wait is bounded.
 constexpr int SPLIT_MIN_NB = 64;
-constexpr int SPLIT_ROUND = 64;            // blocks per round for one tile: 8 per warp
-constexpr int SPLIT_WB = SPLIT_ROUND / 8;  // blocks a warp forms per round (and tile)
+constexpr int SPLIT_ROUND = 32;  // blocks per round for one tile
+constexpr int SPLIT_PW = 7;      // warps forming the dot sums
 
-// the activation row (68 B a block) and one round's dot sums and scales
-// (SPLIT_ROUND blocks x 32 rows x 9 floats, whatever the tiles per unit)
+// the activation row (68 B a block) and two rounds' dot sums and scales
+// (SPLIT_ROUND blocks x 32 rows x 9 floats each, whatever the tiles per unit)
 __host__ __device__ inline size_t split_smem(int nb) {
-    return (((size_t)nb * 68 + 15) & ~(size_t)15) + (size_t)SPLIT_ROUND * 32 * 9 * 4 + 16;
+    return (((size_t)nb * 68 + 15) & ~(size_t)15) + 2 * (size_t)SPLIT_ROUND * 32 * 9 * 4 + 16;
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(256) gemv_split_kernel(GemvArgs a, int total_tiles) {
     constexpr int RPT = (EPI == EPI_SWIGLU_Q8) ? 2 : 1;
-    constexpr int R = SPLIT_ROUND / RPT;  // blocks per round
-    constexpr int WB = R / 8;             // blocks per warp and round
+    constexpr int R = SPLIT_ROUND / RPT;                   // blocks per round
+    constexpr int WB = (R + SPLIT_PW - 1) / SPLIT_PW;      // blocks a forming warp takes per round
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bar_full[2], bar_empty[2];
+    __shared__ int s_abort;
     const int nb = a.nb;
     int8_t *s_qs = (int8_t *)smem;                       // [nb][32]
     int32_t *s_c = (int32_t *)(smem + (size_t)nb * 32);  // [nb][8]
     float *s_d = (float *)(smem + (size_t)nb * 64);      // [nb]
-    // [RPT][R][8][32]: f32 of isum_k per (tile, block of the round, k, lane)
-    float *s_f = (float *)(smem + (((size_t)nb * 68 + 15) & ~(size_t)15));
-    float *s_s = s_f + (size_t)RPT * R * 8 * 32;         // [RPT][R][32]: dw*da
+    // per buffer: [RPT][R][2][32] float4 of the 8 dot sums (lanes' rows 16 B
+    // apart for conflict-free 16-byte loads), then [RPT][R][32] dw*da
+    float4 *s_f = (float4 *)(smem + (((size_t)nb * 68 + 15) & ~(size_t)15));
+    constexpr int F4 = RPT * R * 2 * 32, SS = RPT * R * 32;
+    float *s_s = (float *)(s_f + 2 * F4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int tile[RPT];
     tile[0] = blockIdx.x;
     if (RPT == 2) tile[RPT - 1] = blockIdx.x + total_tiles / 2;
+    const int nr = (nb + R - 1) / R;  // rounds
 
-    // this warp's weight blocks of a round: nibbles and scale of row `lane`
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&bar_full[b], SPLIT_PW * 32);
+            mbar_init(&bar_empty[b], 32);
+        }
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    // a forming warp's weight blocks of a round: nibbles and scale of row `lane`
     uint4 wq[RPT][WB];
     unsigned short ws[RPT][WB];
     auto load_w = [&](int r0) {
 #pragma unroll
         for (int u = 0; u < WB; u++) {
-            const int j = r0 + warp * WB + u;
+            const int jr = (warp - 1) + u * SPLIT_PW, j = r0 + jr;
 #pragma unroll
             for (int t = 0; t < RPT; t++) {
-                if (j < nb) {
+                if (jr < R && j < nb) {
                     const uint8_t *tp = a.w + tile_offset((size_t)tile[t], nb, j);
                     wq[t][u] = __ldg(reinterpret_cast<const uint4 *>(tp + lane * 16));
                     ws[t][u] = __ldg(reinterpret_cast<const unsigned short *>(tp + 512 + lane * 2));
@@ -499,8 +512,8 @@ __global__ void __launch_bounds__(256) gemv_split_kernel(GemvArgs a, int total_t
             }
         }
     };
-    load_w(0);  // constant data: in flight while the previous kernel finishes
-    pdl_wait();  // the activation row is the previous kernel's output
+    if (warp > 0) load_w(0);  // constant data: in flight while the previous kernel finishes
+    pdl_wait();               // the activation row is the previous kernel's output
     for (int i = threadIdx.x; i < nb * 4; i += blockDim.x) {
         const int j = i >> 2, part = i & 3;
         void *dst = part < 2 ? (void *)(s_qs + j * 32 + part * 16) : (void *)(s_c + j * 8 + (part - 2) * 4);
@@ -511,59 +524,81 @@ __global__ void __launch_bounds__(256) gemv_split_kernel(GemvArgs a, int total_t
     cp_async_commit();
     for (int j = threadIdx.x; j < nb; j += blockDim.x) s_d[j] = a.x.d[j];
     cp_async_wait<0>();
-    __syncthreads();
+    __syncthreads();  // the activation row and the barriers are ready
 
     float acc[RPT][1][8];
 #pragma unroll
     for (int t = 0; t < RPT; t++)
 #pragma unroll
         for (int k = 0; k < 8; k++) acc[t][0][k] = 0.0f;
-    for (int r0 = 0; r0 < nb; r0 += R) {
-        // this warp's blocks of the round: the 8 dot sums and dw*da per row
+    if (warp > 0) {
+        // ---- forming warps
+        for (int r = 0; r < nr; r++) {
+            const int b = r & 1, r0 = r * R;
+            if (r >= 2 && !mbar_wait(&bar_empty[b], (unsigned)((r >> 1) - 1) & 1u, &s_abort, a.err)) break;
+            float4 *f = s_f + (size_t)b * F4;
+            float *ss = s_s + (size_t)b * SS;
 #pragma unroll
-        for (int u = 0; u < WB; u++) {
-            const int jr = warp * WB + u, j = r0 + jr;
-            if (j < nb) {
-                const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[0];
-                const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[1];
-                const int4 c0 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[0];
-                const int4 c1 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[1];
-                const float da = s_d[j];
-                const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            for (int u = 0; u < WB; u++) {
+                const int jr = (warp - 1) + u * SPLIT_PW, j = r0 + jr;
+                if (jr < R && j < nb) {
+                    const int4 a0 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[0];
+                    const int4 a1 = reinterpret_cast<const int4 *>(s_qs + (size_t)j * 32)[1];
+                    const int4 c0 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[0];
+                    const int4 c1 = reinterpret_cast<const int4 *>(s_c + (size_t)j * 8)[1];
+                    const float da = s_d[j];
+                    const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    const int cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-                for (int t = 0; t < RPT; t++) {
-                    const unsigned qw[4] = {wq[t][u].x, wq[t][u].y, wq[t][u].z, wq[t][u].w};
-                    const float dw = __half2float(__ushort_as_half(ws[t][u]));
-                    float *f = s_f + ((size_t)(t * R + jr) * 8) * 32 + lane;
+                    for (int t = 0; t < RPT; t++) {
+                        const unsigned qw[4] = {wq[t][u].x, wq[t][u].y, wq[t][u].z, wq[t][u].w};
+                        float v[8];
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        f[k * 32] = __fsub_rn(__int_as_float(dp4a_us(qw[k] & 0x0F0F0F0Fu, av[k], cv[k])), MAGIC_F);
-                        f[(4 + k) * 32] =
-                            __fsub_rn(__int_as_float(dp4a_us((qw[k] >> 4) & 0x0F0F0F0Fu, av[4 + k], cv[4 + k])), MAGIC_F);
+                        for (int k = 0; k < 4; k++) {
+                            v[k] = __fsub_rn(__int_as_float(dp4a_us(qw[k] & 0x0F0F0F0Fu, av[k], cv[k])), MAGIC_F);
+                            v[4 + k] = __fsub_rn(
+                                __int_as_float(dp4a_us((qw[k] >> 4) & 0x0F0F0F0Fu, av[4 + k], cv[4 + k])), MAGIC_F);
+                        }
+                        const size_t fi = ((size_t)(t * R + jr) * 2) * 32 + lane;
+                        f[fi] = make_float4(v[0], v[1], v[2], v[3]);
+                        f[fi + 32] = make_float4(v[4], v[5], v[6], v[7]);
+                        ss[(size_t)(t * R + jr) * 32 + lane] =
+                            __fmul_rn(__half2float(__ushort_as_half(ws[t][u])), da);
                     }
-                    s_s[(size_t)(t * R + jr) * 32 + lane] = __fmul_rn(dw, da);
                 }
             }
+            if (r + 1 < nr) load_w(r0 + R);  // the next round's blocks, in flight from here
+            mbar_arrive(&bar_full[b]);
         }
-        if (r0 + R < nb) load_w(r0 + R);  // the next round's blocks, in flight during the chains
-        __syncthreads();
-        if (warp == 0) {
-            const int rn = nb - r0 < R ? nb - r0 : R;
+    } else {
+        // ---- warp 0: the chains, round after round in block order
+        for (int r = 0; r < nr; r++) {
+            const int b = r & 1, rn = nb - r * R < R ? nb - r * R : R;
+            if (!mbar_wait(&bar_full[b], (unsigned)(r >> 1) & 1u, &s_abort, a.err)) break;
+            const float4 *f = s_f + (size_t)b * F4;
+            const float *ss = s_s + (size_t)b * SS;
             for (int jr = 0; jr < rn; jr++) {
 #pragma unroll
                 for (int t = 0; t < RPT; t++) {
-                    const float *f = s_f + ((size_t)(t * R + jr) * 8) * 32 + lane;
-                    const float dd = s_s[(size_t)(t * R + jr) * 32 + lane];
-#pragma unroll
-                    for (int k = 0; k < 8; k++) acc[t][0][k] = __fmaf_rn(dd, f[k * 32], acc[t][0][k]);
+                    const size_t fi = ((size_t)(t * R + jr) * 2) * 32 + lane;
+                    const float4 x = f[fi], y = f[fi + 32];
+                    const float dd = ss[(size_t)(t * R + jr) * 32 + lane];
+                    acc[t][0][0] = __fmaf_rn(dd, x.x, acc[t][0][0]);
+                    acc[t][0][1] = __fmaf_rn(dd, x.y, acc[t][0][1]);
+                    acc[t][0][2] = __fmaf_rn(dd, x.z, acc[t][0][2]);
+                    acc[t][0][3] = __fmaf_rn(dd, x.w, acc[t][0][3]);
+                    acc[t][0][4] = __fmaf_rn(dd, y.x, acc[t][0][4]);
+                    acc[t][0][5] = __fmaf_rn(dd, y.y, acc[t][0][5]);
+                    acc[t][0][6] = __fmaf_rn(dd, y.z, acc[t][0][6]);
+                    acc[t][0][7] = __fmaf_rn(dd, y.w, acc[t][0][7]);
                 }
             }
+            mbar_arrive(&bar_empty[b]);
         }
-        __syncthreads();
     }
     pdl_release();
-    if (warp == 0) gemv_epilogue<RPT, 1, EPI>(a, acc, tile, total_tiles, 0, lane);
+    __syncthreads();
+    if (warp == 0 && !s_abort) gemv_epilogue<RPT, 1, EPI>(a, acc, tile, total_tiles, 0, lane);
 }
 
 // Tensor-core GEMM (opt-in, prefill-sized batches; not bit-exact).  The int8
